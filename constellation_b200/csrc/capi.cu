@@ -1,0 +1,621 @@
+// C ABI of the hot path (include/constellation_b200.h): context, expert arena, workspace
+// and the layer-level entry points that chain the kernels of this folder.
+//
+// Per call, everything is enqueued on the caller's stream with no host synchronisation:
+//   cst_moe_layer   = router (2 kernels) -> route_pack -> pack x -> grouped up/gate ->
+//                     pack h -> grouped down -> combine          (8 launches)
+//   cst_moe_routed  = the same without the router
+//   cst_grouped_ffn / cst_expert_forward = route_pack (rows mode) -> ... -> combine
+// Capacity checks happen on the host from the call's shapes, so no device overflow can
+// occur and nothing has to be read back.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/constellation_b200.h"
+#include "cst_common.cuh"
+#include "kernels.h"
+#include "layout.cuh"
+
+using namespace cst;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define CST_CUDA(call)                                                                         \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            return fail(CST_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                        __FILE__, __LINE__);                                                   \
+    } while (0)
+
+struct Workspace {
+    float* router_partial = nullptr;  // [kz, max_tokens, E]
+    int32_t* topk_idx = nullptr;      // [max_tokens, 16]
+    float* topk_w = nullptr;
+    GroupRec* groups = nullptr;       // [max_rows]
+    int32_t* tile_group = nullptr;    // [max_rows]
+    int32_t* row_token = nullptr;     // [max_rows]
+    float* row_weight = nullptr;
+    int32_t* tk_row = nullptr;        // [max(max_tokens * 16, max_rows)]
+    PackMeta* meta = nullptr;
+    uint8_t* xfrag = nullptr;         // [max_rows, H/128, 3072]
+    float* xscale = nullptr;          // [max_rows, H/128, 8]
+    float* h = nullptr;               // [max_rows, I]
+    uint8_t* hfrag = nullptr;
+    float* hscale = nullptr;
+    float* y = nullptr;               // [max_rows, H]
+    int* err = nullptr;
+};
+
+}  // namespace
+
+struct cst_ctx {
+    int device = -1;
+    cst_config cfg{};
+    int num_sms = 0;
+    ArenaGeom geo{};
+    uint8_t* arena = nullptr;
+    uint8_t* staging = nullptr;        // 3 * I * H bytes for uploads
+    int32_t* d_slot_of_expert = nullptr;
+    std::vector<int32_t> slot_of_expert;  // router expert -> slot
+    std::vector<int32_t> expert_of_slot;  // slot -> router expert, -1 shared, -2 empty
+    int32_t shared_slot = -1;
+    int max_rows = 0;
+    uint8_t* ws_base = nullptr;
+    size_t ws_bytes = 0;
+    Workspace ws;
+    // stage profiling (cst_profile_enable): one event per stage boundary per call
+    bool prof = false;
+    std::vector<cudaEvent_t> ev_pool;
+    std::vector<std::vector<cudaEvent_t>> prof_calls;
+};
+
+namespace {
+
+// Stage boundaries of one call: 0 start | router | route_pack | pack x | up/gate | pack h |
+// down | combine -> 8 events, 7 stages (CST_N_STAGES).
+constexpr int kProfEvents = CST_N_STAGES + 1;
+
+void prof_begin(cst_ctx* c, cudaStream_t s) {
+    if (!c->prof) return;
+    std::vector<cudaEvent_t> ev(kProfEvents);
+    for (auto& e : ev) {
+        if (!c->ev_pool.empty()) {
+            e = c->ev_pool.back();
+            c->ev_pool.pop_back();
+        } else {
+            cudaEventCreate(&e);
+        }
+    }
+    c->prof_calls.push_back(std::move(ev));
+    cudaEventRecord(c->prof_calls.back()[0], s);
+}
+
+// Records the end of `stage` (and of every earlier stage not recorded in this call).
+void prof_mark(cst_ctx* c, int stage, cudaStream_t s) {
+    if (!c->prof || c->prof_calls.empty()) return;
+    cudaEventRecord(c->prof_calls.back()[stage + 1], s);
+}
+
+void prof_fill_skipped(cst_ctx* c, int upto_stage, cudaStream_t s) {
+    if (!c->prof || c->prof_calls.empty()) return;
+    for (int st = 0; st <= upto_stage; ++st) cudaEventRecord(c->prof_calls.back()[st + 1], s);
+}
+
+}  // namespace
+
+namespace {
+
+int ensure_device(const cst_ctx* c) {
+    int cur = -1;
+    CST_CUDA(cudaGetDevice(&cur));
+    if (cur != c->device) CST_CUDA(cudaSetDevice(c->device));
+    return CST_OK;
+}
+
+bool valid_dtype(int d) { return d == CST_DTYPE_FP16 || d == CST_DTYPE_BF16 || d == CST_DTYPE_FP32; }
+
+// Activation rows are read and written with 8/16-byte vector accesses.
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// rows-mode packing encodes the row index in 14 bits of the sort key (route_pack.cu)
+constexpr int kMaxRowsModeRows = 16383;
+
+size_t carve(uint8_t** cursor, size_t bytes) {
+    const size_t a = (bytes + 255) / 256 * 256;
+    *cursor += a;
+    return a;
+}
+
+int alloc_workspace(cst_ctx* c) {
+    const cst_config& f = c->cfg;
+    const int H = f.hidden_dim, I = f.inter_dim, E = f.n_routed_experts;
+    const int64_t R = c->max_rows;
+    const int kz = router_k_split(H);
+    struct Piece {
+        void** p;
+        size_t bytes;
+    };
+    Workspace& w = c->ws;
+    const size_t tk = size_t(std::max<int64_t>(int64_t(f.max_tokens) * 16, R));
+    std::vector<Piece> pieces = {
+        {reinterpret_cast<void**>(&w.router_partial), size_t(kz) * f.max_tokens * E * 4},
+        {reinterpret_cast<void**>(&w.topk_idx), size_t(f.max_tokens) * 16 * 4},
+        {reinterpret_cast<void**>(&w.topk_w), size_t(f.max_tokens) * 16 * 4},
+        {reinterpret_cast<void**>(&w.groups), size_t(R) * sizeof(GroupRec)},
+        {reinterpret_cast<void**>(&w.tile_group), size_t(R) * 4},
+        {reinterpret_cast<void**>(&w.row_token), size_t(R) * 4},
+        {reinterpret_cast<void**>(&w.row_weight), size_t(R) * 4},
+        {reinterpret_cast<void**>(&w.tk_row), tk * 4},
+        {reinterpret_cast<void**>(&w.meta), sizeof(PackMeta)},
+        {reinterpret_cast<void**>(&w.xfrag), size_t(R) * (H / kBlock) * kBTileBytes},
+        {reinterpret_cast<void**>(&w.xscale), size_t(R) * (H / kBlock) * kTileCols * 4},
+        {reinterpret_cast<void**>(&w.h), size_t(R) * I * 4},
+        {reinterpret_cast<void**>(&w.hfrag), size_t(R) * (I / kBlock) * kBTileBytes},
+        {reinterpret_cast<void**>(&w.hscale), size_t(R) * (I / kBlock) * kTileCols * 4},
+        {reinterpret_cast<void**>(&w.y), size_t(R) * H * 4},
+        {reinterpret_cast<void**>(&w.err), 256},
+    };
+    size_t total = 0;
+    for (auto& p : pieces) total += (p.bytes + 255) / 256 * 256;
+    CST_CUDA(cudaMalloc(&c->ws_base, total));
+    CST_CUDA(cudaMemset(c->ws_base, 0, total));
+    c->ws_bytes = total;
+    uint8_t* cur = c->ws_base;
+    for (auto& p : pieces) {
+        *p.p = cur;
+        carve(&cur, p.bytes);
+    }
+    return CST_OK;
+}
+
+// route_pack -> pack x -> up/gate -> pack h -> down.  Leaves y rows and tk_row filled.
+int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_t s) {
+    const int H = c->cfg.hidden_dim, I = c->cfg.inter_dim;
+    Workspace& w = c->ws;
+    pa.n_slots = c->cfg.n_slots;
+    pa.max_rows = c->max_rows;
+    pa.max_groups = c->max_rows;
+    pa.groups = w.groups;
+    pa.tile_group = w.tile_group;
+    pa.row_token = w.row_token;
+    pa.row_weight = w.row_weight;
+    pa.tk_row = w.tk_row;
+    pa.meta = w.meta;
+    CST_CUDA(launch_route_pack(pa, s));
+    prof_mark(c, 1, s);
+
+    PackActArgs px{x, x_dtype, H, w.row_token, w.groups, w.tile_group, w.meta, H, w.xfrag, w.xscale};
+    CST_CUDA(launch_pack_act(px, c->num_sms, s));
+    prof_mark(c, 2, s);
+
+    FfnArgs up{};
+    up.arena = c->arena;
+    up.slot_bytes = c->geo.slot_bytes;
+    up.a_off = 0;
+    up.s0_off = c->geo.su_off;
+    up.s1_off = c->geo.sg_off;
+    up.KB = H / kBlock;
+    up.n_mb = I / kRowsPerItem;
+    up.scale_ld = H / kBlock;
+    up.groups = w.groups;
+    up.meta = w.meta;
+    up.bfrag = w.xfrag;
+    up.bscale = w.xscale;
+    up.out = w.h;
+    up.ld_out = I;
+    up.row_weight = nullptr;
+    up.err = w.err;
+    CST_CUDA(launch_grouped_ffn(up, true, c->num_sms, s));
+    prof_mark(c, 3, s);
+
+    PackActArgs ph{w.h, CST_DTYPE_FP32, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale};
+    CST_CUDA(launch_pack_act(ph, c->num_sms, s));
+    prof_mark(c, 4, s);
+
+    FfnArgs dn = up;
+    dn.a_off = c->geo.upgate_bytes;
+    dn.s0_off = c->geo.sd_off;
+    dn.s1_off = c->geo.sd_off;
+    dn.KB = I / kBlock;
+    dn.n_mb = H / kRowsPerItem;
+    dn.scale_ld = I / kBlock;
+    dn.bfrag = w.hfrag;
+    dn.bscale = w.hscale;
+    dn.out = w.y;
+    dn.ld_out = H;
+    dn.row_weight = w.row_weight;
+    CST_CUDA(launch_grouped_ffn(dn, false, c->num_sms, s));
+    prof_mark(c, 5, s);
+    return CST_OK;
+}
+
+int check_ctx(const cst_ctx* c) {
+    if (c == nullptr) return fail(CST_ERR_INVALID_ARG, "null context");
+    return CST_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t cst_abi_version(void) { return 100; }
+
+const char* cst_last_error(void) { return g_last_error.c_str(); }
+
+int cst_create(int32_t device, const cst_config* cfg, cst_ctx** out) {
+    g_last_error.clear();
+    if (cfg == nullptr || out == nullptr) return fail(CST_ERR_INVALID_ARG, "null cfg/out");
+    *out = nullptr;
+    const cst_config& f = *cfg;
+    if (f.block_size != kBlock) return fail(CST_ERR_INVALID_ARG, "block_size must be 128, got %d", f.block_size);
+    if (f.hidden_dim <= 0 || f.hidden_dim % kBlock || f.inter_dim <= 0 || f.inter_dim % kBlock)
+        return fail(CST_ERR_INVALID_ARG, "hidden_dim (%d) and inter_dim (%d) must be positive multiples of 128",
+                    f.hidden_dim, f.inter_dim);
+    if (f.n_routed_experts <= 0 || f.n_routed_experts > 1024)
+        return fail(CST_ERR_INVALID_ARG, "n_routed_experts must be in [1, 1024]");
+    if (f.n_group <= 0 || f.n_group > 32 || f.n_routed_experts % f.n_group)
+        return fail(CST_ERR_INVALID_ARG, "invalid n_group=%d for n_routed_experts=%d", f.n_group,
+                    f.n_routed_experts);
+    if (f.topk_group <= 0 || f.topk_group > f.n_group)
+        return fail(CST_ERR_INVALID_ARG, "invalid topk_group=%d for n_group=%d", f.topk_group, f.n_group);
+    if (f.top_k <= 0 || f.top_k > 15 || f.top_k > f.n_routed_experts)
+        return fail(CST_ERR_INVALID_ARG, "invalid top_k=%d", f.top_k);
+    if (f.n_slots < 0 || f.n_slots > 8191) return fail(CST_ERR_INVALID_ARG, "n_slots must be in [0, 8191]");
+    if (f.max_tokens <= 0 || f.max_tokens > 16383) return fail(CST_ERR_INVALID_ARG, "max_tokens must be in [1, 16383]");
+    auto* c = new cst_ctx();
+    c->device = device;
+    c->cfg = f;
+    c->max_rows = f.max_rows > 0 ? f.max_rows : f.max_tokens * (f.top_k + 1);
+    if (c->max_rows > kRoutePackMaxKeys) {
+        delete c;
+        return fail(CST_ERR_INVALID_ARG, "max_rows=%d exceeds %d", f.max_rows, kRoutePackMaxKeys);
+    }
+    c->geo = ArenaGeom::make(f.hidden_dim, f.inter_dim);
+    c->slot_of_expert.assign(f.n_routed_experts, -1);
+    c->expert_of_slot.assign(f.n_slots, -2);
+    int rc = CST_OK;
+    auto bail = [&](int code) {
+        cst_destroy(c);
+        return code;
+    };
+    if (cudaSetDevice(device) != cudaSuccess) return bail(fail(CST_ERR_CUDA, "cudaSetDevice(%d) failed", device));
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+        return bail(fail(CST_ERR_CUDA, "cannot query SM count"));
+    c->num_sms = sms;
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (major != 10 || minor != 0)
+        return bail(fail(CST_ERR_CUDA, "this library is built for sm_100a (B200); device %d is sm_%d%d", device,
+                         major, minor));
+    if (route_pack_init_attributes() != cudaSuccess || grouped_ffn_init_attributes() != cudaSuccess)
+        return bail(fail(CST_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(cudaGetLastError())));
+    const size_t arena = size_t(f.n_slots) * size_t(c->geo.slot_bytes);
+    if (cudaMalloc(&c->arena, arena) != cudaSuccess)
+        return bail(fail(CST_ERR_CUDA, "cannot allocate the %zu-byte expert arena", arena));
+    if (cudaMalloc(&c->staging, size_t(3) * f.inter_dim * f.hidden_dim) != cudaSuccess)
+        return bail(fail(CST_ERR_CUDA, "cannot allocate the upload staging buffer"));
+    if (cudaMalloc(&c->d_slot_of_expert, size_t(f.n_routed_experts) * 4) != cudaSuccess)
+        return bail(fail(CST_ERR_CUDA, "cannot allocate the slot table"));
+    if (cudaMemcpy(c->d_slot_of_expert, c->slot_of_expert.data(), size_t(f.n_routed_experts) * 4,
+                   cudaMemcpyHostToDevice) != cudaSuccess)
+        return bail(fail(CST_ERR_CUDA, "slot table copy failed"));
+    rc = alloc_workspace(c);
+    if (rc != CST_OK) return bail(rc);
+    *out = c;
+    return CST_OK;
+}
+
+void cst_destroy(cst_ctx* c) {
+    if (c == nullptr) return;
+    if (c->device >= 0) {
+        cudaSetDevice(c->device);
+        cudaDeviceSynchronize();
+    }
+    for (auto& ev : c->prof_calls)
+        for (auto e : ev) cudaEventDestroy(e);
+    for (auto e : c->ev_pool) cudaEventDestroy(e);
+    cudaFree(c->arena);
+    cudaFree(c->staging);
+    cudaFree(c->d_slot_of_expert);
+    cudaFree(c->ws_base);
+    delete c;
+}
+
+int cst_upload_expert(cst_ctx* c, int32_t slot, int32_t expert_id, const cst_expert_weights* w, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (w == nullptr) return fail(CST_ERR_INVALID_ARG, "null weights");
+    const int H = c->cfg.hidden_dim, I = c->cfg.inter_dim;
+    if (slot < 0 || slot >= c->cfg.n_slots) return fail(CST_ERR_INVALID_ARG, "slot %d out of [0, %d)", slot, c->cfg.n_slots);
+    if (expert_id < -1 || expert_id >= c->cfg.n_routed_experts)
+        return fail(CST_ERR_UNKNOWN_EXPERT, "expert_id %d out of [-1, %d)", expert_id, c->cfg.n_routed_experts);
+    // BuildExpertWeightsViewV2 rules (expert_format_v2.cc:68-175) for this context's shape
+    if (w->rows != I || w->cols != H)
+        return fail(CST_ERR_INVALID_ARG, "expert shape [%d, %d] does not match the context [%d, %d]", w->rows,
+                    w->cols, I, H);
+    if (w->row_block != kBlock || w->col_block != kBlock)
+        return fail(CST_ERR_INVALID_ARG, "block (%d, %d) must be (128, 128)", w->row_block, w->col_block);
+    if (!w->w_up || !w->w_gate || !w->w_down || !w->w_up_scale || !w->w_gate_scale || !w->w_down_scale)
+        return fail(CST_ERR_INVALID_ARG, "null tensor pointer");
+    if (int rc = ensure_device(c)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t mat = size_t(I) * H;
+    CST_CUDA(cudaMemcpyAsync(c->staging, w->w_up, mat, cudaMemcpyDefault, s));
+    CST_CUDA(cudaMemcpyAsync(c->staging + mat, w->w_gate, mat, cudaMemcpyDefault, s));
+    CST_CUDA(cudaMemcpyAsync(c->staging + 2 * mat, w->w_down, mat, cudaMemcpyDefault, s));
+    uint8_t* dst = c->arena + int64_t(slot) * c->geo.slot_bytes;
+    CST_CUDA(launch_relayout(c->staging, c->staging + mat, c->staging + 2 * mat, dst, I, H, c->num_sms, s));
+    const size_t grid = size_t(I / kBlock) * (H / kBlock) * 4;
+    CST_CUDA(cudaMemcpyAsync(dst + c->geo.su_off, w->w_up_scale, grid, cudaMemcpyDefault, s));
+    CST_CUDA(cudaMemcpyAsync(dst + c->geo.sg_off, w->w_gate_scale, grid, cudaMemcpyDefault, s));
+    CST_CUDA(cudaMemcpyAsync(dst + c->geo.sd_off, w->w_down_scale, grid, cudaMemcpyDefault, s));
+    // bookkeeping: a slot holds one expert; re-uploading replaces it (ExpertRegistryV2::Update)
+    const int old = c->expert_of_slot[slot];
+    if (old >= 0) c->slot_of_expert[old] = -1;
+    if (old == -1 && c->shared_slot == slot) c->shared_slot = -1;
+    if (expert_id >= 0) {
+        const int prev = c->slot_of_expert[expert_id];
+        if (prev >= 0 && prev != slot) c->expert_of_slot[prev] = -2;
+        c->slot_of_expert[expert_id] = slot;
+        c->expert_of_slot[slot] = expert_id;
+    } else {
+        c->expert_of_slot[slot] = -1;
+        c->shared_slot = slot;
+    }
+    CST_CUDA(cudaMemcpyAsync(c->d_slot_of_expert, c->slot_of_expert.data(), c->slot_of_expert.size() * 4,
+                             cudaMemcpyHostToDevice, s));
+    // upload is a load-time path: finish it before the staging buffer is reused
+    CST_CUDA(cudaStreamSynchronize(s));
+    return CST_OK;
+}
+
+int cst_free_expert(cst_ctx* c, int32_t slot) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (slot < 0 || slot >= c->cfg.n_slots) return fail(CST_ERR_INVALID_ARG, "slot %d out of range", slot);
+    if (int rc = ensure_device(c)) return rc;
+    const int e = c->expert_of_slot[slot];
+    if (e >= 0) c->slot_of_expert[e] = -1;
+    if (c->shared_slot == slot) c->shared_slot = -1;
+    c->expert_of_slot[slot] = -2;
+    CST_CUDA(cudaDeviceSynchronize());
+    CST_CUDA(cudaMemcpy(c->d_slot_of_expert, c->slot_of_expert.data(), c->slot_of_expert.size() * 4,
+                        cudaMemcpyHostToDevice));
+    return CST_OK;
+}
+
+int32_t cst_find_slot(const cst_ctx* c, int32_t expert_id) {
+    if (c == nullptr || expert_id < 0 || expert_id >= c->cfg.n_routed_experts) return -1;
+    return c->slot_of_expert[expert_id];
+}
+
+int cst_set_shared_slot(cst_ctx* c, int32_t slot) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (slot < -1 || slot >= c->cfg.n_slots) return fail(CST_ERR_INVALID_ARG, "slot %d out of range", slot);
+    c->shared_slot = slot;
+    return CST_OK;
+}
+
+int cst_route(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float* gate_weight, const float* bias,
+              const uint8_t* resident, int32_t top_k, int32_t* topk_idx, float* topk_weight, float* logits,
+              float* group_scores, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (!valid_dtype(x_dtype)) return fail(CST_ERR_INVALID_ARG, "bad x_dtype %d", x_dtype);
+    if (T < 0 || T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, c->cfg.max_tokens);
+    if (top_k <= 0 || top_k > c->cfg.top_k) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of [1, %d]", top_k, c->cfg.top_k);
+    if (!x || !gate_weight || !bias || !topk_idx || !topk_weight) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (T == 0) return CST_OK;
+    if (int rc = ensure_device(c)) return rc;
+    const cst_config& f = c->cfg;
+    CST_CUDA(launch_router(x, x_dtype, gate_weight, bias, resident, T, f.n_routed_experts, f.hidden_dim, f.n_group,
+                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor, c->ws.router_partial,
+                           topk_idx, topk_weight, logits, group_scores, static_cast<cudaStream_t>(stream)));
+    return CST_OK;
+}
+
+static int moe_routed_impl(cst_ctx* c, const void* x, int x_dtype, int T, const int32_t* topk_idx,
+                           const float* topk_w, int K, uint32_t flags, const void* residual, void* out,
+                           int out_dtype, cudaStream_t s) {
+    const bool shared = (flags & CST_FLAG_ADD_SHARED) != 0;
+    if (shared && c->shared_slot < 0) return fail(CST_ERR_NOT_RESIDENT, "no shared expert is resident");
+    if (int64_t(T) * (K + 1) > c->max_rows)
+        return fail(CST_ERR_INVALID_ARG, "T*(top_k+1)=%d exceeds the workspace (%d rows)", T * (K + 1), c->max_rows);
+    PackArgs pa{};
+    pa.topk_idx = topk_idx;
+    pa.topk_w = topk_w;
+    pa.slot_of_expert = c->d_slot_of_expert;
+    pa.E = c->cfg.n_routed_experts;
+    pa.K = K;
+    pa.shared_slot = shared ? c->shared_slot : -1;
+    pa.row_slot = nullptr;
+    pa.single_slot = -1;
+    pa.row_weight_in = nullptr;
+    pa.T = T;
+    if (int rc = run_experts(c, pa, x, x_dtype, s)) return rc;
+    CombineArgs ca{c->ws.y, c->cfg.hidden_dim, c->ws.tk_row, K + 1, T, c->cfg.hidden_dim,
+                   residual, x_dtype, out, out_dtype, nullptr};
+    CST_CUDA(launch_combine(ca, s));
+    prof_mark(c, 6, s);
+    return CST_OK;
+}
+
+int cst_moe_routed(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const int32_t* topk_idx,
+                   const float* topk_weight, int32_t top_k, uint32_t flags, void* out, int32_t out_dtype,
+                   void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
+    if (T < 0 || T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d out of range", T);
+    if (top_k <= 0 || top_k > 15) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of range", top_k);
+    if (!x || !out || !topk_idx || !topk_weight) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (!aligned16(x) || !aligned16(out)) return fail(CST_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+    if (T == 0) return CST_OK;
+    if (int rc = ensure_device(c)) return rc;
+    prof_begin(c, static_cast<cudaStream_t>(stream));
+    prof_fill_skipped(c, 0, static_cast<cudaStream_t>(stream));
+    return moe_routed_impl(c, x, x_dtype, T, topk_idx, topk_weight, top_k, flags, nullptr, out, out_dtype,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int cst_moe_layer(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float* gate_weight, const float* bias,
+                  const uint8_t* resident, int32_t top_k, uint32_t flags, const void* residual, void* out,
+                  int32_t out_dtype, int32_t* topk_idx, float* topk_weight, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
+    if (T < 0 || T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, c->cfg.max_tokens);
+    if (top_k <= 0 || top_k > c->cfg.top_k) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of range", top_k);
+    if (!x || !out || !gate_weight || !bias) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (!aligned16(x) || !aligned16(out) || (residual && !aligned16(residual)))
+        return fail(CST_ERR_INVALID_ARG, "x, out and residual must be 16-byte aligned");
+    if (T == 0) return CST_OK;
+    if (int rc = ensure_device(c)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int32_t* idx = topk_idx ? topk_idx : c->ws.topk_idx;
+    float* wts = topk_weight ? topk_weight : c->ws.topk_w;
+    const cst_config& f = c->cfg;
+    prof_begin(c, s);
+    CST_CUDA(launch_router(x, x_dtype, gate_weight, bias, resident, T, f.n_routed_experts, f.hidden_dim, f.n_group,
+                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor, c->ws.router_partial, idx,
+                           wts, nullptr, nullptr, s));
+    prof_mark(c, 0, s);
+    return moe_routed_impl(c, x, x_dtype, T, idx, wts, top_k, flags, residual, out, out_dtype, s);
+}
+
+int cst_grouped_ffn(cst_ctx* c, const void* x, int32_t x_dtype, int32_t R, const int32_t* row_slot,
+                    const float* row_weight, void* y, int32_t y_dtype, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
+    if (R < 0 || R > c->max_rows) return fail(CST_ERR_INVALID_ARG, "R=%d exceeds the workspace (%d rows)", R, c->max_rows);
+    if (!x || !y || !row_slot) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (R > kMaxRowsModeRows) return fail(CST_ERR_INVALID_ARG, "R=%d exceeds %d rows per call", R, kMaxRowsModeRows);
+    if (!aligned16(x) || !aligned16(y)) return fail(CST_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
+    if (R == 0) return CST_OK;
+    if (int rc = ensure_device(c)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    PackArgs pa{};
+    pa.row_slot = row_slot;
+    pa.single_slot = -1;
+    pa.row_weight_in = row_weight;
+    pa.T = R;
+    pa.shared_slot = -1;
+    prof_begin(c, s);
+    prof_fill_skipped(c, 0, s);
+    if (int rc = run_experts(c, pa, x, x_dtype, s)) return rc;
+    CombineArgs ca{c->ws.y, c->cfg.hidden_dim, c->ws.tk_row, 1, R, c->cfg.hidden_dim, nullptr, 0, y, y_dtype, nullptr};
+    CST_CUDA(launch_combine(ca, s));
+    prof_mark(c, 6, s);
+    return CST_OK;
+}
+
+int cst_expert_forward(cst_ctx* c, int32_t expert_id, const void* x, int32_t in_dtype, int32_t batch, void* y,
+                       int32_t out_dtype, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (expert_id < 0 || expert_id >= c->cfg.n_routed_experts)
+        return fail(CST_ERR_UNKNOWN_EXPERT, "unknown expert %d", expert_id);
+    const int slot = c->slot_of_expert[expert_id];
+    if (slot < 0) return fail(CST_ERR_NOT_RESIDENT, "expert %d is not resident on this device", expert_id);
+    // the reference serves fp16/bf16 in x fp16/bf16 out; fp32 output is an extension that
+    // returns the unrounded expert result
+    if ((in_dtype != CST_DTYPE_FP16 && in_dtype != CST_DTYPE_BF16) || !valid_dtype(out_dtype))
+        return fail(CST_ERR_BACKEND, "unsupported dtype pair (%d, %d)", in_dtype, out_dtype);
+    if (batch <= 0 || batch > c->max_rows) return fail(CST_ERR_BACKEND, "batch %d out of [1, %d]", batch, c->max_rows);
+    if (!x || !y) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (batch > kMaxRowsModeRows) return fail(CST_ERR_BACKEND, "batch %d exceeds %d", batch, kMaxRowsModeRows);
+    if (!aligned16(x) || !aligned16(y)) return fail(CST_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
+    if (int rc = ensure_device(c)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    PackArgs pa{};
+    pa.row_slot = nullptr;
+    pa.single_slot = slot;
+    pa.row_weight_in = nullptr;
+    pa.T = batch;
+    pa.shared_slot = -1;
+    prof_begin(c, s);
+    prof_fill_skipped(c, 0, s);
+    if (int rc = run_experts(c, pa, x, in_dtype, s)) return rc;
+    CombineArgs ca{c->ws.y, c->cfg.hidden_dim, c->ws.tk_row, 1, batch, c->cfg.hidden_dim, nullptr, 0, y, out_dtype,
+                   nullptr};
+    CST_CUDA(launch_combine(ca, s));
+    prof_mark(c, 6, s);
+    return CST_OK;
+}
+
+int cst_device_error(cst_ctx* c) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = ensure_device(c)) return rc;
+    CST_CUDA(cudaDeviceSynchronize());
+    int v = 0;
+    CST_CUDA(cudaMemcpy(&v, c->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v != CST_DEV_OK) {
+        CST_CUDA(cudaMemset(c->ws.err, 0, sizeof(int)));
+        return fail(CST_ERR_DEVICE_TIMEOUT, "a device-side wait gave up (code %d)", v);
+    }
+    return CST_OK;
+}
+
+int cst_profile_enable(cst_ctx* c, int32_t enable) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    c->prof = enable != 0;
+    return CST_OK;
+}
+
+int cst_profile_read(cst_ctx* c, float* stage_ms, int32_t max_calls) {
+    g_last_error.clear();
+    if (c == nullptr) return -fail(CST_ERR_INVALID_ARG, "null context");
+    if (ensure_device(c) != CST_OK) return -CST_ERR_CUDA;
+    int n = 0;
+    for (auto& ev : c->prof_calls) {
+        if (cudaEventSynchronize(ev.back()) != cudaSuccess) return -fail(CST_ERR_CUDA, "event sync failed");
+        if (stage_ms != nullptr && n < max_calls) {
+            for (int st = 0; st < CST_N_STAGES; ++st) {
+                float ms = 0.0f;
+                cudaEventElapsedTime(&ms, ev[st], ev[st + 1]);
+                stage_ms[n * CST_N_STAGES + st] = ms;
+            }
+            ++n;
+        }
+        for (auto e : ev) c->ev_pool.push_back(e);
+    }
+    c->prof_calls.clear();
+    return n;
+}
+
+int cst_ctx_info(const cst_ctx* c, int64_t* out, int32_t n) {
+    if (c == nullptr || out == nullptr) return 0;
+    int resident = 0;
+    for (int v : c->slot_of_expert) resident += v >= 0;
+    const int64_t vals[] = {int64_t(c->cfg.n_slots) * c->geo.slot_bytes, c->geo.slot_bytes, int64_t(c->ws_bytes),
+                            c->num_sms, resident, c->shared_slot};
+    const int m = std::min<int>(n, int(sizeof(vals) / sizeof(vals[0])));
+    for (int i = 0; i < m; ++i) out[i] = vals[i];
+    return m;
+}
+
+}  // extern "C"

@@ -1,0 +1,87 @@
+// Weighted combine: out[t] = sum_k y[row(t, k)] (+ y[row(t, shared)]), cast once.
+//
+// Replaces combine_outputs_torch (server/moe_layer_runtime.py:148-167, fp32
+// `combined.add_(w * y)` per route) and the routed + shared sum of run_sparse_layer
+// (server/full_model_runtime.py:348).  The routing weights were already applied in the
+// down-projection epilogue; here the rows of a token are added in the fixed order
+// k = 0 .. top_k-1 then the shared expert, in fp32, so the result is bit-identical from
+// run to run.  Optionally adds a residual (server/full_model_runtime.py:355).
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "cst_common.cuh"
+#include "kernels.h"
+
+namespace cst {
+
+
+__device__ __forceinline__ float4 load_act4(const void* p, int dtype, int64_t idx) {
+    if (dtype == 3) return *reinterpret_cast<const float4*>(static_cast<const float*>(p) + idx);
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + idx);
+    if (dtype == 2) {
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                           __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+    }
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+__global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
+    const int t = blockIdx.x;
+    if (t >= a.T) return;
+    const int32_t* rows = a.tk_row + int64_t(t) * a.K1;
+    for (int h = threadIdx.x * 4; h < a.H; h += blockDim.x * 4) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < a.K1; ++k) {
+            const int r = rows[k];
+            if (r < 0) continue;
+            const float4 v = *reinterpret_cast<const float4*>(a.y + int64_t(r) * a.ldy + h);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        if (a.extra) {
+            const float4 v = *reinterpret_cast<const float4*>(a.extra + int64_t(t) * a.H + h);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        if (a.residual) {
+            const float4 v = load_act4(a.residual, a.residual_dtype, int64_t(t) * a.H + h);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const int64_t o = int64_t(t) * a.H + h;
+        if (a.out_dtype == 3) {
+            *reinterpret_cast<float4*>(static_cast<float*>(a.out) + o) = acc;
+        } else if (a.out_dtype == 2) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+            __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t*>(&lo);
+            u.y = *reinterpret_cast<uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.out) + o) = u;
+        } else {
+            __half2 lo = __floats2half2_rn(acc.x, acc.y);
+            __half2 hi = __floats2half2_rn(acc.z, acc.w);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t*>(&lo);
+            u.y = *reinterpret_cast<uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.out) + o) = u;
+        }
+    }
+}
+
+cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream) {
+    if (a.T <= 0) return cudaSuccess;
+    combine_kernel<<<a.T, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace cst

@@ -1,0 +1,163 @@
+// Device helpers shared by the sm_100a kernels of the MoE hot path.
+//
+//  * TMA bulk copies (cp.async.bulk global -> shared, completion on an mbarrier) and
+//    the mbarrier primitives that pace the producer/consumer stage ring.  Every wait
+//    is bounded: after kSpinLimit polls it records CST_DEV_ERR_TIMEOUT in the
+//    context's device error word and returns false, so a broken pipeline ends the
+//    kernel with a status the host can read instead of hanging the GPU.
+//  * FP8 E4M3 tensor-core MMA (mma.sync m16n8k32, fp32 accumulate).
+//  * E4M3 encode/decode used by the activation packer.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+namespace cst {
+
+constexpr int kBlock = 128;          // FP8 scale block (rows and cols)
+constexpr int kRowsPerItem = 64;     // weight rows one CTA work item covers
+constexpr int kWarpRows = 16;        // rows per consumer warp (one MMA M tile)
+constexpr int kKStep = 32;           // K per mma.m16n8k32
+constexpr int kSplits = 3;           // E4M3 terms per activation element
+constexpr int kTileCols = 8;         // tokens per MMA N tile
+constexpr int kFragBytes = 256;      // one B fragment (32 x 8 e4m3) for a warp
+constexpr int kAFragBytes = 512;     // one A fragment (16 x 32 e4m3) for a warp
+constexpr int kMaxTilesPerGroup = 2; // routed groups carry at most 16 rows
+constexpr int kGroupRows = kMaxTilesPerGroup * kTileCols;
+// B bytes of one n-tile for one 128-wide K block: 4 k-steps x 3 splits x 256 B
+constexpr int kBTileBytes = (kBlock / kKStep) * kSplits * kFragBytes;  // 3072
+
+// Device error word values (written with atomicMax so the first/most severe sticks).
+constexpr int CST_DEV_OK = 0;
+constexpr int CST_DEV_ERR_TIMEOUT = 1;
+constexpr int CST_DEV_ERR_BOUNDS = 2;
+
+constexpr uint32_t kSpinLimit = 1u << 26;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait on an mbarrier phase: gives up after kWaitLimitNs of wall time (checked
+// every 256 polls) or kSpinLimit polls, whichever comes first.  Returns false and flags
+// the error word on timeout.
+constexpr uint64_t kWaitLimitNs = 4000000000ull;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0u && global_ns() - t0 > kWaitLimitNs) break;
+    }
+    if (err != nullptr) atomicMax(err, CST_DEV_ERR_TIMEOUT);
+    return false;
+}
+
+// 1-D bulk copy global -> shared; completes `bytes` of transaction count on `bar`.
+// Source and destination must be 16-byte aligned and `bytes` a multiple of 16.
+__device__ __forceinline__ void tma_bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                             uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_e4m3_16832(float (&d)[4], const uint4& a, uint32_t b0,
+                                               uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(smem_u32(p)));
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds64(const void* p) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(smem_u32(p)));
+    return v;
+}
+
+// E4M3 round-to-nearest-even with saturation to +-448 (hardware cvt).
+__device__ __forceinline__ uint8_t e4m3_rn(float v) {
+    return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+    __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
+    return __half2float(__half(h));
+}
+
+// Smallest power of two s with amax / s <= 448 (s = 1 for amax == 0).  Returns s.
+__device__ __forceinline__ float pow2_scale_for(float amax) {
+    if (!(amax > 0.0f)) return 1.0f;
+    const float t = amax * (1.0f / 448.0f);
+    uint32_t bits = __float_as_uint(t);
+    // round t up to a power of two: clear the mantissa, bump the exponent if it was nonzero
+    const uint32_t mant = bits & 0x007FFFFFu;
+    uint32_t e = bits & 0x7F800000u;
+    if (e == 0) return 1.1754943508222875e-38f * 1.0f;  // tiny amax: smallest normal
+    if (mant != 0) e += 0x00800000u;
+    if (e >= 0x7F800000u) e = 0x7F000000u;
+    return __uint_as_float(e);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+}  // namespace cst

@@ -1,0 +1,106 @@
+// Launch interfaces of the hot-path kernels (host side of the .cu files in this folder).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "layout.cuh"
+
+namespace cst {
+
+// relayout.cu
+cudaError_t launch_relayout(const uint8_t* wu, const uint8_t* wg, const uint8_t* wd, uint8_t* slot,
+                            int inter, int hidden, int num_sms, cudaStream_t stream);
+
+// router.cu
+int router_k_split(int H);
+cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
+                          int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
+                          float* partial, int32_t* topk_idx, float* topk_w, float* logits_out,
+                          float* group_scores_out, cudaStream_t stream);
+
+// route_pack.cu
+struct PackArgs {
+    // mode A (routes): topk_idx/topk_w [T, K]; slot_of_expert [E]
+    const int32_t* topk_idx;
+    const float* topk_w;
+    const int32_t* slot_of_expert;
+    int E;
+    int K;
+    int shared_slot;  // -1: none
+    // mode B (rows): row_slot [T] (one route per row, weight row_weight or 1), or every
+    // row to `single_slot` when row_slot is null and single_slot >= 0
+    const int32_t* row_slot;
+    int single_slot;
+    const float* row_weight_in;
+    int T;
+    int n_slots;
+    int max_rows;
+    int max_groups;
+    // outputs
+    GroupRec* groups;
+    int32_t* tile_group;  // [max_rows] group of each n-tile
+    int32_t* row_token;   // [max_rows]
+    float* row_weight;    // [max_rows]
+    int32_t* tk_row;      // [T, K + 1] (mode A) or [T] (mode B); -1 = not here
+    PackMeta* meta;
+};
+constexpr int kRoutePackMaxKeys = 32768;
+cudaError_t route_pack_init_attributes();
+cudaError_t launch_route_pack(const PackArgs& a, cudaStream_t stream);
+
+// pack_act.cu
+struct PackActArgs {
+    const void* src;         // [rows_src, K] activations
+    int src_dtype;           // 1 fp16, 2 bf16, 3 fp32
+    int64_t ld;              // row stride of src in elements
+    const int32_t* row_map;  // packed row -> source row (x pack); null: identity (h pack)
+    const GroupRec* groups;
+    const int32_t* tile_group;
+    const PackMeta* meta;
+    int K;                   // H (x) or I (h)
+    uint8_t* bfrag;          // B fragments
+    float* bscale;           // per (row, K block) scales
+};
+cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream);
+
+// grouped_ffn.cu
+struct FfnArgs {
+    const uint8_t* arena;
+    int64_t slot_bytes;
+    int64_t a_off;   // byte offset of this projection's chunks inside a slot
+    int64_t s0_off;  // scale grid (up or down)
+    int64_t s1_off;  // scale grid (gate), up/gate only
+    int KB;          // K / 128
+    int n_mb;        // output rows / 64
+    int scale_ld;    // columns of the scale grid (= KB)
+    const GroupRec* groups;
+    const PackMeta* meta;
+    const uint8_t* bfrag;
+    const float* bscale;
+    float* out;               // h [rows, I] (up/gate) or y [rows, H] (down)
+    int64_t ld_out;
+    const float* row_weight;  // down only
+    int* err;
+};
+cudaError_t grouped_ffn_init_attributes();
+cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream);
+
+// combine.cu
+struct CombineArgs {
+    const float* y;         // [rows, H] fp32 weighted expert outputs
+    int64_t ldy;
+    const int32_t* tk_row;  // [T, K1]; -1 = contribution absent on this device
+    int K1;
+    int T;
+    int H;
+    const void* residual;   // [T, H] in residual_dtype, or null
+    int residual_dtype;
+    void* out;              // [T, H]
+    int out_dtype;          // 1 fp16, 2 bf16, 3 fp32
+    const float* extra;     // [T, H] fp32 added before the cast (remote contributions), or null
+};
+cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream);
+
+}  // namespace cst

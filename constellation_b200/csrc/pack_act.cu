@@ -1,0 +1,112 @@
+// Activation packer: rows of x (bf16 / fp16 / fp32) or of the SwiGLU intermediate h (fp32)
+// -> E4M3 tensor-core B fragments, three terms per element.
+//
+// The grouped FFN kernels multiply FP8 E4M3 weights by activations on the FP8 tensor
+// pipe.  One E4M3 term carries 4 significant bits, so each activation element v of a
+// (row, 128-wide K block) is written as
+//     v = s * (q1 + q2 + q3),  q1 = e4m3(v/s), q2 = e4m3(v/s - q1), q3 = e4m3(v/s - q1 - q2)
+// with s the smallest power of two that maps the block's max |v| to <= 448.  The three
+// terms reproduce v/s to ~2^-12 relative (absolute floor 2^-10 in the scaled domain, i.e.
+// about 2e-6 of the block max), far inside the bf16 resolution of the inputs, and the
+// residuals are exact in fp32.  The grouped kernel applies s per (row, K block) and the
+// weight scale_inv per 128x128 weight block while accumulating in fp32 -- the same
+// algebra as dequantize-then-matmul (server/fp8_utils.py:4-39,
+// server/moe_layer_runtime.py:604-609).
+//
+// One warp per (packed row, K block): 128 elements, 4 per lane, one 32-bit store per term.
+// Rows of a group's last n-tile beyond its row count are written as zeros.
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "cst_common.cuh"
+#include "kernels.h"
+#include "layout.cuh"
+
+namespace cst {
+
+
+__device__ __forceinline__ void load4(const PackActArgs& a, int64_t src_row, int k, float (&v)[4]) {
+    if (src_row < 0) {
+        v[0] = v[1] = v[2] = v[3] = 0.0f;
+        return;
+    }
+    if (a.src_dtype == 3) {
+        const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(a.src) + src_row * a.ld + k);
+        v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    } else if (a.src_dtype == 2) {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.src) + src_row * a.ld + k);
+        v[0] = __uint_as_float(u.x << 16);
+        v[1] = __uint_as_float(u.x & 0xffff0000u);
+        v[2] = __uint_as_float(u.y << 16);
+        v[3] = __uint_as_float(u.y & 0xffff0000u);
+    } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __half*>(a.src) + src_row * a.ld + k);
+        const __half2 h0 = *reinterpret_cast<const __half2*>(&u.x);
+        const __half2 h1 = *reinterpret_cast<const __half2*>(&u.y);
+        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+        v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+    }
+}
+
+__global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
+    const int KB = a.K / kBlock;
+    const int n_tiles = a.meta->n_tiles;
+    const int lane = threadIdx.x & 31;
+    const int64_t n_tasks = int64_t(n_tiles) * kTileCols * KB;
+    const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t task = warp_global; task < n_tasks; task += n_warps) {
+        const int kb = static_cast<int>(task % KB);
+        const int64_t tr = task / KB;
+        const int tile = static_cast<int>(tr / kTileCols);
+        const int j = static_cast<int>(tr % kTileCols);  // token column inside the n-tile
+        const int gi = a.tile_group[tile];
+        const GroupRec gr = a.groups[gi];
+        const int nt = tile - gr.tile_base;
+        const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
+        const int r = nt * kTileCols + j;
+        int64_t src_row = -1;
+        if (r < gr.n_rows) {
+            const int prow = gr.row_start + r;
+            src_row = a.row_map ? a.row_map[prow] : prow;
+        }
+        float v[4];
+        load4(a, src_row, kb * kBlock + 4 * lane, v);
+        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        amax = warp_max(amax);
+        const float s = pow2_scale_for(amax);
+        const float inv = 1.0f / s;  // exact: s is a power of two
+        uint32_t q[kSplits] = {0u, 0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float rsd = v[e] * inv;
+#pragma unroll
+            for (int sp = 0; sp < kSplits; ++sp) {
+                const uint8_t b = e4m3_rn(rsd);
+                q[sp] |= uint32_t(b) << (8 * e);
+                rsd -= e4m3_to_f32(b);
+            }
+        }
+        // B fragment placement of k = 4 lane .. 4 lane + 3 inside the 128-wide block
+        const int ks = lane >> 3;
+        const int kk = 4 * (lane & 7);
+        const int t = (kk & 15) >> 2;
+        const int half = kk >> 4;
+        const int out_lane = j * 4 + t;
+        const int64_t tile_off = (int64_t(gr.tile_base) * KB + int64_t(kb) * NT + nt);
+        uint8_t* base = a.bfrag + tile_off * kBTileBytes;
+#pragma unroll
+        for (int sp = 0; sp < kSplits; ++sp) {
+            *reinterpret_cast<uint32_t*>(base + (ks * kSplits + sp) * kFragBytes + out_lane * 8 + half * 4) = q[sp];
+        }
+        if (lane == 0) a.bscale[tile_off * kTileCols + j] = s;
+    }
+}
+
+cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream) {
+    pack_act_kernel<<<num_sms * 8, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace cst

@@ -1,0 +1,203 @@
+// Dispatch planning: turn (token, k) -> expert routes into expert-sorted packed rows.
+//
+// Replaces the reference's per-(token, expert) dispatch loop (dispatch_topk_experts,
+// server/moe_layer_runtime.py:111-145, and the placement lookup find_expert_placement,
+// server/expert_placement.py:101-106): instead of one socket request per route, every
+// route that targets an expert resident on this device becomes one row of a packed
+// activation matrix whose rows are sorted by (expert slot, token, k).  The rows of one
+// slot are cut into groups of at most 16 rows (two 8-wide MMA n-tiles) that the grouped
+// FFN kernels consume.
+//
+// One CTA of 1024 threads.  Each route is encoded as a 31-bit key
+//   slot << 18 | token << 4 | k        (k == top_k marks the shared expert)
+// and the keys are bitonic-sorted in shared memory, which makes the packing fully
+// deterministic (no atomics decide an order).  Routes whose expert is not resident
+// here get key 0x7fffffff and sort to the end (under expert parallelism they belong to
+// another rank).
+#include <cstdint>
+
+#include "cst_common.cuh"
+#include "kernels.h"
+#include "layout.cuh"
+
+namespace cst {
+
+constexpr int kPackThreads = 1024;
+constexpr uint32_t kInvalidKey = 0x7fffffffu;
+constexpr int kRoutePackMaxSmem = kRoutePackMaxKeys * 4 + 8192 * 4;
+
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = s_warp[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        s_warp[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int warp_prefix = (warp == 0) ? 0 : s_warp[warp - 1];
+    const int tot = s_warp[31];
+    __syncthreads();
+    *total = tot;
+    return warp_prefix + x - v;
+}
+
+__global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, int n_keys_pow2) {
+    extern __shared__ uint32_t s_keys[];  // n_keys_pow2 keys, then n_slots ints
+    int* s_first = reinterpret_cast<int*>(s_keys + n_keys_pow2);
+    __shared__ int s_warp[32];
+    const int tid = threadIdx.x;
+    const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
+    const int K1 = mode_rows ? 1 : a.K + 1;
+    const int n_routes = mode_rows ? a.T : a.T * K1;
+
+    for (int i = tid; i < a.n_slots; i += kPackThreads) s_first[i] = 0x7fffffff;
+    for (int i = tid; i < a.T * K1; i += kPackThreads) a.tk_row[i] = -1;
+    // build keys
+    for (int i = tid; i < n_keys_pow2; i += kPackThreads) {
+        uint32_t key = kInvalidKey;
+        if (i < n_routes) {
+            int t, k, slot = -1;
+            if (mode_rows) {
+                t = i;
+                k = 0;
+                slot = a.row_slot ? a.row_slot[i] : a.single_slot;
+            } else {
+                t = i / K1;
+                k = i % K1;
+                if (k < a.K) {
+                    const int e = a.topk_idx[t * a.K + k];
+                    slot = (e >= 0 && e < a.E) ? a.slot_of_expert[e] : -1;
+                } else {
+                    slot = a.shared_slot;
+                }
+            }
+            if (slot >= 0 && slot < a.n_slots)
+                key = (uint32_t(slot) << 18) | (uint32_t(t) << 4) | uint32_t(k);
+        }
+        s_keys[i] = key;
+    }
+    __syncthreads();
+    // bitonic sort, ascending
+    for (int size = 2; size <= n_keys_pow2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < (n_keys_pow2 >> 1); i += kPackThreads) {
+                const int lo = 2 * i - (i & (stride - 1));
+                const int hi = lo + stride;
+                const bool asc = (lo & size) == 0;
+                const uint32_t a0 = s_keys[lo], a1 = s_keys[hi];
+                if ((a0 > a1) == asc) {
+                    s_keys[lo] = a1;
+                    s_keys[hi] = a0;
+                }
+            }
+            __syncthreads();
+        }
+    }
+    // number of valid rows and the first row of each slot
+    int valid_local = 0;
+    for (int i = tid; i < n_keys_pow2; i += kPackThreads) {
+        const uint32_t key = s_keys[i];
+        if (key != kInvalidKey) {
+            ++valid_local;
+            const int slot = int(key >> 18);
+            if (i == 0 || (s_keys[i - 1] >> 18) != uint32_t(slot)) s_first[slot] = i;
+        }
+    }
+    int n_rows;
+    block_exclusive_scan(valid_local, s_warp, &n_rows);
+    // group starts: every 16th row of a slot run, in row order.  Each thread owns a
+    // contiguous range of rows so that one block scan numbers the groups.
+    const int per = (n_rows + kPackThreads - 1) / kPackThreads;
+    const int r0 = tid * per, r1 = min(n_rows, r0 + per);
+    int starts = 0;
+    for (int p = r0; p < r1; ++p) {
+        const int slot = int(s_keys[p] >> 18);
+        if (((p - s_first[slot]) % kGroupRows) == 0) ++starts;
+    }
+    int n_groups;
+    int g = block_exclusive_scan(starts, s_warp, &n_groups);
+    // per-group row counts -> tile counts; each group start writes its record
+    int tiles_local = 0;
+    for (int p = r0; p < r1; ++p) {
+        const int slot = int(s_keys[p] >> 18);
+        if (((p - s_first[slot]) % kGroupRows) == 0) {
+            int end = p + 1;
+            while (end < n_rows && end < p + kGroupRows && int(s_keys[end] >> 18) == slot) ++end;
+            tiles_local += (end - p + kTileCols - 1) / kTileCols;
+        }
+    }
+    int n_tiles;
+    int tile = block_exclusive_scan(tiles_local, s_warp, &n_tiles);
+    const bool overflow = (n_rows > a.max_rows) || (n_groups > a.max_groups);
+    if (!overflow) {
+        for (int p = r0; p < r1; ++p) {
+            const uint32_t key = s_keys[p];
+            const int slot = int(key >> 18);
+            const int t = int((key >> 4) & 0x3fff);
+            const int k = int(key & 15);
+            a.row_token[p] = t;
+            float wt = 1.0f;
+            if (mode_rows) {
+                if (a.row_weight_in) wt = a.row_weight_in[t];
+            } else if (k < a.K) {
+                wt = a.topk_w[t * a.K + k];
+            }
+            a.row_weight[p] = wt;
+            a.tk_row[t * K1 + k] = p;
+            if (((p - s_first[slot]) % kGroupRows) == 0) {
+                int end = p + 1;
+                while (end < n_rows && end < p + kGroupRows && int(s_keys[end] >> 18) == slot) ++end;
+                const int nt = (end - p + kTileCols - 1) / kTileCols;
+                a.groups[g] = GroupRec{slot, p, end - p, tile};
+                for (int j = 0; j < nt; ++j) a.tile_group[tile + j] = g;
+                ++g;
+                tile += nt;
+            }
+        }
+    }
+    if (tid == 0) {
+        a.meta->n_rows = overflow ? 0 : n_rows;
+        a.meta->n_groups = overflow ? 0 : n_groups;
+        a.meta->n_tiles = overflow ? 0 : n_tiles;
+        a.meta->overflow = overflow ? 1 : 0;
+    }
+}
+
+cudaError_t route_pack_init_attributes() {
+    return cudaFuncSetAttribute(route_pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kRoutePackMaxSmem);
+}
+
+int route_pack_pow2(int n) {
+    int p = 1;
+    while (p < n) p <<= 1;
+    return p < 64 ? 64 : p;
+}
+
+size_t route_pack_smem(int n_keys_pow2, int n_slots) {
+    return size_t(n_keys_pow2) * 4 + size_t(n_slots) * 4;
+}
+
+cudaError_t launch_route_pack(const PackArgs& a, cudaStream_t stream) {
+    const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
+    const int n_routes = mode_rows ? a.T : a.T * (a.K + 1);
+    const int p2 = route_pack_pow2(n_routes);
+    const size_t smem = route_pack_smem(p2, a.n_slots);
+    route_pack_kernel<<<1, kPackThreads, smem, stream>>>(a, p2);
+    return cudaGetLastError();
+}
+
+}  // namespace cst

@@ -1,0 +1,241 @@
+// Fused sigmoid group-limited top-k router for a batch of tokens.
+//
+// Restates route_token_real (server/moe_layer_runtime.py:232-408) for T tokens at once:
+//   logits = gate_weight @ x        fp32, fixed summation order        (:322)
+//   scores = sigmoid(logits)                                             (:323)
+//   choice = scores + e_score_correction_bias, -inf where not resident   (:325-340)
+//   group score = sum of the top-2 choice values of each group          (:343-345)
+//   keep the topk_group best groups, choose top_k experts among them    (:347-371)
+//   weight = unbiased score / (sum + 1e-20) * routed_scaling_factor     (:373-381)
+// Every selection orders candidates by (value desc, index asc), so equal values go to
+// the lowest index; the k experts of a token are returned in that order.
+//
+// Two kernels:
+//   router_logits_kernel: [T, H] x [E, H]^T in fp32 on CUDA cores (the router needs exact
+//     fp32 products; TF32 tensor cores would change which experts win).  32x32 output
+//     tiles, K split across gridDim.z into fixed slices; partial sums go to
+//     partial[z][T][E] and are added in z order by the select kernel, so results are
+//     bit-identical from run to run.
+//   router_select_kernel: one warp per token does the sigmoid / bias / group / top-k
+//     logic with warp-shuffle arg-max reductions.
+#include <cfloat>
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "cst_common.cuh"
+#include "kernels.h"
+
+namespace cst {
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+constexpr int kRT = 32;   // tile edge (experts and tokens)
+constexpr int kRK = 32;   // K chunk per shared-memory step
+
+template <typename TX>
+__global__ void __launch_bounds__(256) router_logits_kernel(const TX* __restrict__ x, const float* __restrict__ w,
+                                                            float* __restrict__ partial, int T, int E, int H,
+                                                            int k_slice) {
+    __shared__ float xs[kRT][kRK + 1];
+    __shared__ float ws[kRT][kRK + 1];
+    const int e0 = blockIdx.x * kRT;
+    const int t0 = blockIdx.y * kRT;
+    const int kz = blockIdx.z;
+    const int k_begin = kz * k_slice;
+    const int tid = threadIdx.x;
+    const int tx = tid & 15;  // expert pair
+    const int ty = tid >> 4;  // token pair
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    for (int k0 = k_begin; k0 < k_begin + k_slice; k0 += kRK) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int idx = tid + i * 256;  // 0..1023
+            const int r = idx >> 5, c = idx & 31;
+            const int t = t0 + r;
+            xs[r][c] = (t < T) ? to_f32<TX>(x[int64_t(t) * H + k0 + c]) : 0.0f;
+            const int e = e0 + r;
+            ws[r][c] = (e < E) ? w[int64_t(e) * H + k0 + c] : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int c = 0; c < kRK; ++c) {
+            const float x0 = xs[2 * ty][c], x1 = xs[2 * ty + 1][c];
+            const float w0 = ws[2 * tx][c], w1 = ws[2 * tx + 1][c];
+            acc[0][0] = fmaf(x0, w0, acc[0][0]);
+            acc[0][1] = fmaf(x0, w1, acc[0][1]);
+            acc[1][0] = fmaf(x1, w0, acc[1][0]);
+            acc[1][1] = fmaf(x1, w1, acc[1][1]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int t = t0 + 2 * ty + i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int e = e0 + 2 * tx + j;
+            if (e < E) partial[(int64_t(kz) * T + t) * E + e] = acc[i][j];
+        }
+    }
+}
+
+struct RouterArgs {
+    const float* partial;   // [kz][T][E]
+    int kz;
+    const float* bias;      // [E]
+    const uint8_t* resident;  // [E] or null (all resident)
+    int T, E, n_group, topk_group, top_k, norm;
+    float scale;
+    int32_t* topk_idx;      // [T, top_k]
+    float* topk_w;          // [T, top_k]
+    float* logits_out;      // [T, E] or null
+    float* group_scores_out;  // [T, n_group] or null
+};
+
+// Warp arg-max with (value desc, index asc); inactive candidates carry idx = INT_MAX.
+__device__ __forceinline__ void warp_argmax(float& v, int& idx) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > v || (ov == v && oi < idx)) {
+            v = ov;
+            idx = oi;
+        }
+    }
+}
+
+constexpr int kSelWarps = 4;
+constexpr int kMaxE = 1024;
+
+__global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(RouterArgs a) {
+    __shared__ float s_choice[kSelWarps][kMaxE];
+    __shared__ float s_score[kSelWarps][kMaxE];
+    __shared__ uint32_t s_taken[kSelWarps][kMaxE / 32];
+    __shared__ float s_gs[kSelWarps][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kSelWarps + warp;
+    if (t >= a.T) return;
+    const int E = a.E;
+    float* ch = s_choice[warp];
+    float* sc = s_score[warp];
+    uint32_t* taken = s_taken[warp];
+    for (int e = lane; e < E; e += 32) {
+        float l = 0.0f;
+        for (int z = 0; z < a.kz; ++z) l += a.partial[(int64_t(z) * a.T + t) * E + e];
+        if (a.logits_out) a.logits_out[int64_t(t) * E + e] = l;
+        const float s = 1.0f / (1.0f + expf(-l));
+        const bool res = (a.resident == nullptr) || (a.resident[e] != 0);
+        ch[e] = res ? (s + a.bias[e]) : -INFINITY;
+        sc[e] = res ? s : 0.0f;
+    }
+    for (int i = lane; i < kMaxE / 32; i += 32) taken[i] = 0u;
+    __syncwarp();
+    // group scores: sum of the two largest choice values of each group
+    const int epg = E / a.n_group;
+    float gs = -INFINITY;
+    if (lane < a.n_group) {
+        float m1 = -INFINITY, m2 = -INFINITY;
+        for (int j = 0; j < epg; ++j) {
+            const float v = ch[lane * epg + j];
+            if (v > m1) {
+                m2 = m1;
+                m1 = v;
+            } else if (v > m2) {
+                m2 = v;
+            }
+        }
+        gs = m1 + m2;
+        s_gs[warp][lane] = gs;
+        if (a.group_scores_out) a.group_scores_out[int64_t(t) * a.n_group + lane] = gs;
+    }
+    __syncwarp();
+    // keep the topk_group best groups (value desc, index asc)
+    uint32_t gmask = 0u;
+    {
+        float v = (lane < a.n_group) ? gs : -INFINITY;
+        bool used = lane >= a.n_group;
+        for (int r = 0; r < a.topk_group; ++r) {
+            float bv = used ? -INFINITY : v;
+            int bi = used ? 0x7fffffff : lane;
+            warp_argmax(bv, bi);
+            gmask |= 1u << bi;
+            if (lane == bi) used = true;
+        }
+    }
+    // top_k experts over the group-masked choice values
+    float wsel = 0.0f;
+    int isel = -1;
+    float denom = 0.0f;
+    for (int r = 0; r < a.top_k; ++r) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < E; e += 32) {
+            if (taken[e >> 5] & (1u << (e & 31))) continue;
+            const float v = ((gmask >> (e / epg)) & 1u) ? ch[e] : -INFINITY;
+            if (v > bv || (v == bv && e < bi)) {
+                bv = v;
+                bi = e;
+            }
+        }
+        warp_argmax(bv, bi);
+        if (lane == 0) taken[bi >> 5] |= 1u << (bi & 31);
+        __syncwarp();
+        const float wv = sc[bi];
+        denom += wv;  // sequential sum in selection order
+        if (lane == r) {
+            isel = bi;
+            wsel = wv;
+        }
+    }
+    if (lane < a.top_k) {
+        float wv = wsel;
+        if (a.norm && a.top_k > 1) wv = wv / (denom + 1e-20f);
+        wv = wv * a.scale;
+        a.topk_idx[int64_t(t) * a.top_k + lane] = isel;
+        a.topk_w[int64_t(t) * a.top_k + lane] = wv;
+    }
+}
+
+int router_k_split(int H) {
+    const int chunks = H / kRK;
+    for (int z : {8, 4, 2}) {
+        if (chunks % z == 0) return z;
+    }
+    return 1;
+}
+
+// x_dtype: 1 fp16, 2 bf16, 3 fp32.  partial needs k_split * T * E floats.
+cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
+                          int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
+                          float* partial, int32_t* topk_idx, float* topk_w, float* logits_out,
+                          float* group_scores_out, cudaStream_t stream) {
+    const int kz = router_k_split(H);
+    dim3 grid((E + kRT - 1) / kRT, (T + kRT - 1) / kRT, kz);
+    const int k_slice = H / kz;
+    if (x_dtype == 2) {
+        router_logits_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), w, partial, T, E, H, k_slice);
+    } else if (x_dtype == 1) {
+        router_logits_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(x), w, partial, T, E, H,
+                                                               k_slice);
+    } else {
+        router_logits_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(x), w, partial, T, E, H,
+                                                              k_slice);
+    }
+    RouterArgs a{partial, kz, bias, resident, T, E, n_group, topk_group, top_k, norm, scale,
+                 topk_idx, topk_w, logits_out, group_scores_out};
+    router_select_kernel<<<(T + kSelWarps - 1) / kSelWarps, kSelWarps * 32, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace cst

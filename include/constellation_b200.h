@@ -1,0 +1,188 @@
+/*
+ * constellation_b200 -- C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * Plain pointers, sizes and status codes; no C++ or torch types cross this boundary.
+ * Every device pointer argument is caller-owned, except the expert arena the context
+ * allocates and fills through cst_upload_expert.  All work is enqueued on the `stream`
+ * argument (a cudaStream_t passed as void*; NULL = legacy default stream); nothing
+ * synchronises the device except cst_device_error and cst_destroy.
+ *
+ * Threading: one context per device; calls on one context must be serialised by the
+ * caller, like the reference node's one worker thread per GPU
+ * (expert_node_v2/main.cc:132-149) and its registry lock (worker.cc:120, control.cc:172).
+ *
+ * Status codes (int): 0 ok; 1 unknown expert; 2 expert not resident on this device;
+ * 4 backend failure -- these three mirror the worker reply statuses
+ * (expert_node_v2/worker.cc:112-131) -- plus 3 invalid argument, 5 CUDA error,
+ * 6 NCCL / peer error, 7 a device-side wait hit its iteration limit.
+ * cst_last_error() returns the message of the last failure on the calling thread.
+ */
+#ifndef CONSTELLATION_B200_H_
+#define CONSTELLATION_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CST_OK 0
+#define CST_ERR_UNKNOWN_EXPERT 1
+#define CST_ERR_NOT_RESIDENT 2
+#define CST_ERR_INVALID_ARG 3
+#define CST_ERR_BACKEND 4
+#define CST_ERR_CUDA 5
+#define CST_ERR_PEER 6
+#define CST_ERR_DEVICE_TIMEOUT 7
+
+/* Activation dtypes; 1 and 2 are the values of common::ActivationDType
+ * (common/protocol.h:48-52). */
+#define CST_DTYPE_FP16 1
+#define CST_DTYPE_BF16 2
+#define CST_DTYPE_FP32 3
+
+/* cst_moe_layer / cst_moe_routed flags */
+#define CST_FLAG_ADD_SHARED 1u
+
+typedef struct cst_ctx cst_ctx;
+
+/* Layer geometry and router hyper-parameters.  Mirrors the router config that
+ * run_moe_layer reads (server/moe_layer_runtime.py:428-522: n_group, topk_group, top_k,
+ * norm_topk_prob, routed_scaling_factor, n_routed_experts, hidden_size) plus the expert
+ * shape of ExpertWorkspaceConfigV2 (expert_node_v2/expert_format_v2.h:31-34).
+ * hidden_dim and inter_dim must be multiples of 128; block_size must be 128. */
+typedef struct cst_config {
+    int32_t hidden_dim;
+    int32_t inter_dim;
+    int32_t n_routed_experts; /* router width E (<= 1024) */
+    int32_t n_group;          /* <= 32, divides E */
+    int32_t topk_group;
+    int32_t top_k;            /* <= 15 */
+    int32_t norm_topk_prob;
+    float routed_scaling_factor;
+    int32_t block_size;
+    int32_t n_slots;          /* expert slots in this device's arena (routed + shared) */
+    int32_t max_tokens;       /* largest T of one layer call */
+    int32_t max_rows;         /* largest number of (token, expert) rows per call; 0 = max_tokens*(top_k+1) */
+} cst_config;
+
+/* One expert in the reference upload format (ExpertTensorBundleV2,
+ * expert_node_v2/expert_format_v2.h:59-86): float8_e4m3fn weights, row-major, and fp32
+ * scale_inv grids [ceil(rows/row_block), ceil(cols/col_block)], row-major.  Pointers may
+ * be host or device memory. */
+typedef struct cst_expert_weights {
+    const uint8_t* w_up;         /* [rows=inter, cols=hidden] */
+    const float* w_up_scale;
+    const uint8_t* w_gate;       /* [inter, hidden] */
+    const float* w_gate_scale;
+    const uint8_t* w_down;       /* [hidden, inter] */
+    const float* w_down_scale;
+    int32_t rows;                /* inter */
+    int32_t cols;                /* hidden */
+    int32_t row_block;
+    int32_t col_block;
+} cst_expert_weights;
+
+/* Creates a context on `device`: validates the config, allocates the expert arena
+ * (n_slots experts in the kernels' fragment-major layout) and the per-call workspace
+ * sized for max_rows.  Replaces CreateBackendWorkspaceV2 / InitExpertWorkspaceCudaV2
+ * (backend/backend_workspace_v2.cc:30-89, backend/cuda/backend_cuda_v2.cc:166-197). */
+int cst_create(int32_t device, const cst_config* cfg, cst_ctx** out);
+void cst_destroy(cst_ctx* ctx);
+
+/* Uploads one expert into arena slot `slot` and makes router expert `expert_id`
+ * (0 <= expert_id < n_routed_experts) resident there; expert_id = -1 uploads the shared
+ * expert (see cst_set_shared_slot).  Validates dtype-free shape / block / size rules of
+ * BuildExpertWeightsViewV2 (expert_format_v2.cc:68-175).  Replaces the backend registry's
+ * upload_expert hook UploadExpertCudaV2 (backend/cuda/backend_cuda_v2.cc:94-145,
+ * backend/backend_registry_v2.h:20-23).  Stream-ordered; the source may be reused once
+ * the stream has passed this call. */
+int cst_upload_expert(cst_ctx* ctx, int32_t slot, int32_t expert_id, const cst_expert_weights* w,
+                      void* stream);
+
+/* Makes `slot` non-resident (the free_expert_weights hook, FreeExpertWeightsCudaV2,
+ * backend/cuda/backend_cuda_v2.cc:147-164).  The arena memory is kept for reuse. */
+int cst_free_expert(cst_ctx* ctx, int32_t slot);
+
+/* Slot holding router expert `expert_id`, or -1 (ExpertRegistryV2::FindDeviceStorage,
+ * expert_node_v2/expert_registry_v2.cc:437). */
+int32_t cst_find_slot(const cst_ctx* ctx, int32_t expert_id);
+
+/* Marks `slot` as the shared expert (-1: none). */
+int cst_set_shared_slot(cst_ctx* ctx, int32_t slot);
+
+/* Routing for T tokens (route_token_real, server/moe_layer_runtime.py:232-408, batched):
+ *   x            [T, hidden] in x_dtype (device)
+ *   gate_weight  [n_routed_experts, hidden] fp32 (device)
+ *   bias         [n_routed_experts] fp32 e_score_correction_bias (device)
+ *   resident     [n_routed_experts] uint8 mask or NULL (all resident)
+ *   top_k        experts per token (<= cfg.top_k; callers pass min(top_k, #resident))
+ *   topk_idx     [T, top_k] int32 out, sorted by (biased score desc, index asc)
+ *   topk_weight  [T, top_k] fp32 out
+ *   logits, group_scores: optional fp32 outputs [T, E] and [T, n_group] (aux), or NULL. */
+int cst_route(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, const float* gate_weight,
+              const float* bias, const uint8_t* resident, int32_t top_k, int32_t* topk_idx,
+              float* topk_weight, float* logits, float* group_scores, void* stream);
+
+/* Routed experts for given routes + fp32 combine (+ shared expert when flags has
+ * CST_FLAG_ADD_SHARED): run_topk_moe_layer / dispatch_topk_experts / combine_outputs_torch
+ * (server/moe_layer_runtime.py:111-229) for a batch.  Routes to experts that are not
+ * resident here contribute nothing.  out: [T, hidden] in out_dtype. */
+int cst_moe_routed(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, const int32_t* topk_idx,
+                   const float* topk_weight, int32_t top_k, uint32_t flags, void* out, int32_t out_dtype,
+                   void* stream);
+
+/* Whole layer: route -> dispatch -> grouped FP8 SwiGLU -> combine (+ shared).
+ * run_moe_layer (server/moe_layer_runtime.py:411-578) batched over T tokens, plus the
+ * shared-expert sum of run_sparse_layer (server/full_model_runtime.py:283-348).
+ * topk_idx / topk_weight receive the routes when non-NULL.  residual (same dtype as
+ * x, or NULL) is added before the final cast (full_model_runtime.py:355). */
+int cst_moe_layer(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, const float* gate_weight,
+                  const float* bias, const uint8_t* resident, int32_t top_k, uint32_t flags,
+                  const void* residual, void* out, int32_t out_dtype, int32_t* topk_idx,
+                  float* topk_weight, void* stream);
+
+/* Grouped expert FFN over rows that are already assigned to slots (the expert node's
+ * batched request path): y[r] = row_weight[r] * Expert_{row_slot[r]}(x[r]).
+ *   x          [R, hidden] in x_dtype; row_slot [R] int32 slot ids; row_weight [R] or NULL (1.0)
+ *   y          [R, hidden] in y_dtype (fp32 keeps the unrounded expert output) */
+int cst_grouped_ffn(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t R, const int32_t* row_slot,
+                    const float* row_weight, void* y, int32_t y_dtype, void* stream);
+
+/* One expert, `batch` rows: the BackendWorkspaceV2::RunExpertRequest replacement
+ * (backend/backend_workspace_v2.h:18-21; backend/cuda/backend_workspace_cuda_v2.cc:139-181)
+ * without its batch_size == 1 restriction.  in_dtype / out_dtype: CST_DTYPE_FP16 or BF16
+ * (any pair, as the reference dispatches).  Returns 1 for an expert id outside the router
+ * range and 2 when the expert is not resident on this device, like the worker. */
+int cst_expert_forward(cst_ctx* ctx, int32_t expert_id, const void* x, int32_t in_dtype, int32_t batch,
+                       void* y, int32_t out_dtype, void* stream);
+
+/* Synchronises the context's device, then returns CST_OK or CST_ERR_DEVICE_TIMEOUT if a
+ * kernel's bounded wait gave up since the last call (and clears the flag). */
+int cst_device_error(cst_ctx* ctx);
+
+/* Per-stage device timing (the reference has only ad hoc host timers, server/client.py:130-176,
+ * and cudaEvent means in its benchmark harness, test_benchmark_run_expert_cuda_v2.cc:310-368).
+ * When enabled, every layer-level call records CUDA events at its stage boundaries:
+ *   0 router, 1 route_pack, 2 pack x, 3 grouped up/gate, 4 pack h, 5 grouped down, 6 combine.
+ * cst_profile_read waits for the recorded calls, writes max_calls x CST_N_STAGES
+ * milliseconds (row-major) and returns the number of calls written (negative status on error). */
+#define CST_N_STAGES 7
+int cst_profile_enable(cst_ctx* ctx, int32_t enable);
+int cst_profile_read(cst_ctx* ctx, float* stage_ms, int32_t max_calls);
+
+/* Context facts: out[0] arena bytes, [1] bytes per slot, [2] workspace bytes,
+ * [3] number of SMs, [4] resident routed experts, [5] shared slot. Returns #values written. */
+int cst_ctx_info(const cst_ctx* ctx, int64_t* out, int32_t n);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* cst_last_error(void);
+
+/* ABI version (major * 100 + minor). */
+int32_t cst_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CONSTELLATION_B200_H_ */

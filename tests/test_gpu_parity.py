@@ -1,0 +1,223 @@
+"""CUDA path vs the CPU oracle on seeded inputs (needs a B200).
+
+Tolerances (written here, used below):
+* routing: ``topk_idx`` bit-exact for every token whose selection margin (oracle) is
+  above 1e-5 -- a closer call depends on the last ulp of the fp32 logit and is reported,
+  not compared; weights within rtol 2e-6.
+* expert / layer outputs vs the fp32 dequantize-then-matmul oracle: normwise relative
+  error ``max|a - b| / max|ref|`` per token row <= 1e-2 (BASELINE's bf16 bar); the
+  measured errors are far below (about 3e-3 for bf16 outputs, 1e-4 for fp32).
+* the reference node's own thresholds on its dummy fixture
+  (test_benchmark_run_expert_cuda_v2.cc:302-305): max_abs <= 5e-3, mean_abs <= 1e-3,
+  cos >= 0.9999.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import cases, codec, refbuild, router
+from oracle.expert import DequantExpert
+from oracle.layer import moe_layer
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-2
+
+
+def rowwise_rel(a: np.ndarray, ref: np.ndarray) -> float:
+    a = np.atleast_2d(a).astype(np.float64)
+    ref = np.atleast_2d(ref).astype(np.float64)
+    num = np.abs(a - ref).max(axis=1)
+    den = np.maximum(np.abs(ref).max(axis=1), 1e-30)
+    return float((num / den).max())
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def make_ctx(dev, H, I, E=64, G=8, TG=4, K=8, n_slots=8, max_tokens=64):
+    from constellation_b200.context import ExpertContext, MoEConfig
+
+    cfg = MoEConfig(hidden_size=H, moe_intermediate_size=I, n_routed_experts=E, n_group=G, topk_group=TG,
+                    num_experts_per_tok=K)
+    return ExpertContext(dev, cfg, n_slots=n_slots, max_tokens=max_tokens)
+
+
+def test_library_is_sm100a(dev):
+    from constellation_b200 import _lib
+
+    assert _lib.lib.cst_abi_version() >= 100
+
+
+@pytest.mark.parametrize("H,I,n", [(256, 128, 1), (256, 128, 5), (512, 256, 16), (1024, 384, 11)])
+def test_expert_forward_vs_oracle(dev, H, I, n):
+    ctx = make_ctx(dev, H, I, E=32, G=4, TG=2, K=4, n_slots=2, max_tokens=16)
+    e = cases.expert(300 + n, H, I)
+    ctx.upload_bundle(1, 7, e)
+    x = cases.activations(400 + n, n, H)
+    xt = torch.from_numpy(x).to(dev, torch.bfloat16)
+    y = ctx.expert_forward(7, xt, out_dtype=torch.float32)
+    ref = DequantExpert(e).forward(x)
+    err = rowwise_rel(y.cpu().numpy(), ref)
+    assert err < 2e-3, err
+    yb = ctx.expert_forward(7, xt, out_dtype=torch.bfloat16)
+    assert rowwise_rel(yb.float().cpu().numpy(), ref) < REL_TOL
+
+
+def test_expert_forward_status_codes(dev):
+    from constellation_b200._lib import CstError
+
+    ctx = make_ctx(dev, 256, 128, E=32, G=4, TG=2, K=4, n_slots=2, max_tokens=4)
+    x = torch.zeros((1, 256), dtype=torch.bfloat16, device=dev)
+    with pytest.raises(CstError) as ei:
+        ctx.expert_forward(5, x)
+    assert ei.value.code == 2  # not resident here
+    with pytest.raises(CstError) as ei:
+        ctx.expert_forward(99, x)
+    assert ei.value.code == 1  # unknown expert
+
+
+def test_dummy_fixture_full_size_vs_reference(dev, golden):
+    """The reference's dummy bundle (bytes include 0x7F/0xFF, decoded as +-448 like its LUT)."""
+    g = golden("expert_golden")
+    H, I = 7168, 2048
+    e = refbuild.dummy_expert_formula(H, I)
+    ctx = make_ctx(dev, H, I, E=256, n_slots=1, max_tokens=2)
+    ctx.upload_bundle(0, 3, e)
+    for din, dout in [(1, 1), (2, 2)]:
+        key = f"dummy_full__in{din}_out{dout}"
+        xb = g[key + "__x"]
+        tdt = torch.float16 if din == 1 else torch.bfloat16
+        xt = torch.from_numpy(xb.view(np.int16)).view(tdt).reshape(1, H).to(dev)
+        y = ctx.expert_forward(3, xt, out_dtype=(torch.float16 if dout == 1 else torch.bfloat16))
+        got = y.float().cpu().numpy()[0]
+        ref = (codec.decode_fp16 if dout == 1 else codec.decode_bf16)(g[key + "__y"])
+        d = np.abs(got - ref)
+        cos = float(np.dot(got, ref) / (np.linalg.norm(got) * np.linalg.norm(ref)))
+        # the reference output itself is rounded to 16 bits: compare in its units
+        ulp = 2.0 ** -8 if dout == 2 else 2.0 ** -11
+        assert d.max() <= max(5e-3, 2 * ulp * np.abs(ref).max()), d.max()
+        assert d.mean() <= 1e-3 * max(1.0, np.abs(ref).mean()), d.mean()
+        assert cos >= 0.9999, cos
+
+
+@pytest.mark.parametrize("case", ["small", "bias_heavy", "restricted", "g4_k6", "full"])
+def test_router_vs_oracle(dev, golden, case):
+    g = golden("router_golden")
+    seed, T, E, H, G, TG, K = (int(v) for v in g[f"{case}__cfg"])
+    x = cases.activations(seed, T, H)
+    w, b = cases.router(seed, E, H, bias_std=float(g[f"{case}__bias_std"]))
+    res = None
+    resident_t = None
+    if int(g[f"{case}__has_resident"]):
+        res = np.zeros(E, bool)
+        res[g[f"{case}__resident"]] = True
+        resident_t = torch.from_numpy(res.astype(np.uint8)).to(dev)
+    k = K if res is None else min(K, int(res.sum()))
+    ctx = make_ctx(dev, H, 128, E=E, G=G, TG=TG, K=K, n_slots=0, max_tokens=T)
+    idx, wt, logits, gs = ctx.route(torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev),
+                                    torch.from_numpy(b).to(dev), resident=resident_t, top_k=k, return_aux=True)
+    r = router.route_batched(x, w, b, n_group=G, topk_group=TG, top_k=K, resident_mask=res)
+    ok = r.margin > 1e-5
+    np.testing.assert_array_equal(idx.cpu().numpy()[ok], r.topk_idx[ok])
+    np.testing.assert_allclose(wt.cpu().numpy()[ok], r.topk_weight[ok], rtol=2e-6, atol=1e-7)
+    np.testing.assert_allclose(logits.cpu().numpy(), r.logits, rtol=1e-4, atol=2e-5)
+    # and against the reference itself (golden fixture)
+    np.testing.assert_array_equal(idx.cpu().numpy()[ok], g[f"{case}__topk_idx"][ok])
+
+
+def test_router_repeat_bit_stable(dev):
+    """10 runs bit-identical (1_smoke_moe_router_validation.py:117-162)."""
+    T, E, H = 32, 256, 7168
+    x = torch.from_numpy(cases.activations(5, T, H)).to(dev, torch.bfloat16)
+    w, b = cases.router(5, E, H)
+    w, b = torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev)
+    ctx = make_ctx(dev, H, 128, E=E, n_slots=0, max_tokens=T)
+    i0, w0 = ctx.route(x, w, b)
+    for _ in range(10):
+        i1, w1 = ctx.route(x, w, b)
+        assert torch.equal(i0, i1) and torch.equal(w0, w1)
+
+
+def _layer_setup(dev, seed, T, E, H, I, G, TG, K, shared=True, max_tokens=None):
+    x = cases.activations(seed, T, H)
+    w, b = cases.router(seed, E, H, bias_std=0.05)
+    experts = {e: cases.expert(1000 * seed + e, H, I) for e in range(E)}
+    sh = cases.expert(1000 * seed + 999, H, I) if shared else None
+    ctx = make_ctx(dev, H, I, E=E, G=G, TG=TG, K=K, n_slots=E + 1, max_tokens=max_tokens or T)
+    for e in range(E):
+        ctx.upload_bundle(e, e, experts[e])
+    if shared:
+        ctx.upload_bundle(E, -1, sh)
+    return ctx, x, w, b, experts, sh
+
+
+@pytest.mark.parametrize("T", [1, 4, 37])
+def test_moe_layer_vs_oracle(dev, golden, T):
+    E, H, I, G, TG, K = 16, 256, 128, 4, 2, 4
+    ctx, x, w, b, experts, sh = _layer_setup(dev, 51 + T, T, E, H, I, G, TG, K)
+    out, idx, wt = ctx.moe_layer(torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev),
+                                 torch.from_numpy(b).to(dev), return_routes=True, out_dtype=torch.float32)
+    de = {e: DequantExpert(v) for e, v in experts.items()}
+    ref = moe_layer(x, w, b, de, DequantExpert(sh), n_group=G, topk_group=TG, top_k=K)
+    ok = ref.route.margin > 1e-5
+    np.testing.assert_array_equal(idx.cpu().numpy()[ok], ref.route.topk_idx[ok])
+    assert rowwise_rel(out.cpu().numpy()[ok], ref.out_f32[ok]) < 2e-3
+
+
+def test_moe_layer_matches_reference_golden(dev, golden):
+    """Same layer as tests/golden/layer_golden.npz (reference route_token_real +
+    dequant path + combine_outputs_torch), bf16 output within 1e-2."""
+    g = golden("layer_golden")
+    seed, T, E, H, I, G, TG, K = (int(v) for v in g["cfg"])
+    x = cases.activations(seed, T, H)
+    w, b = cases.router(seed, E, H, bias_std=0.05)
+    ctx = make_ctx(dev, H, I, E=E, G=G, TG=TG, K=K, n_slots=E + 1, max_tokens=T)
+    for e in range(E):
+        ctx.upload_bundle(e, e, cases.expert(1000 + e, H, I))
+    ctx.upload_bundle(E, -1, cases.expert(999, H, I))
+    out, idx, _ = ctx.moe_layer(torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev),
+                                torch.from_numpy(b).to(dev), return_routes=True)
+    np.testing.assert_array_equal(idx.cpu().numpy(), g["topk_idx"])
+    assert out.dtype == torch.bfloat16
+    assert rowwise_rel(out.float().cpu().numpy(), g["out_f32"]) <= REL_TOL
+
+
+def test_moe_layer_repeat_bit_stable(dev):
+    E, H, I, G, TG, K = 16, 256, 128, 4, 2, 4
+    ctx, x, w, b, _, _ = _layer_setup(dev, 77, 9, E, H, I, G, TG, K)
+    args = (torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev))
+    o0 = ctx.moe_layer(*args)
+    for _ in range(10):
+        assert torch.equal(ctx.moe_layer(*args), o0)
+
+
+def test_grouped_ffn_config1_shape(dev):
+    """Grouped matvec over several full-size experts with 1..16 rows each (config 1 shapes)."""
+    H, I, n_exp = 7168, 2048, 3
+    ctx = make_ctx(dev, H, I, E=256, n_slots=n_exp, max_tokens=64)
+    es = [cases.expert(700 + i, H, I) for i in range(n_exp)]
+    for i, e in enumerate(es):
+        ctx.upload_bundle(i, i, e)
+    counts = [1, 16, 7]
+    rows = sum(counts)
+    x = cases.activations(800, rows, H)
+    slot = np.repeat(np.arange(n_exp), counts).astype(np.int32)
+    wts = np.linspace(0.5, 1.5, rows).astype(np.float32)
+    y = ctx.grouped_ffn(torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(slot).to(dev),
+                        torch.from_numpy(wts).to(dev))
+    y = y.cpu().numpy()
+    r0 = 0
+    for i, n in enumerate(counts):
+        ref = DequantExpert(es[i]).forward(x[r0:r0 + n]) * wts[r0:r0 + n, None]
+        assert rowwise_rel(y[r0:r0 + n], ref) < 2e-3
+        r0 += n
+
+
+def test_device_error_clear(dev):
+    ctx = make_ctx(dev, 256, 128, E=32, G=4, TG=2, K=4, n_slots=1, max_tokens=4)
+    ctx.device_error()  # no kernel wait gave up
