@@ -1,0 +1,460 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MoE-layer hot path (decode).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (``config.workload``): one DeepSeek-V3 MoE layer at decode batch T=64 (bf16
+hidden 7168, 256 routed FP8 experts + 1 shared, n_group 8 / topk_group 4 / top_k 8,
+scaling 2.5), experts sharded 256/N per GPU (expert parallel over NCCL for N > 1), tokens
+sharded T/N per rank.  A step = one full layer: route -> dispatch -> grouped FP8 SwiGLU
+-> combine + shared expert.  Total work is fixed as N grows ("scaling": "strong").  Weights
+are seeded synthetic N(0, 0.02) quantized per 128x128 block (no checkpoint is available);
+the 11.3 GB of expert weights (1.4 GB per GPU at N=8) exceed the 126 MB L2, so no flush is
+needed between steps.
+
+Printed (rank 0, one JSON line): tokens/s of the whole job (``value``), µs per layer, the
+grouped-kernel roofline (algorithmic bytes / CUDA-event time vs the measured HBM copy
+bandwidth), the same metric end to end through the public API with host buffers
+(``e2e``), the reference CPU path timed on this host (``cpu_baseline``), and the SM clocks
+sampled during the timed region.
+
+``--impl reference`` times the reference's CPU implementation of the path on this host's
+cores instead: the reference node's OpenMP FP8 expert kernels (compiled from the
+reference sources into ``oracle/_ref``) at batch 1 per (token, expert), as the reference
+runs them, plus the CPU restatement of its router and fp32 combine.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+H, I, E, G, TG, K = 7168, 2048, 256, 8, 4, 8
+EXPERT_BYTES = 3 * I * H + 3 * (I // 128) * (H // 128) * 4  # 44,050,944
+ROUTER_BYTES = E * H * 4 + E * 4
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--tokens", type=int, default=64, help="decode batch T (whole job)")
+    p.add_argument("--ep-mode", choices=["allgather", "alltoall"], default="allgather")
+    p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
+    p.add_argument("--cpu-sample-tokens", type=int, default=2)
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--resident-experts", type=int, default=E,
+                   help="upload only the first N routed experts of each rank (small profiling case; "
+                        "routes to the others contribute nothing)")
+    return p.parse_args()
+
+
+def measured_peaks():
+    f = REPO / "MEASURED_PEAKS.json"
+    if f.is_file():
+        try:
+            d = json.loads(f.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.p = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        for line in Path(self.f.name).read_text().splitlines():
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------------------
+def setup_layer(torch, rank, world, T_total, dev, resident=E):
+    from constellation_b200 import synthetic
+    from constellation_b200.context import ExpertContext, MoEConfig
+
+    cfg = MoEConfig()
+    epr = E // world
+    ctx = ExpertContext(dev, cfg, n_slots=epr + 1, max_tokens=T_total)
+    for j in range(min(epr, resident)):
+        e = rank * epr + j
+        ex = synthetic.make_expert(H, I, seed=1000 + e, device=dev)
+        ctx.upload_expert(j, e, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
+        del ex
+    sh = synthetic.make_expert(H, I, seed=999, device=dev)
+    ctx.upload_expert(epr, -1, sh.w_up, sh.s_up, sh.w_gate, sh.s_gate, sh.w_down, sh.s_down)
+    del sh
+    gw, gb = synthetic.make_router(H, E, seed=7, device=dev)
+    x_all = synthetic.make_activations(T_total, H, seed=11, device=dev)
+    Tl = T_total // world
+    x = x_all[rank * Tl:(rank + 1) * Tl].contiguous()
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    return ctx, gw, gb, x, x_all
+
+
+def touched_experts(torch, ctx, gw, gb, x_all):
+    idx, _ = ctx.route(x_all, gw, gb)
+    return int(torch.unique(idx).numel())
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+    T = args.tokens
+    if T % world:
+        raise SystemExit(f"T={T} does not shard over {world} ranks")
+    from constellation_b200.ep import ExpertParallelMoE
+
+    ctx, gw, gb, x, x_all = setup_layer(torch, rank, world, T, dev, args.resident_experts)
+    moe = ExpertParallelMoE(ctx, rank=rank, world=world, n_routed_experts=E, mode=args.ep_mode)
+    out = torch.empty_like(x)
+
+    def step():
+        if world == 1:
+            ctx.moe_layer(x, gw, gb, out=out)
+        else:
+            out.copy_(moe.forward(x, gw, gb))
+
+    use_graph = (not args.no_graph) and world == 1
+    graph = None
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    if use_graph:
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+    launches_per_step = 8 if world == 1 else 16
+
+    def timed(fn, k):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(k):
+            fn()
+        b.record()
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    run = graph.replay if graph is not None else step
+    with ClockSampler(local) as clk:
+        ms_total = timed(run, args.steps)
+    clocks = clk.summary()
+    ms_step = ms_total / args.steps
+    value = T / (ms_step / 1e3)
+
+    # end to end through the public API: pinned host input -> layer -> host output
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty_like(out, device="cpu").pin_memory()
+
+    def e2e_step():
+        x.copy_(x_host, non_blocking=True)
+        run()
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    ms_e2e = timed(e2e_step, args.steps) / args.steps
+    h2d = x_host.numel() * x_host.element_size() * world
+    d2h = out_host.numel() * out_host.element_size() * world
+
+    # per-stage device times (separate profiled pass) for the roofline
+    ctx.profile(True)
+    nprof = 10
+    for _ in range(nprof):
+        if world == 1:
+            ctx.moe_layer(x, gw, gb, out=out)
+        else:
+            moe.forward(x, gw, gb)
+    torch.cuda.synchronize(dev)
+    stages = ctx.profile_read()
+    ctx.profile(False)
+    upg = [s["grouped_up_gate"] for s in stages if s["grouped_up_gate"] > 0]
+    dn = [s["grouped_down"] for s in stages if s["grouped_down"] > 0]
+    stage_ms = {k: statistics.mean(s[k] for s in stages) for k in stages[0]} if stages else {}
+
+    # algorithmic bytes of the grouped kernels on this rank
+    U_total = touched_experts(torch, ctx, gw, gb, x_all) if world == 1 else None
+    if world > 1:
+        idx, _ = ctx.route(x_all, gw, gb)
+        lo, hi = rank * (E // world), (rank + 1) * (E // world)
+        loc = idx[(idx >= lo) & (idx < hi)]
+        U_local = int(torch.unique(loc).numel())
+        rows = int(loc.numel())
+        U_t = torch.tensor([U_local], device=dev)
+        dist.all_reduce(U_t)
+        U_total = int(U_t.item())
+    else:
+        U_local = U_total
+        rows = T * K
+    rows_incl_shared = rows + T // world
+    n_mat = U_local + 1
+    grid = (I // 128) * (H // 128) * 4
+    upg_bytes = n_mat * (2 * I * H + 2 * grid) + rows_incl_shared * (H * 2 + I * 4)
+    dn_bytes = n_mat * (I * H + grid) + rows_incl_shared * (I * 4 + H * 4)
+    peak, peak_kind = measured_peaks()
+    upg_ms = statistics.mean(upg) if upg else float("nan")
+    dn_ms = statistics.mean(dn) if dn else float("nan")
+    ach_upg = upg_bytes / (upg_ms / 1e3) / 1e9
+    pair_bytes = n_mat * EXPERT_BYTES + rows_incl_shared * (H * 2 + H * 4)
+    ach_pair = pair_bytes / ((upg_ms + dn_ms) / 1e3) / 1e9
+    layer_bytes = pair_bytes + ROUTER_BYTES + (T // world) * H * 4
+
+    line = {
+        "metric": "MoE-layer decode tokens/s (1 DeepSeek-V3 MoE layer, T=64, 256 FP8 experts + shared)",
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "us_per_layer": round(ms_step * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "e4m3 weights x e4m3(3-term) activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, 128x128 block E4M3; RMS-normalised N(0,1) bf16 hidden)",
+        "config": {"workload": "config2_decode_T64_one_layer", "tokens": T, "routed_experts": E,
+                   "shared_expert": True, "hidden": H, "inter": I, "top_k": K,
+                   "parallelism": f"ep{world}" + (f"_{args.ep_mode}" if world > 1 else ""),
+                   "cuda_graph": graph is not None,
+                   "touched_experts": U_total,
+                   "l2": "no flush: 11.3 GB of expert weights (>= 1.2 GB per GPU) exceed the 126 MB L2"},
+        "roofline": {"kernel": "grouped_ffn up/gate (E4M3 mma.sync, TMA bulk ring)", "bound": "hbm",
+                     "achieved": round(ach_upg, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(ach_upg / peak, 4), "peak_source": peak_kind,
+                     "bytes_per_launch": upg_bytes, "ms_per_launch": round(upg_ms, 4), "traffic": None},
+        "expert_matvec": {"kernels": "grouped up/gate + down", "bytes": pair_bytes,
+                          "ms": round(upg_ms + dn_ms, 4), "achieved_gbs": round(ach_pair, 1),
+                          "frac": round(ach_pair / peak, 4)},
+        "layer_hbm": {"bytes_per_rank": layer_bytes, "achieved_gbs": round(layer_bytes / (ms_step / 1e3) / 1e9, 1),
+                      "frac": round(layer_bytes / (ms_step / 1e3) / 1e9 / peak, 4)},
+        "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+        "e2e": {"value": round(T / (ms_e2e / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms_e2e, 4),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = cpu_reference_rate(args.cpu_sample_tokens, args.cpu_seconds)
+        except Exception as exc:  # the baseline is reported, never required
+            line["cpu_baseline"] = {"value": None, "error": f"{type(exc).__name__}: {exc}"}
+    if graph is not None:
+        del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+class CpuReferenceLayer:
+    """The reference CPU path for a sample of tokens: router (CPU restatement of
+    route_token_real), one batch-1 call of the reference node's OpenMP FP8 expert kernels
+    per (token, expert) and for the shared expert, fp32 combine (combine_outputs_torch)."""
+
+    def __init__(self, sample_tokens: int, threads: int):
+        import numpy as np
+        import torch
+
+        from constellation_b200 import synthetic
+        from oracle import refbuild
+
+        self.np = np
+        self.threads = threads
+        self.kind = "reference" if refbuild.ref_available() else "port"
+        self.refbuild = refbuild
+        torch.manual_seed(0)
+        gw, gb = synthetic.make_router(H, E, seed=7, device="cpu")
+        self.gw, self.gb = gw.numpy(), gb.numpy()
+        x = synthetic.make_activations(sample_tokens, H, seed=11, device="cpu")
+        self.x_bits = x.view(torch.int16).numpy().view(np.uint16)
+        self.x = x.float().numpy()
+        from oracle import router as orouter
+
+        self.orouter = orouter
+        r = orouter.route_batched(self.x, self.gw, self.gb, n_group=G, topk_group=TG, top_k=K)
+        need = sorted(set(int(e) for e in r.topk_idx.reshape(-1)))
+        self.experts = {}
+        for e in need + [-1]:
+            ex = synthetic.make_expert(H, I, seed=1000 + e if e >= 0 else 999, device="cpu")
+            self.experts[e] = refbuild.ExpertBytes(ex.w_up.numpy(), ex.s_up.numpy(), ex.w_gate.numpy(),
+                                                   ex.s_gate.numpy(), ex.w_down.numpy(), ex.s_down.numpy())
+        self.sample_tokens = sample_tokens
+
+    def run(self):
+        np = self.np
+        out = np.zeros((self.sample_tokens, H), np.float32)
+        for t in range(self.sample_tokens):
+            r = self.orouter.route_batched(self.x[t:t + 1], self.gw, self.gb, n_group=G, topk_group=TG, top_k=K)
+            acc = np.zeros(H, np.float32)
+            for e, w in zip(r.topk_idx[0], r.topk_weight[0]):
+                y = self._expert(int(e), self.x_bits[t:t + 1])
+                acc += np.float32(w) * y
+            acc += self._expert(-1, self.x_bits[t:t + 1])
+            out[t] = acc
+        return out
+
+    def _expert(self, e, xb):
+        """One batch-1 expert call on bf16 bits ``xb [1, H]`` -> fp32 ``[H]``."""
+        np = self.np
+        ex = self.experts[e]
+        if self.kind == "reference":
+            yb = self.refbuild.ref_expert_cpu(ex, xb, 2, 2, self.threads)  # bf16 in, bf16 out
+            return (yb[0].astype(np.uint32) << 16).view(np.float32)
+        xf = (xb[0].astype(np.uint32) << 16).view(np.float32)
+        _, y = self.refbuild.oracle_expert_lut(ex, xf[None])
+        return y[0]
+
+
+def cpu_reference_rate(sample_tokens: int, seconds: float):
+    threads = os.cpu_count() or 1
+    layer = CpuReferenceLayer(sample_tokens, threads)
+    layer.run()  # warm-up (page in the weights)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        layer.run()
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    tok_s = n * sample_tokens / dt
+    return {"value": round(tok_s, 3), "unit": "tokens/s", "cores": threads, "kind": layer.kind,
+            "sample": f"{sample_tokens} tokens of the T=64 batch through router + 8 routed + shared experts at "
+                      f"batch 1 per (token, expert), {n} repetitions, {dt:.1f} s",
+            "ms_per_token": round(dt / (n * sample_tokens) * 1e3, 2)}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    layer = CpuReferenceLayer(args.cpu_sample_tokens, threads)
+    for _ in range(max(1, args.warmup)):
+        layer.run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        layer.run()
+    dt = time.perf_counter() - t0
+    value = args.steps * args.cpu_sample_tokens / dt
+    ms = dt / args.steps * 1e3
+    line = {
+        "impl": "reference",
+        "metric": "MoE-layer decode tokens/s (1 DeepSeek-V3 MoE layer, T=64, 256 FP8 experts + shared)",
+        "value": round(value, 3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp32 (FP8 LUT decode x block scale)",
+        "data": "synthetic (seeded N(0,0.02) weights, 128x128 block E4M3; RMS-normalised N(0,1) bf16 hidden)",
+        "config": {"workload": "config2_decode_T64_one_layer", "tokens": args.tokens, "routed_experts": E,
+                   "shared_expert": True, "hidden": H, "inter": I, "top_k": K, "parallelism": "cpu",
+                   "sample_tokens_per_step": args.cpu_sample_tokens},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": layer.kind,
+                         "sample": f"{args.cpu_sample_tokens} tokens of the T={args.tokens} batch per step, batch 1 "
+                                   "per (token, expert) through the reference node's OpenMP FP8 CPU kernels"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -259,6 +259,51 @@ class ExpertContext:
                                               _stream(self.device)))
         return out
 
+    def shared_combine(self, x: torch.Tensor, *, extra: torch.Tensor | None = None,
+                       residual: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+        """``out = shared(x) + extra (+ residual)`` cast once (``cst_shared_combine``)."""
+        x = self._check_x(x)
+        T = x.shape[0]
+        if extra is not None:
+            if extra.dtype != torch.float32 or extra.shape != x.shape or extra.device != self.device:
+                raise RuntimeError("extra must be fp32 [T, hidden] on the context's device")
+            extra = extra.contiguous()
+        if residual is not None:
+            if residual.dtype != x.dtype or residual.shape != x.shape:
+                raise RuntimeError("residual must match hidden in shape and dtype")
+            residual = residual.contiguous()
+        if out is None:
+            out = torch.empty((T, self.cfg.hidden_size), dtype=out_dtype or x.dtype, device=self.device)
+        with torch.cuda.device(self.device):
+            check(_lib.lib.cst_shared_combine(self.handle, x.data_ptr(), dtype_code(x.dtype), T, _ptr(extra),
+                                              _ptr(residual), out.data_ptr(), dtype_code(out.dtype),
+                                              _stream(self.device)))
+        return out
+
+    def combine_rows(self, rows: torch.Tensor, tk_row: torch.Tensor, *, extra: torch.Tensor | None = None,
+                     residual: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+        """``out[t] = sum_k rows[tk_row[t, k]] (+ extra) (+ residual)`` (``cst_combine_rows``)."""
+        T, k1 = tk_row.shape
+        tk_row = tk_row.to(device=self.device, dtype=torch.int32).contiguous()
+        if rows.dtype != torch.float32 or rows.dim() != 2 or rows.shape[1] != self.cfg.hidden_size:
+            raise RuntimeError("rows must be fp32 [*, hidden]")
+        if rows.stride(1) != 1:
+            rows = rows.contiguous()
+        if extra is not None:
+            extra = extra.contiguous()
+        if residual is not None:
+            residual = residual.contiguous()
+        if out is None:
+            out = torch.empty((T, self.cfg.hidden_size), dtype=out_dtype, device=self.device)
+        with torch.cuda.device(self.device):
+            check(_lib.lib.cst_combine_rows(self.handle, rows.data_ptr(), rows.stride(0), tk_row.data_ptr(), k1, T,
+                                            _ptr(extra), _ptr(residual),
+                                            dtype_code(residual.dtype) if residual is not None else 0,
+                                            out.data_ptr(), dtype_code(out.dtype), _stream(self.device)))
+        return out
+
     def profile(self, enable: bool = True) -> None:
         """Record CUDA events at every stage boundary of the following calls."""
         check(_lib.lib.cst_profile_enable(self.handle, int(bool(enable))))

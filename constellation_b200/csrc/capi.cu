@@ -565,6 +565,58 @@ int cst_expert_forward(cst_ctx* c, int32_t expert_id, const void* x, int32_t in_
     return CST_OK;
 }
 
+int cst_shared_combine(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float* extra,
+                       const void* residual, void* out, int32_t out_dtype, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
+    if (T < 0 || T > c->max_rows || T > kMaxRowsModeRows) return fail(CST_ERR_INVALID_ARG, "T=%d out of range", T);
+    if (!x || !out) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (!aligned16(x) || !aligned16(out) || (extra && !aligned16(extra)) || (residual && !aligned16(residual)))
+        return fail(CST_ERR_INVALID_ARG, "x, extra, residual and out must be 16-byte aligned");
+    if (T == 0) return CST_OK;
+    if (int rc = ensure_device(c)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    prof_begin(c, s);
+    prof_fill_skipped(c, 0, s);
+    if (c->shared_slot >= 0) {
+        PackArgs pa{};
+        pa.row_slot = nullptr;
+        pa.single_slot = c->shared_slot;
+        pa.row_weight_in = nullptr;
+        pa.T = T;
+        pa.shared_slot = -1;
+        if (int rc = run_experts(c, pa, x, x_dtype, s)) return rc;
+    } else {
+        // no shared expert: only extra + residual; tk_row = -1 everywhere
+        CST_CUDA(cudaMemsetAsync(c->ws.tk_row, 0xff, size_t(T) * sizeof(int32_t), s));
+        prof_fill_skipped(c, 5, s);
+    }
+    CombineArgs ca{c->ws.y, c->cfg.hidden_dim, c->ws.tk_row, 1, T, c->cfg.hidden_dim, residual, x_dtype, out,
+                   out_dtype, extra};
+    CST_CUDA(launch_combine(ca, s));
+    prof_mark(c, 6, s);
+    return CST_OK;
+}
+
+int cst_combine_rows(cst_ctx* c, const float* rows, int64_t ld_rows, const int32_t* tk_row, int32_t k1, int32_t T,
+                     const float* extra, const void* residual, int32_t residual_dtype, void* out, int32_t out_dtype,
+                     void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (!valid_dtype(out_dtype) || (residual && !valid_dtype(residual_dtype)))
+        return fail(CST_ERR_INVALID_ARG, "bad dtype");
+    if (T < 0 || k1 < 0 || (k1 > 0 && (!rows || !tk_row)) || !out) return fail(CST_ERR_INVALID_ARG, "bad arguments");
+    if ((rows && (!aligned16(rows) || ld_rows % 4)) || !aligned16(out) || (extra && !aligned16(extra)) ||
+        (residual && !aligned16(residual)))
+        return fail(CST_ERR_INVALID_ARG, "rows, extra, residual and out must be 16-byte aligned");
+    if (T == 0) return CST_OK;
+    if (int rc = ensure_device(c)) return rc;
+    CombineArgs ca{rows, ld_rows, tk_row, k1, T, c->cfg.hidden_dim, residual, residual_dtype, out, out_dtype, extra};
+    CST_CUDA(launch_combine(ca, static_cast<cudaStream_t>(stream)));
+    return CST_OK;
+}
+
 int cst_device_error(cst_ctx* c) {
     g_last_error.clear();
     if (int rc = check_ctx(c)) return rc;

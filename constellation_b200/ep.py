@@ -1,0 +1,139 @@
+"""Expert parallelism for one MoE layer: one process per GPU, NCCL over NVLink/NVSwitch.
+
+Replaces the reference's socket dispatch -- one TCP ``InferRequest`` per (token, expert),
+run one after the other (``server/moe_layer_runtime.py:27-145``) -- with collectives
+between the ranks of one node.  Expert ``e`` lives on rank ``e // experts_per_rank``
+(contiguous blocks, the EP convention of the reference's patched HF model,
+``tmp/patched_modeling/modeling_deepseek_eager.py:648-649``); tokens are sharded across
+ranks; the router weights and the shared expert are replicated and every rank applies the
+shared expert to its own tokens.
+
+Two exchange strategies, both deterministic and both behind ``ExpertParallelMoE.forward``:
+
+``allgather`` (default for decode)
+    all-gather the tokens and their routes, run the rank's own experts on every row routed
+    to them (routes to other ranks' experts are skipped by the packer), reduce-scatter the
+    fp32 partial sums back to the owning ranks, add the shared expert.  Message sizes are
+    fixed, so nothing waits on the host.  At decode batch the bytes match the all-to-all
+    (T x H in, T x H x 4 back) because top_k equals the rank count at 8 GPUs.
+
+``alltoall`` (the NCCL all-to-all-v that BASELINE names)
+    exchange per-rank row counts (``all_to_all_single`` of ``world`` ints, the count step of
+    ``modeling_deepseek_eager.py:656``), send each routed row to the rank that owns its
+    expert (``:671-674``), run the grouped FFN on the received rows, send the weighted
+    outputs back (``:780-790``) and combine at the source in fixed k order.  The split
+    sizes must reach the host (NCCL takes host counts), which costs one device sync.
+
+The communication plan (``plan_dispatch``) is plain torch and runs on any device, so the
+multi-rank host logic is tested on CPU with the gloo backend.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class DispatchPlan:
+    order: torch.Tensor        # [Tl*K] flat (t, k) indices sorted by destination rank (stable)
+    dest: torch.Tensor         # [Tl*K] destination rank of each flat route
+    counts: torch.Tensor       # [world] rows sent to each rank
+    inv: torch.Tensor          # [Tl, K] position of route (t, k) in the send order
+
+
+def plan_dispatch(topk_idx: torch.Tensor, experts_per_rank: int, world: int) -> DispatchPlan:
+    Tl, K = topk_idx.shape
+    flat = topk_idx.reshape(-1).to(torch.int64)
+    dest = torch.div(flat, experts_per_rank, rounding_mode="floor")
+    order = torch.sort(dest * (Tl * K) + torch.arange(Tl * K, device=flat.device)).indices
+    counts = torch.bincount(dest, minlength=world)[:world]
+    inv = torch.empty_like(order)
+    inv[order] = torch.arange(Tl * K, device=flat.device)
+    return DispatchPlan(order=order, dest=dest, counts=counts, inv=inv.reshape(Tl, K))
+
+
+class ExpertParallelMoE:
+    """One MoE layer sharded over ``world`` ranks.
+
+    ``compute`` is the rank's ``ExpertContext`` holding its ``experts_per_rank`` routed
+    experts (router ids ``[rank * epr, (rank + 1) * epr)``) and the shared expert.
+    """
+
+    def __init__(self, compute, *, rank: int, world: int, n_routed_experts: int, group=None,
+                 mode: str = "allgather"):
+        if n_routed_experts % world:
+            raise ValueError(f"{n_routed_experts} experts do not shard over {world} ranks")
+        if mode not in ("allgather", "alltoall"):
+            raise ValueError(f"unknown EP mode {mode!r}")
+        self.c = compute
+        self.rank, self.world, self.group, self.mode = rank, world, group, mode
+        self.E = n_routed_experts
+        self.epr = n_routed_experts // world
+        self._slot_map = None
+
+    # ------------------------------------------------------------------------------
+    def slot_map(self, device) -> torch.Tensor:
+        """Router expert id -> local arena slot (-1 elsewhere), on ``device``."""
+        if self._slot_map is None:
+            m = [self.c.find_slot(e) for e in range(self.E)]
+            self._slot_map = torch.tensor(m, dtype=torch.int32, device=device)
+        return self._slot_map
+
+    def forward(self, x_local: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor, *,
+                residual: torch.Tensor | None = None, resident: torch.Tensor | None = None,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        topk_idx, topk_w = self.c.route(x_local, gate_weight, bias, resident=resident)
+        if self.world == 1:
+            part = self.c.moe_routed(x_local, topk_idx, topk_w, add_shared=False, out_dtype=torch.float32)
+            return self.c.shared_combine(x_local, extra=part, residual=residual, out_dtype=out_dtype)
+        if self.mode == "allgather":
+            part = self._routed_allgather(x_local, topk_idx, topk_w)
+        else:
+            part = self._routed_alltoall(x_local, topk_idx, topk_w)
+        return self.c.shared_combine(x_local, extra=part, residual=residual, out_dtype=out_dtype)
+
+    # ------------------------------------------------------------------------------
+    def _routed_allgather(self, x_local, topk_idx, topk_w) -> torch.Tensor:
+        Tl, K = topk_idx.shape
+        H = x_local.shape[1]
+        x_all = torch.empty((self.world * Tl, H), dtype=x_local.dtype, device=x_local.device)
+        dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
+        meta = torch.cat([topk_idx.to(torch.int32), topk_w.view(torch.int32)], dim=1).contiguous()
+        meta_all = torch.empty((self.world * Tl, 2 * K), dtype=torch.int32, device=x_local.device)
+        dist.all_gather_into_tensor(meta_all, meta, group=self.group)
+        idx_all = meta_all[:, :K].contiguous()
+        w_all = meta_all[:, K:].contiguous().view(torch.float32)
+        partial = self.c.moe_routed(x_all, idx_all, w_all, add_shared=False, out_dtype=torch.float32)
+        mine = torch.empty((Tl, H), dtype=torch.float32, device=x_local.device)
+        dist.reduce_scatter_tensor(mine, partial, op=dist.ReduceOp.SUM, group=self.group)
+        return mine
+
+    def _routed_alltoall(self, x_local, topk_idx, topk_w) -> torch.Tensor:
+        Tl, K = topk_idx.shape
+        H = x_local.shape[1]
+        dev = x_local.device
+        plan = plan_dispatch(topk_idx, self.epr, self.world)
+        counts_recv = torch.empty_like(plan.counts)
+        dist.all_to_all_single(counts_recv, plan.counts, group=self.group)
+        send_sizes = plan.counts.tolist()
+        recv_sizes = counts_recv.tolist()
+        n_recv = int(sum(recv_sizes))
+        tok = torch.div(plan.order, K, rounding_mode="floor")
+        x_send = x_local.index_select(0, tok)
+        meta_send = torch.stack([topk_idx.reshape(-1)[plan.order].to(torch.int32),
+                                 topk_w.reshape(-1)[plan.order].view(torch.int32)], dim=1).contiguous()
+        x_recv = torch.empty((n_recv, H), dtype=x_local.dtype, device=dev)
+        meta_recv = torch.empty((n_recv, 2), dtype=torch.int32, device=dev)
+        dist.all_to_all_single(x_recv, x_send, recv_sizes, send_sizes, group=self.group)
+        dist.all_to_all_single(meta_recv, meta_send, recv_sizes, send_sizes, group=self.group)
+        if n_recv:
+            slot = self.slot_map(dev)[meta_recv[:, 0].to(torch.int64)]
+            y_recv = self.c.grouped_ffn(x_recv, slot, meta_recv[:, 1].contiguous().view(torch.float32),
+                                        out_dtype=torch.float32)
+        else:
+            y_recv = torch.empty((0, H), dtype=torch.float32, device=dev)
+        y_back = torch.empty((Tl * K, H), dtype=torch.float32, device=dev)
+        dist.all_to_all_single(y_back, y_recv, send_sizes, recv_sizes, group=self.group)
+        return self.c.combine_rows(y_back, plan.inv, out_dtype=torch.float32)

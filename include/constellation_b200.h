@@ -157,6 +157,23 @@ int cst_grouped_ffn(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t R, con
 int cst_expert_forward(cst_ctx* ctx, int32_t expert_id, const void* x, int32_t in_dtype, int32_t batch,
                        void* y, int32_t out_dtype, void* stream);
 
+/* out[t] = SharedExpert(x[t]) + extra[t] (+ residual[t]), one final cast, for T rows.
+ * The last step of an expert-parallel layer: `extra` ([T, hidden] fp32, or NULL) is the
+ * routed sum that came back from the other ranks; the shared expert is applied to the
+ * rank's own tokens (run_shared_expert_block, server/deepseek_full_model_executor.py:264-316,
+ * and the sums of server/full_model_runtime.py:348-355).  Without a resident shared
+ * expert only extra + residual is written. */
+int cst_shared_combine(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, const float* extra,
+                       const void* residual, void* out, int32_t out_dtype, void* stream);
+
+/* out[t] = sum_{k < k1, tk_row[t,k] >= 0} rows[tk_row[t,k]] (+ extra[t]) (+ residual[t]), fp32
+ * sums in k order, one final cast: the source-side combine of an all-to-all return
+ * (combine_outputs_torch, server/moe_layer_runtime.py:148-167, over rows that already
+ * carry their routing weight).  rows: [*, hidden] fp32 with row stride ld_rows. */
+int cst_combine_rows(cst_ctx* ctx, const float* rows, int64_t ld_rows, const int32_t* tk_row, int32_t k1,
+                     int32_t T, const float* extra, const void* residual, int32_t residual_dtype, void* out,
+                     int32_t out_dtype, void* stream);
+
 /* Synchronises the context's device, then returns CST_OK or CST_ERR_DEVICE_TIMEOUT if a
  * kernel's bounded wait gave up since the last call (and clears the flag). */
 int cst_device_error(cst_ctx* ctx);
