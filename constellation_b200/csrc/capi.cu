@@ -617,6 +617,19 @@ int cst_combine_rows(cst_ctx* c, const float* rows, int64_t ld_rows, const int32
     return CST_OK;
 }
 
+int cst_dequant_fp8(const uint8_t* w, const float* scale_inv, int32_t rows, int32_t cols, int32_t block, float* out,
+                    void* stream) {
+    g_last_error.clear();
+    if (!w || !scale_inv || !out) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (rows <= 0 || cols <= 0 || block <= 0) return fail(CST_ERR_INVALID_ARG, "bad shape (%d, %d, %d)", rows, cols, block);
+    if (!aligned16(w) || !aligned16(out)) return fail(CST_ERR_INVALID_ARG, "w and out must be 16-byte aligned");
+    int dev = 0, sms = 0;
+    CST_CUDA(cudaGetDevice(&dev));
+    CST_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    CST_CUDA(launch_dequant_fp8(w, scale_inv, out, rows, cols, block, sms, static_cast<cudaStream_t>(stream)));
+    return CST_OK;
+}
+
 int cst_device_error(cst_ctx* c) {
     g_last_error.clear();
     if (int rc = check_ctx(c)) return rc;

@@ -13,6 +13,10 @@ namespace cst {
 cudaError_t launch_relayout(const uint8_t* wu, const uint8_t* wg, const uint8_t* wd, uint8_t* slot,
                             int inter, int hidden, int num_sms, cudaStream_t stream);
 
+// dequant.cu
+cudaError_t launch_dequant_fp8(const uint8_t* w, const float* s, float* out, int rows, int cols, int block,
+                               int num_sms, cudaStream_t stream);
+
 // router.cu
 int router_k_split(int H);
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,

@@ -174,6 +174,13 @@ int cst_combine_rows(cst_ctx* ctx, const float* rows, int64_t ld_rows, const int
                      int32_t T, const float* extra, const void* residual, int32_t residual_dtype, void* out,
                      int32_t out_dtype, void* stream);
 
+/* out[r, c] = float8_e4m3fn(w[r, c]) * scale_inv[r / block, c / block] on the current device:
+ * dequant_fp8_weight_blockwise (server/fp8_utils.py:4-39), bit-identical (true e4m3fn
+ * decode, 0x7F/0xFF -> NaN; ceil-div block grid for ragged shapes; one fp32 multiply).
+ * w [rows, cols] uint8, scale_inv [ceil(rows/block), ceil(cols/block)] fp32, out fp32. */
+int cst_dequant_fp8(const uint8_t* w, const float* scale_inv, int32_t rows, int32_t cols, int32_t block,
+                    float* out, void* stream);
+
 /* Synchronises the context's device, then returns CST_OK or CST_ERR_DEVICE_TIMEOUT if a
  * kernel's bounded wait gave up since the last call (and clears the flag). */
 int cst_device_error(cst_ctx* ctx);

@@ -1,0 +1,144 @@
+"""Expert-parallel host logic on CPU: 2 gloo ranks, both exchange strategies.
+
+The compute side is a stand-in backed by the CPU oracle (the CUDA kernels need a GPU);
+what is tested here is the product's communication plan, permutations, collectives and
+combine order in ``constellation_b200.ep``.  The result must equal the single-process
+oracle layer over the whole batch.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from constellation_b200.ep import ExpertParallelMoE, plan_dispatch
+
+E, H, I, G, TG, K = 16, 256, 128, 4, 2, 4
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+class OracleCompute:
+    """CPU stand-in for ExpertContext holding experts [lo, hi) + the shared expert."""
+
+    def __init__(self, lo, hi, experts, shared):
+        from oracle.expert import DequantExpert
+
+        self.lo, self.hi = lo, hi
+        self.ex = {e: DequantExpert(experts[e]) for e in range(lo, hi)}
+        self.shared = DequantExpert(shared)
+
+    def find_slot(self, e):
+        return e - self.lo if self.lo <= e < self.hi else -1
+
+    def route(self, x, gw, gb, resident=None):
+        from oracle.router import route_batched
+
+        r = route_batched(x.float().numpy(), gw.numpy(), gb.numpy(), n_group=G, topk_group=TG, top_k=K)
+        return torch.from_numpy(r.topk_idx.astype(np.int32)), torch.from_numpy(r.topk_weight)
+
+    def moe_routed(self, x, idx, w, add_shared=False, out_dtype=torch.float32):
+        xf = x.float().numpy()
+        out = np.zeros((x.shape[0], H), np.float32)
+        for t in range(x.shape[0]):
+            for k in range(idx.shape[1]):
+                e = int(idx[t, k])
+                if self.lo <= e < self.hi:
+                    out[t] += np.float32(w[t, k]) * self.ex[e].forward(xf[t:t + 1])[0]
+        return torch.from_numpy(out).to(out_dtype)
+
+    def grouped_ffn(self, x, slot, w, out_dtype=torch.float32):
+        xf = x.float().numpy()
+        out = np.zeros((x.shape[0], H), np.float32)
+        for r in range(x.shape[0]):
+            out[r] = np.float32(w[r]) * self.ex[int(slot[r]) + self.lo].forward(xf[r:r + 1])[0]
+        return torch.from_numpy(out)
+
+    def combine_rows(self, rows, tk_row, out_dtype=torch.float32):
+        out = torch.zeros((tk_row.shape[0], H), dtype=torch.float32)
+        for t in range(tk_row.shape[0]):
+            for k in range(tk_row.shape[1]):
+                if int(tk_row[t, k]) >= 0:
+                    out[t] += rows[int(tk_row[t, k])]
+        return out.to(out_dtype)
+
+    def shared_combine(self, x, extra=None, residual=None, out_dtype=None):
+        y = torch.from_numpy(self.shared.forward(x.float().numpy()))
+        if extra is not None:
+            y = y + extra
+        if residual is not None:
+            y = y + residual.float()
+        return y.to(out_dtype or torch.float32)
+
+
+def _worker(rank, world, port, mode, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import cases
+
+        T = 8
+        x = torch.from_numpy(cases.activations(61, T, H))
+        gw, gb = (torch.from_numpy(a) for a in cases.router(61, E, H, bias_std=0.05))
+        experts = {e: cases.expert(2000 + e, H, I) for e in range(E)}
+        shared = cases.expert(2999, H, I)
+        epr = E // world
+        comp = OracleCompute(rank * epr, (rank + 1) * epr, experts, shared)
+        moe = ExpertParallelMoE(comp, rank=rank, world=world, n_routed_experts=E, mode=mode)
+        Tl = T // world
+        out = moe.forward(x[rank * Tl:(rank + 1) * Tl].to(torch.bfloat16), gw, gb, out_dtype=torch.float32)
+        q.put((rank, out.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["allgather", "alltoall"])
+def test_ep_two_ranks_matches_single_process_oracle(mode):
+    from oracle import cases
+    from oracle.expert import DequantExpert
+    from oracle.layer import moe_layer
+
+    world, T = 2, 8
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    out = np.concatenate([got[r] for r in range(world)])
+    x = cases.activations(61, T, H)
+    gw, gb = cases.router(61, E, H, bias_std=0.05)
+    ref = moe_layer(x, gw, gb, {e: DequantExpert(cases.expert(2000 + e, H, I)) for e in range(E)},
+                    DequantExpert(cases.expert(2999, H, I)), n_group=G, topk_group=TG, top_k=K)
+    np.testing.assert_allclose(out, ref.out_f32, rtol=1e-5, atol=1e-5 * np.abs(ref.out_f32).max())
+
+
+def test_plan_dispatch_orders_by_owner_and_inverts():
+    idx = torch.tensor([[5, 0, 12], [3, 9, 15], [8, 1, 4]])
+    p = plan_dispatch(idx, experts_per_rank=4, world=4)
+    # owners of [5, 0, 12, 3, 9, 15, 8, 1, 4] with 4 experts per rank: [1, 0, 3, 0, 2, 3, 2, 0, 1]
+    assert p.counts.tolist() == [3, 2, 2, 2]
+    dest_sorted = p.dest[p.order].tolist()
+    assert dest_sorted == sorted(dest_sorted)
+    # stable: within a destination, original (t, k) order is kept
+    assert p.order.tolist() == [1, 3, 7, 0, 8, 4, 6, 2, 5]
+    flat = idx.reshape(-1)
+    assert torch.equal(flat[p.order][p.inv.reshape(-1)], flat)
+
+
+def test_ep_rejects_uneven_sharding():
+    with pytest.raises(ValueError):
+        ExpertParallelMoE(object(), rank=0, world=3, n_routed_experts=16)
