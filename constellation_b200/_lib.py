@@ -32,6 +32,7 @@ EXPORTED = (
     "cst_set_shared_slot", "cst_route", "cst_moe_routed", "cst_moe_layer", "cst_grouped_ffn",
     "cst_expert_forward", "cst_device_error", "cst_ctx_info", "cst_last_error", "cst_abi_version",
     "cst_profile_enable", "cst_profile_read", "cst_shared_combine", "cst_combine_rows", "cst_dequant_fp8",
+    "cst_route_noalloc",
 )
 CST_N_STAGES = 7
 STAGE_NAMES = ("router", "route_pack", "pack_x", "grouped_up_gate", "pack_h", "grouped_down", "combine")
@@ -99,6 +100,7 @@ def _load() -> ctypes.CDLL:
         "cst_last_error": (ctypes.c_char_p, []),
         "cst_shared_combine": (ctypes.c_int, [P, P, I32, I32, P, P, P, I32, P]),
         "cst_dequant_fp8": (ctypes.c_int, [P, P, I32, I32, I32, P, P]),
+        "cst_route_noalloc": (ctypes.c_int, [P, I32, I32, I32, P, P, P, I32, I32, I32, I32, I32, F, P, P, P]),
         "cst_combine_rows": (ctypes.c_int, [P, P, ctypes.c_int64, P, I32, I32, P, P, I32, P, I32, P]),
         "cst_profile_enable": (ctypes.c_int, [P, I32]),
         "cst_profile_read": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_float), I32]),

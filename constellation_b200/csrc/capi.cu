@@ -37,7 +37,24 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
-#define CST_CUDA(call)                                                                         \
+}  // namespace
+
+namespace cst {
+void clear_last_error() { g_last_error.clear(); }
+int set_last_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+}  // namespace cst
+
+namespace {
+
+#define CST_CUDA(call)                                                                      \
     do {                                                                                       \
         cudaError_t e_ = (call);                                                               \
         if (e_ != cudaSuccess)                                                                 \

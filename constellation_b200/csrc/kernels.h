@@ -9,6 +9,10 @@
 
 namespace cst {
 
+// capi.cu: the thread's cst_last_error() message, for entry points in other files
+void clear_last_error();
+int set_last_error(int code, const char* fmt, ...);
+
 // relayout.cu
 cudaError_t launch_relayout(const uint8_t* wu, const uint8_t* wg, const uint8_t* wd, uint8_t* slot,
                             int inter, int hidden, int num_sms, cudaStream_t stream);

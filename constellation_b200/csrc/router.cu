@@ -22,6 +22,7 @@
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <mutex>
 
 #include "cst_common.cuh"
 #include "kernels.h"
@@ -238,4 +239,75 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------
+// Router without any allocation (cst_route_noalloc).
+//
+// Some callers of this library cannot call cudaMalloc: a host runtime that has handed all
+// device memory to its own pool before loading the library, code that runs while another
+// component owns the allocator, or a process that must not grow its footprint after
+// start-up.  They still need the router, whose logits kernel writes its K-split partial
+// sums ([kz, T, E] fp32) to global scratch that cst_create would otherwise allocate.
+// This variant keeps that scratch in the file-scope array below instead.  The array is
+// part of the library image: every GPU that loads the library holds it (2 MiB) until the
+// process exits.  Host code cannot use the array's name as a device address, so the first
+// call on each device looks the address up with cudaGetSymbolAddress (with that device
+// current) and caches it; that first call should therefore come before any stream
+// capture.  Every call overwrites every scratch element it later reads, so nothing needs
+// clearing between calls -- but all calls share the one array: calls that overlap on the
+// GPU (other streams, other threads, concurrent graph replays) race on it.
+constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 19;  // 2 MiB
+static __device__ __align__(256) float g_router_noalloc_scratch[kNoAllocScratchFloats];
+
+namespace {
+constexpr int kMaxDevices = 64;
+float* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+}  // namespace
+
 }  // namespace cst
+
+extern "C" int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int32_t hidden, const float* gate_weight,
+                                 const float* bias, const uint8_t* resident, int32_t n_experts, int32_t n_group,
+                                 int32_t topk_group, int32_t top_k, int32_t norm_topk_prob,
+                                 float routed_scaling_factor, int32_t* topk_idx, float* topk_weight, void* stream) {
+    using namespace cst;
+    clear_last_error();
+    if (x_dtype < 1 || x_dtype > 3) return set_last_error(3, "bad x_dtype %d", x_dtype);
+    if (!x || !gate_weight || !bias || !topk_idx || !topk_weight) return set_last_error(3, "null pointer");
+    if (hidden <= 0 || hidden % 128) return set_last_error(3, "hidden=%d must be a positive multiple of 128", hidden);
+    if (n_experts <= 0 || n_experts > 1024) return set_last_error(3, "n_experts=%d out of [1, 1024]", n_experts);
+    if (n_group <= 0 || n_group > 32 || n_experts % n_group)
+        return set_last_error(3, "invalid n_group=%d for n_experts=%d", n_group, n_experts);
+    if (topk_group <= 0 || topk_group > n_group) return set_last_error(3, "invalid topk_group=%d", topk_group);
+    if (top_k <= 0 || top_k > 15 || top_k > n_experts) return set_last_error(3, "invalid top_k=%d", top_k);
+    if (T < 0) return set_last_error(3, "T=%d < 0", T);
+    const int kz = router_k_split(hidden);
+    const int64_t need = int64_t(kz) * T * n_experts;
+    if (need > kNoAllocScratchFloats)
+        return set_last_error(3,
+                              "cst_route_noalloc: T * n_experts * %d = %lld scratch floats exceed the static "
+                              "maximum of %lld (T <= %lld for n_experts = %d); use cst_route",
+                              kz, static_cast<long long>(need), static_cast<long long>(kNoAllocScratchFloats),
+                              static_cast<long long>(kNoAllocScratchFloats / (int64_t(kz) * n_experts)), n_experts);
+    if (T == 0) return 0;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return set_last_error(5, "cudaGetDevice failed or device id out of range");
+    float* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (g_noalloc_ptr[dev] == nullptr) {
+            void* p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_router_noalloc_scratch);
+            if (e != cudaSuccess || p == nullptr)
+                return set_last_error(5, "cudaGetSymbolAddress(router scratch) failed: %s", cudaGetErrorString(e));
+            g_noalloc_ptr[dev] = static_cast<float*>(p);
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    const cudaError_t e = launch_router(x, x_dtype, gate_weight, bias, resident, T, n_experts, hidden, n_group,
+                                        topk_group, top_k, norm_topk_prob, routed_scaling_factor, scratch, topk_idx,
+                                        topk_weight, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return set_last_error(5, "router launch failed: %s", cudaGetErrorString(e));
+    return 0;
+}

@@ -124,6 +124,25 @@ int cst_route(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, const flo
               const float* bias, const uint8_t* resident, int32_t top_k, int32_t* topk_idx,
               float* topk_weight, float* logits, float* group_scores, void* stream);
 
+/* cst_route without a context and without any allocation.  It has no counterpart in the
+ * reference; it exists for callers that cannot call cudaMalloc -- a host runtime that has
+ * already handed the device memory to its own pool, code running while another component
+ * owns the allocator, or a process that must not grow after start-up -- and therefore
+ * cannot create a context.  The caller passes every input and output (device pointers,
+ * same meaning as cst_route plus the router hyper-parameters); the router's scratch (its
+ * K-split partial logits) lives in a 2 MiB static device array inside this library,
+ * which every GPU that loads the library holds until the process exits.  Limit:
+ * kz * T * n_experts <= 524288 floats, where kz = 8 for hidden = 7168 -- T <= 256 at 256
+ * experts; larger calls return CST_ERR_INVALID_ARG with a message naming the limit.
+ * The first call on a device looks the array's device address up (cudaGetSymbolAddress
+ * with that device current) and caches it, so make that first call before any stream
+ * capture.  All calls share the one array: calls that overlap on the GPU (other streams,
+ * threads or graph replays) race on it.  Results equal cst_route's. */
+int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int32_t hidden, const float* gate_weight,
+                      const float* bias, const uint8_t* resident, int32_t n_experts, int32_t n_group,
+                      int32_t topk_group, int32_t top_k, int32_t norm_topk_prob, float routed_scaling_factor,
+                      int32_t* topk_idx, float* topk_weight, void* stream);
+
 /* Routed experts for given routes + fp32 combine (+ shared expert when flags has
  * CST_FLAG_ADD_SHARED): run_topk_moe_layer / dispatch_topk_experts / combine_outputs_torch
  * (server/moe_layer_runtime.py:111-229) for a batch.  Routes to experts that are not
