@@ -180,7 +180,8 @@ def run_ours(args):
         else:
             out.copy_(moe.forward(x, gw, gb))
 
-    use_graph = (not args.no_graph) and world == 1
+    # the all-to-all-v exchange reads split sizes on the host, so it cannot be captured
+    use_graph = (not args.no_graph) and (world == 1 or args.ep_mode == "allgather")
     graph = None
     for _ in range(max(3, args.warmup)):
         step()
@@ -191,13 +192,17 @@ def run_ours(args):
         with torch.cuda.stream(s):
             step()
         torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step()
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize(dev)
-    launches_per_step = 8 if world == 1 else 16
+    # kernels of this library per layer (NCCL and torch copy kernels not counted)
+    launches_per_step = 8 if world == 1 else 9
 
     def timed(fn, k):
         if world > 1:
@@ -321,12 +326,14 @@ def run_ours(args):
         except Exception as exc:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": f"{type(exc).__name__}: {exc}"}
     if graph is not None:
+        torch.cuda.synchronize(dev)
+        graph.reset()  # release the captured NCCL work before the process group goes away
         del graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 # ---------------------------------------------------------------------------------------
@@ -445,11 +452,25 @@ def run_reference(args):
                                    "per (token, expert) through the reference node's OpenMP FP8 CPU kernels"},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_RESULT_FD = None
+
+
+def emit(line: dict) -> None:
+    """Write the one JSON result line to the original stdout."""
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(line) + "\n").encode())
 
 
 def main():
+    global _RESULT_FD
     args = parse()
+    # Libraries (NCCL's banner, CUDA) may print to the C-level stdout; send all of that to
+    # stderr so stdout carries only the result line.
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
     else:

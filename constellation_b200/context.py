@@ -154,6 +154,13 @@ class ExpertContext:
     def find_slot(self, expert_id: int) -> int:
         return int(_lib.lib.cst_find_slot(self.handle, int(expert_id)))
 
+    def find_shared_slot(self) -> int:
+        """Arena slot of the shared expert (raises when none is resident)."""
+        s = int(self.info().get("shared_slot", -1))
+        if s < 0:
+            raise RuntimeError("no shared expert is resident in this context")
+        return s
+
     def set_shared_slot(self, slot: int) -> None:
         check(_lib.lib.cst_set_shared_slot(self.handle, int(slot)))
 
@@ -202,6 +209,33 @@ class ExpertContext:
             check(_lib.lib.cst_moe_routed(self.handle, x.data_ptr(), dtype_code(x.dtype), T, topk_idx.data_ptr(),
                                           topk_weight.data_ptr(), int(topk_idx.shape[1]), flags, out.data_ptr(),
                                           dtype_code(out.dtype), _stream(self.device)))
+        return out
+
+    def moe_routed_range(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tensor,
+                         shared_begin: int, shared_end: int, *, out_dtype: torch.dtype = torch.float32,
+                         out: torch.Tensor | None = None):
+        """Routed rows of every token + the shared expert on tokens [begin, end) (EP form)."""
+        x = self._check_x(x)
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty((T, self.cfg.hidden_size), dtype=out_dtype, device=self.device)
+        with torch.cuda.device(self.device):
+            check(_lib.lib.cst_moe_routed_range(self.handle, x.data_ptr(), dtype_code(x.dtype), T, topk_idx.data_ptr(),
+                                                topk_weight.data_ptr(), int(topk_idx.shape[1]), int(shared_begin),
+                                                int(shared_end), out.data_ptr(), dtype_code(out.dtype),
+                                                _stream(self.device)))
+        return out
+
+    def cast_extra(self, extra: torch.Tensor, *, residual: torch.Tensor | None = None,
+                   out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+        """``out = extra (+ residual)`` cast once (``cst_combine_rows`` with no rows)."""
+        T = extra.shape[0]
+        if out is None:
+            out = torch.empty((T, self.cfg.hidden_size), dtype=out_dtype, device=self.device)
+        with torch.cuda.device(self.device):
+            check(_lib.lib.cst_combine_rows(self.handle, None, 0, None, 0, T, extra.data_ptr(), _ptr(residual),
+                                            dtype_code(residual.dtype) if residual is not None else 0,
+                                            out.data_ptr(), dtype_code(out.dtype), _stream(self.device)))
         return out
 
     def moe_layer(self, x: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor, *,

@@ -454,9 +454,10 @@ int cst_route(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float
 
 static int moe_routed_impl(cst_ctx* c, const void* x, int x_dtype, int T, const int32_t* topk_idx,
                            const float* topk_w, int K, uint32_t flags, const void* residual, void* out,
-                           int out_dtype, cudaStream_t s) {
+                           int out_dtype, cudaStream_t s, int shared_begin = 0, int shared_end = -1) {
     const bool shared = (flags & CST_FLAG_ADD_SHARED) != 0;
     if (shared && c->shared_slot < 0) return fail(CST_ERR_NOT_RESIDENT, "no shared expert is resident");
+    if (shared_end < 0) shared_end = T;
     if (int64_t(T) * (K + 1) > c->max_rows)
         return fail(CST_ERR_INVALID_ARG, "T*(top_k+1)=%d exceeds the workspace (%d rows)", T * (K + 1), c->max_rows);
     PackArgs pa{};
@@ -466,6 +467,8 @@ static int moe_routed_impl(cst_ctx* c, const void* x, int x_dtype, int T, const 
     pa.E = c->cfg.n_routed_experts;
     pa.K = K;
     pa.shared_slot = shared ? c->shared_slot : -1;
+    pa.shared_t_begin = shared_begin;
+    pa.shared_t_end = shared_end;
     pa.row_slot = nullptr;
     pa.single_slot = -1;
     pa.row_weight_in = nullptr;
@@ -494,6 +497,28 @@ int cst_moe_routed(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const 
     prof_fill_skipped(c, 0, static_cast<cudaStream_t>(stream));
     return moe_routed_impl(c, x, x_dtype, T, topk_idx, topk_weight, top_k, flags, nullptr, out, out_dtype,
                            static_cast<cudaStream_t>(stream));
+}
+
+int cst_moe_routed_range(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const int32_t* topk_idx,
+                         const float* topk_weight, int32_t top_k, int32_t shared_begin, int32_t shared_end,
+                         void* out, int32_t out_dtype, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
+    if (T < 0 || T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d out of range", T);
+    if (top_k <= 0 || top_k > 15) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of range", top_k);
+    if (shared_begin < 0 || shared_end < shared_begin || shared_end > T)
+        return fail(CST_ERR_INVALID_ARG, "shared token range [%d, %d) outside [0, %d)", shared_begin, shared_end, T);
+    if (!x || !out || !topk_idx || !topk_weight) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (!aligned16(x) || !aligned16(out)) return fail(CST_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+    if (T == 0) return CST_OK;
+    if (int rc = ensure_device(c)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    prof_begin(c, s);
+    prof_fill_skipped(c, 0, s);
+    const uint32_t flags = shared_end > shared_begin ? CST_FLAG_ADD_SHARED : 0u;
+    return moe_routed_impl(c, x, x_dtype, T, topk_idx, topk_weight, top_k, flags, nullptr, out, out_dtype, s,
+                           shared_begin, shared_end);
 }
 
 int cst_moe_layer(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float* gate_weight, const float* bias,

@@ -37,6 +37,7 @@ struct PackArgs {
     int E;
     int K;
     int shared_slot;  // -1: none
+    int shared_t_begin, shared_t_end;  // tokens [begin, end) get a shared-expert row
     // mode B (rows): row_slot [T] (one route per row, weight row_weight or 1), or every
     // row to `single_slot` when row_slot is null and single_slot >= 0
     const int32_t* row_slot;

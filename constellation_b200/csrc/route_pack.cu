@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, in
                     const int e = a.topk_idx[t * a.K + k];
                     slot = (e >= 0 && e < a.E) ? a.slot_of_expert[e] : -1;
                 } else {
-                    slot = a.shared_slot;
+                    slot = (t >= a.shared_t_begin && t < a.shared_t_end) ? a.shared_slot : -1;
                 }
             }
             if (slot >= 0 && slot < a.n_slots)

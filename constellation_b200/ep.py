@@ -85,17 +85,19 @@ class ExpertParallelMoE:
                 residual: torch.Tensor | None = None, resident: torch.Tensor | None = None,
                 out_dtype: torch.dtype | None = None) -> torch.Tensor:
         topk_idx, topk_w = self.c.route(x_local, gate_weight, bias, resident=resident)
+        od = out_dtype or x_local.dtype
+        Tl = x_local.shape[0]
         if self.world == 1:
-            part = self.c.moe_routed(x_local, topk_idx, topk_w, add_shared=False, out_dtype=torch.float32)
-            return self.c.shared_combine(x_local, extra=part, residual=residual, out_dtype=out_dtype)
+            if residual is None:
+                return self.c.moe_routed_range(x_local, topk_idx, topk_w, 0, Tl, out_dtype=od)
+            part = self.c.moe_routed_range(x_local, topk_idx, topk_w, 0, Tl, out_dtype=torch.float32)
+            return self.c.cast_extra(part, residual=residual, out_dtype=od)
         if self.mode == "allgather":
-            part = self._routed_allgather(x_local, topk_idx, topk_w)
-        else:
-            part = self._routed_alltoall(x_local, topk_idx, topk_w)
-        return self.c.shared_combine(x_local, extra=part, residual=residual, out_dtype=out_dtype)
+            return self._allgather(x_local, topk_idx, topk_w, residual, od)
+        return self._alltoall(x_local, topk_idx, topk_w, residual, od)
 
     # ------------------------------------------------------------------------------
-    def _routed_allgather(self, x_local, topk_idx, topk_w) -> torch.Tensor:
+    def _allgather(self, x_local, topk_idx, topk_w, residual, od) -> torch.Tensor:
         Tl, K = topk_idx.shape
         H = x_local.shape[1]
         x_all = torch.empty((self.world * Tl, H), dtype=x_local.dtype, device=x_local.device)
@@ -105,12 +107,14 @@ class ExpertParallelMoE:
         dist.all_gather_into_tensor(meta_all, meta, group=self.group)
         idx_all = meta_all[:, :K].contiguous()
         w_all = meta_all[:, K:].contiguous().view(torch.float32)
-        partial = self.c.moe_routed(x_all, idx_all, w_all, add_shared=False, out_dtype=torch.float32)
+        # this rank's experts on every gathered row, the shared expert on its own tokens only
+        lo = self.rank * Tl
+        partial = self.c.moe_routed_range(x_all, idx_all, w_all, lo, lo + Tl, out_dtype=torch.float32)
         mine = torch.empty((Tl, H), dtype=torch.float32, device=x_local.device)
         dist.reduce_scatter_tensor(mine, partial, op=dist.ReduceOp.SUM, group=self.group)
-        return mine
+        return self.c.cast_extra(mine, residual=residual, out_dtype=od)
 
-    def _routed_alltoall(self, x_local, topk_idx, topk_w) -> torch.Tensor:
+    def _alltoall(self, x_local, topk_idx, topk_w, residual, od) -> torch.Tensor:
         Tl, K = topk_idx.shape
         H = x_local.shape[1]
         dev = x_local.device
@@ -124,16 +128,19 @@ class ExpertParallelMoE:
         x_send = x_local.index_select(0, tok)
         meta_send = torch.stack([topk_idx.reshape(-1)[plan.order].to(torch.int32),
                                  topk_w.reshape(-1)[plan.order].view(torch.int32)], dim=1).contiguous()
-        x_recv = torch.empty((n_recv, H), dtype=x_local.dtype, device=dev)
+        x_recv = torch.empty((n_recv + Tl, H), dtype=x_local.dtype, device=dev)
         meta_recv = torch.empty((n_recv, 2), dtype=torch.int32, device=dev)
-        dist.all_to_all_single(x_recv, x_send, recv_sizes, send_sizes, group=self.group)
+        dist.all_to_all_single(x_recv[:n_recv], x_send, recv_sizes, send_sizes, group=self.group)
         dist.all_to_all_single(meta_recv, meta_send, recv_sizes, send_sizes, group=self.group)
-        if n_recv:
-            slot = self.slot_map(dev)[meta_recv[:, 0].to(torch.int64)]
-            y_recv = self.c.grouped_ffn(x_recv, slot, meta_recv[:, 1].contiguous().view(torch.float32),
-                                        out_dtype=torch.float32)
-        else:
-            y_recv = torch.empty((0, H), dtype=torch.float32, device=dev)
-        y_back = torch.empty((Tl * K, H), dtype=torch.float32, device=dev)
-        dist.all_to_all_single(y_back, y_recv, send_sizes, recv_sizes, group=self.group)
-        return self.c.combine_rows(y_back, plan.inv, out_dtype=torch.float32)
+        # received routed rows + this rank's own tokens for the shared expert, one grouped call
+        x_recv[n_recv:] = x_local
+        shared_slot = self.c.find_shared_slot()
+        slot = torch.cat([self.slot_map(dev)[meta_recv[:, 0].to(torch.int64)],
+                          torch.full((Tl,), shared_slot, dtype=torch.int32, device=dev)])
+        wts = torch.cat([meta_recv[:, 1].view(torch.float32), torch.ones(Tl, dtype=torch.float32, device=dev)])
+        y_all = self.c.grouped_ffn(x_recv, slot, wts, out_dtype=torch.float32)
+        rows = torch.empty((Tl * K + Tl, H), dtype=torch.float32, device=dev)
+        dist.all_to_all_single(rows[:Tl * K], y_all[:n_recv], send_sizes, recv_sizes, group=self.group)
+        rows[Tl * K:] = y_all[n_recv:]
+        tk_row = torch.cat([plan.inv, torch.arange(Tl * K, Tl * K + Tl, device=dev)[:, None]], dim=1)
+        return self.c.combine_rows(rows, tk_row, residual=residual, out_dtype=od)

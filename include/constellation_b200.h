@@ -151,6 +151,14 @@ int cst_moe_routed(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, cons
                    const float* topk_weight, int32_t top_k, uint32_t flags, void* out, int32_t out_dtype,
                    void* stream);
 
+/* cst_moe_routed with the shared expert applied only to tokens [shared_begin, shared_end):
+ * the expert-parallel form, where every rank runs its own experts on all gathered tokens
+ * but the shared expert only on the tokens it owns, inside the same grouped launches
+ * (run_shared_expert_block, server/deepseek_full_model_executor.py:264-316, per rank). */
+int cst_moe_routed_range(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, const int32_t* topk_idx,
+                         const float* topk_weight, int32_t top_k, int32_t shared_begin, int32_t shared_end,
+                         void* out, int32_t out_dtype, void* stream);
+
 /* Whole layer: route -> dispatch -> grouped FP8 SwiGLU -> combine (+ shared).
  * run_moe_layer (server/moe_layer_runtime.py:411-578) batched over T tokens, plus the
  * shared-expert sum of run_sparse_layer (server/full_model_runtime.py:283-348).

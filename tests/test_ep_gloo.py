@@ -56,19 +56,37 @@ class OracleCompute:
                     out[t] += np.float32(w[t, k]) * self.ex[e].forward(xf[t:t + 1])[0]
         return torch.from_numpy(out).to(out_dtype)
 
+    def find_shared_slot(self):
+        return self.hi - self.lo
+
+    def moe_routed_range(self, x, idx, w, begin, end, out_dtype=torch.float32):
+        out = self.moe_routed(x, idx, w).numpy()
+        xf = x.float().numpy()
+        for t in range(begin, end):
+            out[t] += self.shared.forward(xf[t:t + 1])[0]
+        return torch.from_numpy(out).to(out_dtype)
+
+    def cast_extra(self, extra, residual=None, out_dtype=torch.bfloat16):
+        y = extra if residual is None else extra + residual.float()
+        return y.to(out_dtype)
+
     def grouped_ffn(self, x, slot, w, out_dtype=torch.float32):
         xf = x.float().numpy()
         out = np.zeros((x.shape[0], H), np.float32)
         for r in range(x.shape[0]):
-            out[r] = np.float32(w[r]) * self.ex[int(slot[r]) + self.lo].forward(xf[r:r + 1])[0]
+            s = int(slot[r])
+            ex = self.shared if s == self.find_shared_slot() else self.ex[s + self.lo]
+            out[r] = np.float32(w[r]) * ex.forward(xf[r:r + 1])[0]
         return torch.from_numpy(out)
 
-    def combine_rows(self, rows, tk_row, out_dtype=torch.float32):
+    def combine_rows(self, rows, tk_row, residual=None, out_dtype=torch.float32):
         out = torch.zeros((tk_row.shape[0], H), dtype=torch.float32)
         for t in range(tk_row.shape[0]):
             for k in range(tk_row.shape[1]):
                 if int(tk_row[t, k]) >= 0:
                     out[t] += rows[int(tk_row[t, k])]
+        if residual is not None:
+            out += residual.float()
         return out.to(out_dtype)
 
     def shared_combine(self, x, extra=None, residual=None, out_dtype=None):
