@@ -230,7 +230,7 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     up.s0_off = c->geo.su_off;
     up.s1_off = c->geo.sg_off;
     up.KB = H / kBlock;
-    up.n_mb = I / kRowsPerItem;
+    up.n_mb = I / kBlock;  // one 128-row weight block per work item
     up.scale_ld = H / kBlock;
     up.groups = w.groups;
     up.meta = w.meta;
@@ -252,7 +252,7 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     dn.s0_off = c->geo.sd_off;
     dn.s1_off = c->geo.sd_off;
     dn.KB = I / kBlock;
-    dn.n_mb = H / kRowsPerItem;
+    dn.n_mb = H / kBlock;
     dn.scale_ld = I / kBlock;
     dn.bfrag = w.hfrag;
     dn.bscale = w.hscale;
@@ -443,6 +443,8 @@ int cst_route(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float
     if (T < 0 || T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, c->cfg.max_tokens);
     if (top_k <= 0 || top_k > c->cfg.top_k) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of [1, %d]", top_k, c->cfg.top_k);
     if (!x || !gate_weight || !bias || !topk_idx || !topk_weight) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (!aligned16(x) || !aligned16(gate_weight))
+        return fail(CST_ERR_INVALID_ARG, "x and gate_weight must be 16-byte aligned");
     if (T == 0) return CST_OK;
     if (int rc = ensure_device(c)) return rc;
     const cst_config& f = c->cfg;
@@ -530,8 +532,8 @@ int cst_moe_layer(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const f
     if (T < 0 || T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, c->cfg.max_tokens);
     if (top_k <= 0 || top_k > c->cfg.top_k) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of range", top_k);
     if (!x || !out || !gate_weight || !bias) return fail(CST_ERR_INVALID_ARG, "null pointer");
-    if (!aligned16(x) || !aligned16(out) || (residual && !aligned16(residual)))
-        return fail(CST_ERR_INVALID_ARG, "x, out and residual must be 16-byte aligned");
+    if (!aligned16(x) || !aligned16(out) || !aligned16(gate_weight) || (residual && !aligned16(residual)))
+        return fail(CST_ERR_INVALID_ARG, "x, out, gate_weight and residual must be 16-byte aligned");
     if (T == 0) return CST_OK;
     if (int rc = ensure_device(c)) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

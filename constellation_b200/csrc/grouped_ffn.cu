@@ -1,27 +1,34 @@
-// Grouped FP8 block-scaled expert SwiGLU for decode: the replacement of the reference's
-// fused_up_gate_kernel (expert_node_v2/backend/cuda/fused_up_gate_cuda_v2.cu:31-103) and
-// down_blockscale_kernel (backend/cuda/down_cuda_v2.cu:18-62), for every resident expert
-// and every token routed to it in ONE launch per projection.
+// Grouped FP8 block-scaled expert SwiGLU on the 5th-generation tensor cores (tcgen05):
+// the replacement of the reference's fused_up_gate_kernel
+// (expert_node_v2/backend/cuda/fused_up_gate_cuda_v2.cu:31-103) and down_blockscale_kernel
+// (backend/cuda/down_cuda_v2.cu:18-62), for every resident expert and every token routed to
+// it, in ONE launch per projection.
 //
-// Work item = (group, 64-row block of the output dimension).  A group is <= 16 packed
-// activation rows of one expert slot (route_pack.cu).  Persistent CTAs walk the item list
-// (gridDim = SMs x 2) with 5 warps:
-//   warp 4 (one lane): producer.  For each K block of each item it issues three TMA bulk
-//     copies into a ring of STAGES shared-memory stages: the weight chunk (16 KB up+gate or
-//     8 KB down, contiguous in the arena, already in MMA fragment order), the activation B
-//     fragments (3 KB per 8-row n-tile) and their per-row scales.  It runs ahead across
-//     item boundaries, so the weight stream never drains between items.
-//   warps 0-3: consumers, 16 output rows each.  Per K block: 128-bit shared loads of the A
-//     fragments, mma.sync.m16n8k32 E4M3 x E4M3 -> fp32 over the three activation terms, and
-//     the block-scale promotion acc += partial * scale_inv[rb, kb] * act_scale[row, kb] in
-//     fp32 registers (one 128x128 weight block per K block, as dequant_fp8_weight_blockwise
-//     defines the scales).
-//   Epilogue (fused): up/gate -> h = silu(gate) * up (silu(g) = g / (1 + exp(-g)), the
-//     reference's formula); down -> y * routing weight, written per packed row in fp32 so
-//     the combine adds the k contributions in a fixed order.
+// Work item = (group, 128-row block rb of the output dimension); a group is <= 16 packed
+// activation rows of one expert slot (route_pack.cu).  One persistent CTA per SM walks the
+// item list with 6 warps:
+//   warp 0, one lane: TMA producer.  Per 128-wide K block kb it bulk-copies the weight tile
+//     (16 KB per matrix: up+gate = 32 KB, down = 16 KB; contiguous in the arena and already in
+//     the swizzled K-major image the tensor cores read, relayout.cu) and the group's B tile
+//     (three E4M3 activation terms x 8 or 16 tokens, 3 or 6 KB, pack_act.cu) into a ring of
+//     STAGES shared-memory stages; it runs ahead across item boundaries.
+//   warp 1, one lane: MMA issuer.  Per kb: 4 k-steps x MATS of
+//     tcgen05.mma.cta_group::1.kind::f8f6f4, M = 128 weight rows, N = 3 terms x 8/16 tokens,
+//     K = 32, into one of two TMEM accumulator buffers; tcgen05.commit frees the smem stage
+//     and signals the accumulator to the epilogue.
+//   warps 2-5: epilogue.  Each thread owns one weight row (its TMEM lane): per kb it loads the
+//     accumulator (tcgen05.ld), releases the buffer, and promotes
+//       acc[token] += (D[term0] + D[term1] + D[term2]) * scale_inv[rb, kb] * act_scale[token, kb]
+//     in fp32 -- the block-scaled algebra of dequantize-then-matmul (server/fp8_utils.py:4-39,
+//     server/moe_layer_runtime.py:604-609) with the scales applied once per 128x128 block.
+//     At the end of an item: up/gate -> h = silu(gate) * up (silu(g) = g / (1 + exp(-g))),
+//     down -> y * routing weight, written per packed row in fp32 (coalesced along the rows).
+// TMEM: MATS x 48 fp32 columns per accumulator buffer, double-buffered (256 / 128 columns),
+// allocated by warp 2 and freed on every exit path.
 //
-// Every mbarrier wait is bounded (cst_common.cuh); a timeout sets the context's device
-// error word, the producer drains its in-flight copies and the CTA exits.
+// Every mbarrier wait is bounded (cst_common.cuh).  On a timeout the role records the
+// device error word, stops issuing, waits (bounded) for the work it already launched, and
+// the CTA reaches the common exit where TMEM is released.
 #include <cstdint>
 
 #include "cst_common.cuh"
@@ -30,196 +37,245 @@
 
 namespace cst {
 
-
 template <int MATS>
-struct FfnShape {
-    static constexpr int kABytes = 4 * 4 * MATS * kAFragBytes;            // 16 KB / 8 KB
-    static constexpr int kBBytes = kMaxTilesPerGroup * kBTileBytes;        // 6 KB
-    static constexpr int kSBytes = kMaxTilesPerGroup * kTileCols * 4;      // 64 B
-    static constexpr int kStage = (kABytes + kBBytes + kSBytes + 127) / 128 * 128;
+struct TcShape {
+    static constexpr int kABytes = MATS * 16384;                       // weight tile(s) per kb
+    static constexpr int kBBytes = kMaxTilesPerGroup * kBTileBytes;     // 6 KB
+    static constexpr int kStage = kABytes + kBBytes;                    // multiple of 1024
+    static constexpr int kColsPerBuf = MATS * 48;
+    static constexpr uint32_t kTmemCols = MATS == 2 ? 256 : 128;
+    static_assert(kStage % 1024 == 0, "stages must keep 1024-byte alignment");
 };
 
 template <int MATS, int STAGES>
-__global__ void __launch_bounds__(160, 2) grouped_ffn_kernel(FfnArgs a) {
-    using S = FfnShape<MATS>;
-    extern __shared__ __align__(1024) uint8_t smem[];
+__global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
+    using S = TcShape<MATS>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStage);
     uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 4);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
         }
         fence_barrier_init();
     }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, S::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
     __syncthreads();
-
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
     const int n_items = a.meta->n_groups * a.n_mb;
 
-    if (warp == 4) {
-        if (lane != 0) return;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            uint32_t it = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+                const int gi = item / a.n_mb;
+                const int rb = item - gi * a.n_mb;
+                const GroupRec gr = a.groups[gi];
+                const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
+                const uint8_t* A = a.arena + int64_t(gr.slot) * a.slot_bytes + a.a_off +
+                                   int64_t(rb) * a.KB * S::kABytes;
+                const uint8_t* B = a.bfrag + int64_t(gr.tile_base) * a.KB * kBTileBytes;
+                const uint32_t bbytes = uint32_t(NT) * kBTileBytes;
+                for (int kb = 0; kb < a.KB; ++kb) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + s * S::kStage;
+                    mbar_arrive_expect_tx(&full[s], S::kABytes + bbytes);
+                    tma_bulk_g2s(st, A + int64_t(kb) * S::kABytes, S::kABytes, &full[s]);
+                    tma_bulk_g2s(st + S::kABytes, B + int64_t(kb) * bbytes, bbytes, &full[s]);
+                    ++it;
+                }
+            }
+            // never leave with bulk copies still writing shared memory
+            const uint32_t first = it > uint32_t(STAGES) ? it - STAGES : 0u;
+            for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % STAGES], (j / STAGES) & 1u, a.err);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            uint32_t it = 0;
+            bool ok = true;
+            const uint32_t smem_base = smem_u32(smem);
+            for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+                const int gi = item / a.n_mb;
+                const GroupRec gr = a.groups[gi];
+                const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
+                const uint32_t idesc = umma_idesc_e4m3(128, kSplits * kTileCols * NT);
+                for (int kb = 0; kb < a.KB; ++kb) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1u;
+                    const int b = it & 1;
+                    const uint32_t bph = (it >> 1) & 1u;
+                    if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tempty[b], bph ^ 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = smem_base + s * S::kStage;
+#pragma unroll
+                    for (int ks = 0; ks < kBlock / kKStep; ++ks) {
+                        const uint64_t bdesc = umma_desc_sw128(st + S::kABytes + ks * kKStep);
+#pragma unroll
+                        for (int m = 0; m < MATS; ++m) {
+                            const uint64_t adesc = umma_desc_sw128(st + m * 16384 + ks * kKStep);
+                            tc_mma_e4m3(tmem + b * S::kColsPerBuf + m * 48, adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
+                        }
+                    }
+                    tc_commit(&empty[s]);
+                    tc_commit(&tfull[b]);
+                    ++it;
+                }
+            }
+            // the MMAs issued last must have finished before TMEM is released
+            if (it > 0) mbar_wait(&tfull[(it - 1) & 1], ((it - 1) >> 1) & 1u, a.err);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;                 // TMEM lane quarter this warp may access
+        const int row = quarter * 32 + lane;          // weight row inside the 128-row block
+        const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
         uint32_t it = 0;
         bool ok = true;
         for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
             const int gi = item / a.n_mb;
-            const int mb = item - gi * a.n_mb;
+            const int rb = item - gi * a.n_mb;
             const GroupRec gr = a.groups[gi];
             const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
-            const uint8_t* A = a.arena + int64_t(gr.slot) * a.slot_bytes + a.a_off +
-                               int64_t(mb) * a.KB * S::kABytes;
-            const uint8_t* B = a.bfrag + int64_t(gr.tile_base) * a.KB * kBTileBytes;
-            const float* Sc = a.bscale + int64_t(gr.tile_base) * a.KB * kTileCols;
-            const uint32_t bbytes = uint32_t(NT) * kBTileBytes;
-            const uint32_t sbytes = uint32_t(NT) * kTileCols * 4;
+            const uint8_t* slot = a.arena + int64_t(gr.slot) * a.slot_bytes;
+            const float* ws0 = reinterpret_cast<const float*>(slot + a.s0_off) + int64_t(rb) * a.scale_ld;
+            const float* ws1 = reinterpret_cast<const float*>(slot + a.s1_off) + int64_t(rb) * a.scale_ld;
+            const float* xsc = a.bscale + int64_t(gr.tile_base) * a.KB * kTileCols;
+            float acc[MATS][kGroupRows];
+#pragma unroll
+            for (int m = 0; m < MATS; ++m)
+#pragma unroll
+                for (int t = 0; t < kGroupRows; ++t) acc[m][t] = 0.0f;
+
             for (int kb = 0; kb < a.KB; ++kb) {
-                const int s = it % STAGES;
-                const uint32_t ph = (it / STAGES) & 1u;
-                if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) {
+                const int b = it & 1;
+                const uint32_t bph = (it >> 1) & 1u;
+                if (!mbar_wait(&tfull[b], bph, a.err)) {
                     ok = false;
                     break;
                 }
-                uint8_t* st = smem + s * S::kStage;
-                mbar_arrive_expect_tx(&full[s], S::kABytes + bbytes + sbytes);
-                tma_bulk_g2s(st, A + int64_t(kb) * S::kABytes, S::kABytes, &full[s]);
-                tma_bulk_g2s(st + S::kABytes, B + int64_t(kb) * bbytes, bbytes, &full[s]);
-                tma_bulk_g2s(st + S::kABytes + S::kBBytes, Sc + int64_t(kb) * NT * kTileCols, sbytes,
-                             &full[s]);
+                tc_fence_after();
+                uint32_t d[MATS][48];
+                const uint32_t base = tmem + lane_addr + b * S::kColsPerBuf;
+#pragma unroll
+                for (int m = 0; m < MATS; ++m) {
+                    tmem_ld16(base + m * 48, &d[m][0]);
+                    tmem_ld16(base + m * 48 + 16, &d[m][16]);
+                    tmem_ld16(base + m * 48 + 32, &d[m][32]);
+                }
+                tmem_wait_ld();
+#pragma unroll
+                for (int m = 0; m < MATS; ++m) tmem_reg_fence(d[m]);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);
+
+                float wsc[MATS];
+                wsc[0] = __ldg(ws0 + kb);
+                if constexpr (MATS == 2) wsc[1] = __ldg(ws1 + kb);
+                const float* xs = xsc + int64_t(kb) * NT * kTileCols;
+                if (NT == 1) {
+#pragma unroll
+                    for (int t = 0; t < kTileCols; ++t) {
+                        const float sx = __ldg(xs + t);
+#pragma unroll
+                        for (int m = 0; m < MATS; ++m) {
+                            const float v = __uint_as_float(d[m][t]) + __uint_as_float(d[m][8 + t]) +
+                                            __uint_as_float(d[m][16 + t]);
+                            acc[m][t] = fmaf(v, wsc[m] * sx, acc[m][t]);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int t = 0; t < kGroupRows; ++t) {
+                        const float sx = __ldg(xs + t);
+#pragma unroll
+                        for (int m = 0; m < MATS; ++m) {
+                            const float v = __uint_as_float(d[m][t]) + __uint_as_float(d[m][16 + t]) +
+                                            __uint_as_float(d[m][32 + t]);
+                            acc[m][t] = fmaf(v, wsc[m] * sx, acc[m][t]);
+                        }
+                    }
+                }
                 ++it;
             }
-        }
-        // never leave the CTA with bulk copies still writing its shared memory
-        const uint32_t first = it > uint32_t(STAGES) ? it - STAGES : 0u;
-        for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % STAGES], (j / STAGES) & 1u, a.err);
-        return;
-    }
-
-    // consumers
-    const int g = lane >> 2, t = lane & 3;
-    uint32_t it = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int gi = item / a.n_mb;
-        const int mb = item - gi * a.n_mb;
-        const GroupRec gr = a.groups[gi];
-        const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
-        const int rb = (mb * kRowsPerItem) / kBlock;
-        const uint8_t* slot = a.arena + int64_t(gr.slot) * a.slot_bytes;
-        const float* ws0 = reinterpret_cast<const float*>(slot + a.s0_off) + int64_t(rb) * a.scale_ld;
-        const float* ws1 = reinterpret_cast<const float*>(slot + a.s1_off) + int64_t(rb) * a.scale_ld;
-
-        float acc[MATS][kMaxTilesPerGroup][4];
+            if (!ok) break;
+            // fused epilogue: one weight row, every token of the group
+            const int orow = rb * kBlock + row;
 #pragma unroll
-        for (int m = 0; m < MATS; ++m)
-#pragma unroll
-            for (int nt = 0; nt < kMaxTilesPerGroup; ++nt)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) acc[m][nt][i] = 0.0f;
-
-        for (int kb = 0; kb < a.KB; ++kb) {
-            const int s = it % STAGES;
-            const uint32_t ph = (it / STAGES) & 1u;
-            if (!mbar_wait(&full[s], ph, a.err)) return;
-            const uint8_t* st = smem + s * S::kStage;
-            const uint8_t* sB = st + S::kABytes;
-            const float* sS = reinterpret_cast<const float*>(st + S::kABytes + S::kBBytes);
-            uint4 af[4][MATS];
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-                for (int m = 0; m < MATS; ++m)
-                    af[ks][m] = lds128(st + ((warp * 4 + ks) * MATS + m) * kAFragBytes + lane * 16);
-            float wsc[MATS];
-            wsc[0] = __ldg(ws0 + kb);
-            if constexpr (MATS == 2) wsc[1] = __ldg(ws1 + kb);
-#pragma unroll
-            for (int nt = 0; nt < kMaxTilesPerGroup; ++nt) {
-                if (nt < NT) {
-                    float c[MATS][4][4];
-#pragma unroll
-                    for (int m = 0; m < MATS; ++m)
-#pragma unroll
-                        for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) c[m][ks][i] = 0.0f;
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-                        for (int sp = 0; sp < kSplits; ++sp) {
-                            const uint2 b = lds64(sB + ((nt * 4 + ks) * kSplits + sp) * kFragBytes + lane * 8);
-#pragma unroll
-                            for (int m = 0; m < MATS; ++m) mma_e4m3_16832(c[m][ks], af[ks][m], b.x, b.y);
-                        }
+            for (int t = 0; t < kGroupRows; ++t) {
+                if (t < gr.n_rows) {
+                    const int prow = gr.row_start + t;
+                    float v;
+                    if constexpr (MATS == 2) {
+                        const float up = acc[0][t];
+                        const float gate = acc[1][t];
+                        v = (gate / (1.0f + expf(-gate))) * up;
+                    } else {
+                        v = acc[0][t] * a.row_weight[prow];
                     }
-                    const float xs0 = sS[nt * kTileCols + 2 * t];
-                    const float xs1 = sS[nt * kTileCols + 2 * t + 1];
-#pragma unroll
-                    for (int m = 0; m < MATS; ++m) {
-                        const float f0 = wsc[m] * xs0, f1 = wsc[m] * xs1;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float v = (c[m][0][i] + c[m][1][i]) + (c[m][2][i] + c[m][3][i]);
-                            acc[m][nt][i] = fmaf(v, (i & 1) ? f1 : f0, acc[m][nt][i]);
-                        }
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            ++it;
-        }
-
-        // fused epilogue
-#pragma unroll
-        for (int nt = 0; nt < kMaxTilesPerGroup; ++nt) {
-            if (nt < NT) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int col = nt * kTileCols + 2 * t + (i & 1);
-                    if (col < gr.n_rows) {
-                        const int prow = gr.row_start + col;
-                        const int orow = mb * kRowsPerItem + warp * kWarpRows + g + 8 * (i >> 1);
-                        float v;
-                        if constexpr (MATS == 2) {
-                            const float up = acc[0][nt][i];
-                            const float gate = acc[1][nt][i];
-                            v = (gate / (1.0f + expf(-gate))) * up;
-                        } else {
-                            v = acc[0][nt][i] * a.row_weight[prow];
-                        }
-                        a.out[int64_t(prow) * a.ld_out + orow] = v;
-                    }
+                    a.out[int64_t(prow) * a.ld_out + orow] = v;
                 }
             }
         }
     }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 2) tmem_dealloc(tmem, S::kTmemCols);
 }
 
-constexpr int kUpGateStages = 4;
-constexpr int kDownStages = 6;
+constexpr int kUpGateStages = 5;
+constexpr int kDownStages = 8;
 
 template <int MATS, int STAGES>
-size_t ffn_smem_bytes() {
-    return size_t(STAGES) * FfnShape<MATS>::kStage + 2 * STAGES * sizeof(uint64_t);
+size_t tc_smem_bytes() {
+    return size_t(STAGES) * TcShape<MATS>::kStage + 1024 /* alignment slack */ + 256 /* barriers */;
 }
 
 cudaError_t grouped_ffn_init_attributes() {
-    cudaError_t e = cudaFuncSetAttribute(grouped_ffn_kernel<2, kUpGateStages>,
+    cudaError_t e = cudaFuncSetAttribute(grouped_ffn_tc_kernel<2, kUpGateStages>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(ffn_smem_bytes<2, kUpGateStages>()));
+                                         int(tc_smem_bytes<2, kUpGateStages>()));
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(grouped_ffn_kernel<1, kDownStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(ffn_smem_bytes<1, kDownStages>()));
+    return cudaFuncSetAttribute(grouped_ffn_tc_kernel<1, kDownStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(tc_smem_bytes<1, kDownStages>()));
 }
 
 cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream) {
-    const int grid = num_sms * 2;
     if (upgate) {
-        grouped_ffn_kernel<2, kUpGateStages>
-            <<<grid, 160, ffn_smem_bytes<2, kUpGateStages>(), stream>>>(a);
+        grouped_ffn_tc_kernel<2, kUpGateStages>
+            <<<num_sms, 192, tc_smem_bytes<2, kUpGateStages>(), stream>>>(a);
     } else {
-        grouped_ffn_kernel<1, kDownStages><<<grid, 160, ffn_smem_bytes<1, kDownStages>(), stream>>>(a);
+        grouped_ffn_tc_kernel<1, kDownStages><<<num_sms, 192, tc_smem_bytes<1, kDownStages>(), stream>>>(a);
     }
     return cudaGetLastError();
 }

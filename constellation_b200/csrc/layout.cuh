@@ -1,25 +1,26 @@
 // HBM layouts of the grouped FP8 expert path (shared by host and device code).
 //
-// Expert arena (one slot per resident expert, written once at upload):
-//   [ up/gate chunks | down chunks | scale grids ]
-//   up/gate chunk (mb, kb): the 64 rows [64 mb, 64 mb + 64) of BOTH w_up and w_gate over
-//     the 128 columns of K block kb, 16 KB, fragment-major:
-//       byte = ((w * 4 + ks) * 2 + mat) * 512 + lane * 16 + j
-//     w = consumer warp (16 rows each), ks = 32-wide k step, mat = 0 up / 1 gate,
-//     lane = 4 g + t, j = 4 reg + byte with reg 0..3 the mma.m16n8k32 A registers:
-//       row = 16 w + g + 8 (reg & 1),  col = 32 ks + 4 t + 16 (reg >> 1) + byte.
-//     Chunks of one 64-row item are contiguous: one TMA bulk copy per K block.
-//   down chunk (mb, kb): the same with one matrix (w_down rows = hidden), 8 KB.
+// Swizzled K-major tile (the tensor cores' shared-memory image, SWIZZLE_128B): 128 rows x 128
+// bytes of K, row r at byte 128 r, its 16-byte chunk c stored at chunk position c ^ (r & 7).
+// Eight rows (1024 B) form one swizzle atom; a TMA bulk copy of a tile into a 1024-byte
+// aligned stage gives exactly the operand a tcgen05 smem descriptor describes.
+//
+// Expert arena (one slot per resident expert, written once at upload by relayout.cu):
+//   [ up/gate tiles | down tiles | scale grids ]
+//   up/gate: for 128-row block rb (of I) and 128-column block kb (of H), 32 KB =
+//     [w_up tile | w_gate tile], tiles of one rb contiguous over kb -> the work item
+//     (group, rb) streams rb's row of tiles front to back.
+//   down: the same with one 16 KB w_down tile per (rb of H, kb of I).
 //   scale grids: w_up, w_gate [I/128, H/128] and w_down [H/128, I/128] fp32, row-major
 //     exactly as in the upload format (expert_format_v2.h BlockScaleMetaV2).
 //
-// Packed activations (per layer call, written by the activation packer):
-//   rows are grouped; a group is <= 16 rows of one expert slot (2 n-tiles of 8);
-//   for n-tile `tile` (global tile index) and K block kb the B operand is
-//       ((tile_base_of_group * KB + kb * NT + nt) * 3072) + (ks * 3 + split) * 256 + lane * 8 + j
-//     lane = 4 g + t, j = 4 half + byte:  token col = g, k = 32 ks + 4 t + 16 half + byte
-//   and the per-(row, K block) power-of-two scale sits at
-//       (tile_base_of_group * KB + kb * NT + nt) * 8 + col.
+// Packed activations (per layer call, written by pack_act.cu):
+//   rows are grouped; a group is <= 16 rows of one expert slot (NT = 1 or 2 n-tiles of 8).
+//   For group g and K block kb the B operand is one swizzled K-major tile of 3 * 8 NT rows
+//   (row n = term * 8 NT + token, term = 0..2 of the three-term E4M3 split) at byte
+//       (tile_base(g) * KB + kb * NT) * 3072,
+//   and the power-of-two scale of (token, kb) is the float at
+//       (tile_base(g) * KB + kb * NT) * 8 + token.
 #pragma once
 
 #include <cstddef>

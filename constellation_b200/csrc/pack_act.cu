@@ -88,19 +88,20 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
                 rsd -= e4m3_to_f32(b);
             }
         }
-        // B fragment placement of k = 4 lane .. 4 lane + 3 inside the 128-wide block
-        const int ks = lane >> 3;
-        const int kk = 4 * (lane & 7);
-        const int t = (kk & 15) >> 2;
-        const int half = kk >> 4;
-        const int out_lane = j * 4 + t;
-        const int64_t tile_off = (int64_t(gr.tile_base) * KB + int64_t(kb) * NT + nt);
-        uint8_t* base = a.bfrag + tile_off * kBTileBytes;
+        // K-major, 128-byte swizzled placement: B row n = split * TP + token (TP = 8 NT),
+        // 128 bytes of K per row, 16-byte chunk c of row n stored at chunk c ^ (n & 7).
+        const int tok = nt * kTileCols + j;
+        const int TP = NT * kTileCols;
+        const int64_t gk = int64_t(gr.tile_base) * KB + int64_t(kb) * NT;  // (group, kb) chunk
+        uint8_t* base = a.bfrag + gk * kBTileBytes;
+        const int c = lane >> 2;
 #pragma unroll
         for (int sp = 0; sp < kSplits; ++sp) {
-            *reinterpret_cast<uint32_t*>(base + (ks * kSplits + sp) * kFragBytes + out_lane * 8 + half * 4) = q[sp];
+            const int n = sp * TP + tok;
+            const int pc = c ^ (n & 7);
+            *reinterpret_cast<uint32_t*>(base + n * kBlock + pc * 16 + 4 * (lane & 3)) = q[sp];
         }
-        if (lane == 0) a.bscale[tile_off * kTileCols + j] = s;
+        if (lane == 0) a.bscale[gk * kTileCols + tok] = s;
     }
 }
 

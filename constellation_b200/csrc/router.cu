@@ -39,14 +39,56 @@ template <>
 __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
 
 constexpr int kRT = 32;   // tile edge (experts and tokens)
-constexpr int kRK = 32;   // K chunk per shared-memory step
+constexpr int kRK = 128;  // K chunk per shared-memory step
+constexpr int kRKP = kRK + 4;
 
+// 16 consecutive activations of row `t` starting at column `k` (vector loads), as fp32.
+template <typename TX>
+__device__ __forceinline__ void load16(const TX* x, int64_t off, float (&v)[16]);
+template <>
+__device__ __forceinline__ void load16<float>(const float* x, int64_t off, float (&v)[16]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 f = *reinterpret_cast<const float4*>(x + off + 4 * i);
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+}
+template <>
+__device__ __forceinline__ void load16<__nv_bfloat16>(const __nv_bfloat16* x, int64_t off, float (&v)[16]) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint4 u = *reinterpret_cast<const uint4*>(x + off + 8 * i);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+            v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+        }
+    }
+}
+template <>
+__device__ __forceinline__ void load16<__half>(const __half* x, int64_t off, float (&v)[16]) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint4 u = *reinterpret_cast<const uint4*>(x + off + 8 * i);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+            v[8 * i + 2 * j] = f.x;
+            v[8 * i + 2 * j + 1] = f.y;
+        }
+    }
+}
+
+// 32 experts x 32 tokens per CTA over one K slice, 128-wide chunks staged in shared
+// memory; the next chunk is fetched into registers while the current one is consumed.
 template <typename TX>
 __global__ void __launch_bounds__(256) router_logits_kernel(const TX* __restrict__ x, const float* __restrict__ w,
                                                             float* __restrict__ partial, int T, int E, int H,
                                                             int k_slice) {
-    __shared__ float xs[kRT][kRK + 1];
-    __shared__ float ws[kRT][kRK + 1];
+    __shared__ __align__(16) float xs[kRT][kRKP];
+    __shared__ __align__(16) float ws[kRT][kRKP];
     const int e0 = blockIdx.x * kRT;
     const int t0 = blockIdx.y * kRT;
     const int kz = blockIdx.z;
@@ -54,26 +96,52 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const TX* __restrict
     const int tid = threadIdx.x;
     const int tx = tid & 15;  // expert pair
     const int ty = tid >> 4;  // token pair
+    const int lr = tid >> 3;         // staged row 0..31
+    const int lc = (tid & 7) * 16;   // staged column 0..112
+    const bool t_ok = (t0 + lr) < T;
+    const bool e_ok = (e0 + lr) < E;
+    const int64_t xoff = int64_t(t0 + lr) * H + lc;
+    const int64_t woff = int64_t(e0 + lr) * H + lc;
+    float rx[16], rw[16];
+    auto fetch = [&](int k0) {
+        if (t_ok) {
+            load16<TX>(x, xoff + k0, rx);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) rx[i] = 0.0f;
+        }
+        if (e_ok) {
+            load16<float>(w, woff + k0, rw);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) rw[i] = 0.0f;
+        }
+    };
     float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    fetch(k_begin);
     for (int k0 = k_begin; k0 < k_begin + k_slice; k0 += kRK) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int idx = tid + i * 256;  // 0..1023
-            const int r = idx >> 5, c = idx & 31;
-            const int t = t0 + r;
-            xs[r][c] = (t < T) ? to_f32<TX>(x[int64_t(t) * H + k0 + c]) : 0.0f;
-            const int e = e0 + r;
-            ws[r][c] = (e < E) ? w[int64_t(e) * H + k0 + c] : 0.0f;
+        for (int i = 0; i < 16; i += 4) {
+            *reinterpret_cast<float4*>(&xs[lr][lc + i]) = make_float4(rx[i], rx[i + 1], rx[i + 2], rx[i + 3]);
+            *reinterpret_cast<float4*>(&ws[lr][lc + i]) = make_float4(rw[i], rw[i + 1], rw[i + 2], rw[i + 3]);
         }
         __syncthreads();
-#pragma unroll 8
-        for (int c = 0; c < kRK; ++c) {
-            const float x0 = xs[2 * ty][c], x1 = xs[2 * ty + 1][c];
-            const float w0 = ws[2 * tx][c], w1 = ws[2 * tx + 1][c];
-            acc[0][0] = fmaf(x0, w0, acc[0][0]);
-            acc[0][1] = fmaf(x0, w1, acc[0][1]);
-            acc[1][0] = fmaf(x1, w0, acc[1][0]);
-            acc[1][1] = fmaf(x1, w1, acc[1][1]);
+        if (k0 + kRK < k_begin + k_slice) fetch(k0 + kRK);
+#pragma unroll 4
+        for (int c = 0; c < kRK; c += 4) {
+            const float4 x0 = *reinterpret_cast<const float4*>(&xs[2 * ty][c]);
+            const float4 x1 = *reinterpret_cast<const float4*>(&xs[2 * ty + 1][c]);
+            const float4 w0 = *reinterpret_cast<const float4*>(&ws[2 * tx][c]);
+            const float4 w1 = *reinterpret_cast<const float4*>(&ws[2 * tx + 1][c]);
+            const float xa[4] = {x0.x, x0.y, x0.z, x0.w}, xb[4] = {x1.x, x1.y, x1.z, x1.w};
+            const float wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[0][0] = fmaf(xa[j], wa[j], acc[0][0]);
+                acc[0][1] = fmaf(xa[j], wb[j], acc[0][1]);
+                acc[1][0] = fmaf(xb[j], wa[j], acc[1][0]);
+                acc[1][1] = fmaf(xb[j], wb[j], acc[1][1]);
+            }
         }
         __syncthreads();
     }
@@ -274,6 +342,8 @@ extern "C" int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int3
     clear_last_error();
     if (x_dtype < 1 || x_dtype > 3) return set_last_error(3, "bad x_dtype %d", x_dtype);
     if (!x || !gate_weight || !bias || !topk_idx || !topk_weight) return set_last_error(3, "null pointer");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate_weight)) & 15u)
+        return set_last_error(3, "x and gate_weight must be 16-byte aligned");
     if (hidden <= 0 || hidden % 128) return set_last_error(3, "hidden=%d must be a positive multiple of 128", hidden);
     if (n_experts <= 0 || n_experts > 1024) return set_last_error(3, "n_experts=%d out of [1, 1024]", n_experts);
     if (n_group <= 0 || n_group > 32 || n_experts % n_group)
