@@ -305,7 +305,8 @@ def run_ours(args):
                    "cuda_graph": graph is not None,
                    "touched_experts": U_total,
                    "l2": "no flush: 11.3 GB of expert weights (>= 1.2 GB per GPU) exceed the 126 MB L2"},
-        "roofline": {"kernel": "grouped_ffn up/gate (E4M3 mma.sync, TMA bulk ring)", "bound": "hbm",
+        "roofline": {"kernel": "grouped_ffn_tc up/gate (tcgen05 kind::f8f6f4, TMEM accumulators, TMA bulk ring)",
+                     "bound": "hbm",
                      "achieved": round(ach_upg, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(ach_upg / peak, 4), "peak_source": peak_kind,
                      "bytes_per_launch": upg_bytes, "ms_per_launch": round(upg_ms, 4), "traffic": None},

@@ -650,7 +650,8 @@ int cst_combine_rows(cst_ctx* c, const float* rows, int64_t ld_rows, const int32
     if (int rc = check_ctx(c)) return rc;
     if (!valid_dtype(out_dtype) || (residual && !valid_dtype(residual_dtype)))
         return fail(CST_ERR_INVALID_ARG, "bad dtype");
-    if (T < 0 || k1 < 0 || (k1 > 0 && (!rows || !tk_row)) || !out) return fail(CST_ERR_INVALID_ARG, "bad arguments");
+    if (T < 0 || k1 < 0 || k1 > 16 || (k1 > 0 && (!rows || !tk_row)) || !out)
+        return fail(CST_ERR_INVALID_ARG, "bad arguments (T=%d, k1=%d; k1 must be <= 16)", T, k1);
     if ((rows && (!aligned16(rows) || ld_rows % 4)) || !aligned16(out) || (extra && !aligned16(extra)) ||
         (residual && !aligned16(residual)))
         return fail(CST_ERR_INVALID_ARG, "rows, extra, residual and out must be 16-byte aligned");

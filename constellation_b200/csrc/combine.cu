@@ -28,20 +28,30 @@ __device__ __forceinline__ float4 load_act4(const void* p, int dtype, int64_t id
     return make_float4(a.x, a.y, b.x, b.y);
 }
 
+// grid (T, ceil(H / 1024)): one float4 column group per thread, all k rows loaded
+// independently, so a token's sum costs one memory latency instead of H / 1024 of them.
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
     const int t = blockIdx.x;
     if (t >= a.T) return;
     const int32_t* rows = a.tk_row + int64_t(t) * a.K1;
-    for (int h = threadIdx.x * 4; h < a.H; h += blockDim.x * 4) {
+    for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < a.H; h += gridDim.y * blockDim.x * 4) {
+        // issue every row load before the first add (absent rows read as zero), then sum in k order
+        float4 v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int r = (k < a.K1) ? __ldg(rows + k) : -1;
+            v[k] = (r >= 0) ? __ldg(reinterpret_cast<const float4*>(a.y + int64_t(r) * a.ldy + h))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k = 0; k < a.K1; ++k) {
-            const int r = rows[k];
-            if (r < 0) continue;
-            const float4 v = *reinterpret_cast<const float4*>(a.y + int64_t(r) * a.ldy + h);
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k < a.K1) {
+                acc.x += v[k].x;
+                acc.y += v[k].y;
+                acc.z += v[k].z;
+                acc.w += v[k].w;
+            }
         }
         if (a.extra) {
             const float4 v = *reinterpret_cast<const float4*>(a.extra + int64_t(t) * a.H + h);
@@ -80,7 +90,8 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
 
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream) {
     if (a.T <= 0) return cudaSuccess;
-    combine_kernel<<<a.T, 256, 0, stream>>>(a);
+    const dim3 grid(a.T, (a.H + 1023) / 1024);
+    combine_kernel<<<grid, 256, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

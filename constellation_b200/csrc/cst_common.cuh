@@ -1,11 +1,12 @@
 // Device helpers shared by the sm_100a kernels of the MoE hot path.
 //
 //  * TMA bulk copies (cp.async.bulk global -> shared, completion on an mbarrier) and
-//    the mbarrier primitives that pace the producer/consumer stage ring.  Every wait
-//    is bounded: after kSpinLimit polls it records CST_DEV_ERR_TIMEOUT in the
-//    context's device error word and returns false, so a broken pipeline ends the
+//    the mbarrier primitives that pace the producer/consumer stage rings.  Every wait
+//    is bounded (wall clock or poll count): on timeout it records CST_DEV_ERR_TIMEOUT in
+//    the context's device error word and returns false, so a broken pipeline ends the
 //    kernel with a status the host can read instead of hanging the GPU.
-//  * FP8 E4M3 tensor-core MMA (mma.sync m16n8k32, fp32 accumulate).
+//  * tcgen05 helpers: TMEM alloc/dealloc, kind::f8f6f4 MMA with smem descriptors,
+//    commit to mbarriers, TMEM loads and the tcgen05 fences.
 //  * E4M3 encode/decode used by the activation packer.
 #pragma once
 
@@ -15,18 +16,14 @@
 
 namespace cst {
 
-constexpr int kBlock = 128;          // FP8 scale block (rows and cols)
-constexpr int kRowsPerItem = 64;     // weight rows one CTA work item covers
-constexpr int kWarpRows = 16;        // rows per consumer warp (one MMA M tile)
-constexpr int kKStep = 32;           // K per mma.m16n8k32
+constexpr int kBlock = 128;          // FP8 scale block (rows and cols) = weight rows per item
+constexpr int kKStep = 32;           // K of one tcgen05.mma kind::f8f6f4
 constexpr int kSplits = 3;           // E4M3 terms per activation element
-constexpr int kTileCols = 8;         // tokens per MMA N tile
-constexpr int kFragBytes = 256;      // one B fragment (32 x 8 e4m3) for a warp
-constexpr int kAFragBytes = 512;     // one A fragment (16 x 32 e4m3) for a warp
+constexpr int kTileCols = 8;         // tokens per n-tile
 constexpr int kMaxTilesPerGroup = 2; // routed groups carry at most 16 rows
 constexpr int kGroupRows = kMaxTilesPerGroup * kTileCols;
-// B bytes of one n-tile for one 128-wide K block: 4 k-steps x 3 splits x 256 B
-constexpr int kBTileBytes = (kBlock / kKStep) * kSplits * kFragBytes;  // 3072
+// B bytes of one n-tile for one 128-wide K block: 3 terms x 8 rows x 128 bytes
+constexpr int kBTileBytes = kSplits * kTileCols * kBlock;  // 3072
 
 // Device error word values (written with atomicMax so the first/most severe sticks).
 constexpr int CST_DEV_OK = 0;
@@ -179,29 +176,6 @@ template <int N>
 __device__ __forceinline__ void tmem_reg_fence(uint32_t (&r)[N]) {
 #pragma unroll
     for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
-}
-
-__device__ __forceinline__ void mma_e4m3_16832(float (&d)[4], const uint4& a, uint32_t b0,
-                                               uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
-        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 lds128(const void* p) {
-    uint4 v;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(smem_u32(p)));
-    return v;
-}
-
-__device__ __forceinline__ uint2 lds64(const void* p) {
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(smem_u32(p)));
-    return v;
 }
 
 // E4M3 round-to-nearest-even with saturation to +-448 (hardware cvt).

@@ -13,8 +13,9 @@
 // algebra as dequantize-then-matmul (server/fp8_utils.py:4-39,
 // server/moe_layer_runtime.py:604-609).
 //
-// One warp per (packed row, K block): 128 elements, 4 per lane, one 32-bit store per term.
-// Rows of a group's last n-tile beyond its row count are written as zeros.
+// One warp per (packed row, 8 consecutive K blocks): the row's metadata is read once and
+// the 8 source loads are issued together; per K block 128 elements, 4 per lane, one 32-bit
+// store per term.  Rows of a group's last n-tile beyond its row count are written as zeros.
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -49,18 +50,22 @@ __device__ __forceinline__ void load4(const PackActArgs& a, int64_t src_row, int
     }
 }
 
+constexpr int kPackKbPerTask = 8;  // K blocks one warp packs for one row
+
 __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
     const int KB = a.K / kBlock;
+    const int n_chunks = (KB + kPackKbPerTask - 1) / kPackKbPerTask;
     const int n_tiles = a.meta->n_tiles;
     const int lane = threadIdx.x & 31;
-    const int64_t n_tasks = int64_t(n_tiles) * kTileCols * KB;
+    const int64_t n_tasks = int64_t(n_tiles) * kTileCols * n_chunks;
     const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
     for (int64_t task = warp_global; task < n_tasks; task += n_warps) {
-        const int kb = static_cast<int>(task % KB);
-        const int64_t tr = task / KB;
+        // task = (n-tile, token column j, chunk of 8 K blocks); the row metadata is read once
+        const int chunk = static_cast<int>(task % n_chunks);
+        const int64_t tr = task / n_chunks;
         const int tile = static_cast<int>(tr / kTileCols);
-        const int j = static_cast<int>(tr % kTileCols);  // token column inside the n-tile
+        const int j = static_cast<int>(tr % kTileCols);
         const int gi = a.tile_group[tile];
         const GroupRec gr = a.groups[gi];
         const int nt = tile - gr.tile_base;
@@ -71,37 +76,51 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
             const int prow = gr.row_start + r;
             src_row = a.row_map ? a.row_map[prow] : prow;
         }
-        float v[4];
-        load4(a, src_row, kb * kBlock + 4 * lane, v);
-        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-        amax = warp_max(amax);
-        const float s = pow2_scale_for(amax);
-        const float inv = 1.0f / s;  // exact: s is a power of two
-        uint32_t q[kSplits] = {0u, 0u, 0u};
+        const int kb0 = chunk * kPackKbPerTask;
+        // all source loads of the chunk first
+        float v[kPackKbPerTask][4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            float rsd = v[e] * inv;
-#pragma unroll
-            for (int sp = 0; sp < kSplits; ++sp) {
-                const uint8_t b = e4m3_rn(rsd);
-                q[sp] |= uint32_t(b) << (8 * e);
-                rsd -= e4m3_to_f32(b);
+        for (int i = 0; i < kPackKbPerTask; ++i) {
+            if (kb0 + i < KB) {
+                load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, v[i]);
+            } else {
+                v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.0f;
             }
         }
-        // K-major, 128-byte swizzled placement: B row n = split * TP + token (TP = 8 NT),
-        // 128 bytes of K per row, 16-byte chunk c of row n stored at chunk c ^ (n & 7).
         const int tok = nt * kTileCols + j;
         const int TP = NT * kTileCols;
-        const int64_t gk = int64_t(gr.tile_base) * KB + int64_t(kb) * NT;  // (group, kb) chunk
-        uint8_t* base = a.bfrag + gk * kBTileBytes;
         const int c = lane >> 2;
 #pragma unroll
-        for (int sp = 0; sp < kSplits; ++sp) {
-            const int n = sp * TP + tok;
-            const int pc = c ^ (n & 7);
-            *reinterpret_cast<uint32_t*>(base + n * kBlock + pc * 16 + 4 * (lane & 3)) = q[sp];
+        for (int i = 0; i < kPackKbPerTask; ++i) {
+            const int kb = kb0 + i;
+            if (kb >= KB) break;
+            float amax = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
+            amax = warp_max(amax);
+            const float s = pow2_scale_for(amax);
+            const float inv = 1.0f / s;  // exact: s is a power of two
+            uint32_t q[kSplits] = {0u, 0u, 0u};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float rsd = v[i][e] * inv;
+#pragma unroll
+                for (int sp = 0; sp < kSplits; ++sp) {
+                    const uint8_t b = e4m3_rn(rsd);
+                    q[sp] |= uint32_t(b) << (8 * e);
+                    rsd -= e4m3_to_f32(b);
+                }
+            }
+            // K-major, 128-byte swizzled placement: B row n = split * TP + token (TP = 8 NT),
+            // 128 bytes of K per row, 16-byte chunk c of row n stored at chunk c ^ (n & 7).
+            const int64_t gk = int64_t(gr.tile_base) * KB + int64_t(kb) * NT;  // (group, kb) tile
+            uint8_t* base = a.bfrag + gk * kBTileBytes;
+#pragma unroll
+            for (int sp = 0; sp < kSplits; ++sp) {
+                const int n = sp * TP + tok;
+                const int pc = c ^ (n & 7);
+                *reinterpret_cast<uint32_t*>(base + n * kBlock + pc * 16 + 4 * (lane & 3)) = q[sp];
+            }
+            if (lane == 0) a.bscale[gk * kTileCols + tok] = s;
         }
-        if (lane == 0) a.bscale[gk * kTileCols + tok] = s;
     }
 }
 

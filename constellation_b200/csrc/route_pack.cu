@@ -25,6 +25,11 @@ namespace cst {
 constexpr int kPackThreads = 1024;
 constexpr uint32_t kInvalidKey = 0x7fffffffu;
 constexpr int kRoutePackMaxSmem = kRoutePackMaxKeys * 4 + 8192 * 4;
+constexpr int kRankSortMaxKeys = 2048;  // up to here keys are ranked by counting, beyond by bitonic sort
+
+__host__ __device__ constexpr int route_pack_key_area(int n_keys_pow2) {
+    return n_keys_pow2 <= kRankSortMaxKeys ? 2 * kRankSortMaxKeys : n_keys_pow2;
+}
 
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* total) {
@@ -55,8 +60,10 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* tot
 }
 
 __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, int n_keys_pow2) {
-    extern __shared__ uint32_t s_keys[];  // n_keys_pow2 keys, then n_slots ints
-    int* s_first = reinterpret_cast<int*>(s_keys + n_keys_pow2);
+    // keys (n_keys_pow2, or 2 x kRankSortMaxKeys when the rank sort needs its output
+    // buffer), then n_slots ints
+    extern __shared__ uint32_t s_keys[];
+    int* s_first = reinterpret_cast<int*>(s_keys + route_pack_key_area(n_keys_pow2));
     __shared__ int s_warp[32];
     const int tid = threadIdx.x;
     const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
@@ -90,20 +97,38 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, in
         s_keys[i] = key;
     }
     __syncthreads();
-    // bitonic sort, ascending
-    for (int size = 2; size <= n_keys_pow2; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = tid; i < (n_keys_pow2 >> 1); i += kPackThreads) {
-                const int lo = 2 * i - (i & (stride - 1));
-                const int hi = lo + stride;
-                const bool asc = (lo & size) == 0;
-                const uint32_t a0 = s_keys[lo], a1 = s_keys[hi];
-                if ((a0 > a1) == asc) {
-                    s_keys[lo] = a1;
-                    s_keys[hi] = a0;
+    if (n_keys_pow2 <= kRankSortMaxKeys) {
+        // decode-sized batches: every valid key's position is the number of smaller keys
+        // (keys are unique), one pass of n compares per key instead of log^2 n barriers
+        uint32_t* s_out = s_keys + kRankSortMaxKeys;
+        for (int i = tid; i < n_keys_pow2; i += kPackThreads) s_out[i] = kInvalidKey;
+        __syncthreads();
+        for (int i = tid; i < n_routes; i += kPackThreads) {
+            const uint32_t key = s_keys[i];
+            if (key == kInvalidKey) continue;
+            int rank = 0;
+            for (int j = 0; j < n_routes; ++j) rank += s_keys[j] < key;
+            s_out[rank] = key;
+        }
+        __syncthreads();
+        for (int i = tid; i < n_keys_pow2; i += kPackThreads) s_keys[i] = s_out[i];
+        __syncthreads();
+    } else {
+        // bitonic sort, ascending
+        for (int size = 2; size <= n_keys_pow2; size <<= 1) {
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                for (int i = tid; i < (n_keys_pow2 >> 1); i += kPackThreads) {
+                    const int lo = 2 * i - (i & (stride - 1));
+                    const int hi = lo + stride;
+                    const bool asc = (lo & size) == 0;
+                    const uint32_t a0 = s_keys[lo], a1 = s_keys[hi];
+                    if ((a0 > a1) == asc) {
+                        s_keys[lo] = a1;
+                        s_keys[hi] = a0;
+                    }
                 }
+                __syncthreads();
             }
-            __syncthreads();
         }
     }
     // number of valid rows and the first row of each slot
@@ -188,7 +213,7 @@ int route_pack_pow2(int n) {
 }
 
 size_t route_pack_smem(int n_keys_pow2, int n_slots) {
-    return size_t(n_keys_pow2) * 4 + size_t(n_slots) * 4;
+    return size_t(route_pack_key_area(n_keys_pow2)) * 4 + size_t(n_slots) * 4;
 }
 
 cudaError_t launch_route_pack(const PackArgs& a, cudaStream_t stream) {

@@ -186,36 +186,74 @@ __device__ __forceinline__ void warp_argmax(float& v, int& idx) {
 constexpr int kSelWarps = 4;
 constexpr int kMaxE = 1024;
 
+// Warp top-2 of (a >= b) pairs: merge with the partner lane's pair.
+__device__ __forceinline__ void warp_top2(float& a, float& b) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, a, o);
+        const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+        const float hi = fmaxf(a, oa);
+        const float lo = fmaxf(fminf(a, oa), fmaxf(b, ob));
+        a = hi;
+        b = lo;
+    }
+}
+
+// One warp per token.  Lane l holds experts e = l + 32 i (i < EPL) in registers; the
+// selection rounds touch only registers and warp shuffles.
+template <int EPL>
 __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(RouterArgs a) {
-    __shared__ float s_choice[kSelWarps][kMaxE];
-    __shared__ float s_score[kSelWarps][kMaxE];
-    __shared__ uint32_t s_taken[kSelWarps][kMaxE / 32];
-    __shared__ float s_gs[kSelWarps][32];
+    __shared__ float s_choice[kSelWarps][EPL * 32];
+    __shared__ float s_score[kSelWarps][EPL * 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * kSelWarps + warp;
     if (t >= a.T) return;
     const int E = a.E;
-    float* ch = s_choice[warp];
-    float* sc = s_score[warp];
-    uint32_t* taken = s_taken[warp];
-    for (int e = lane; e < E; e += 32) {
-        float l = 0.0f;
-        for (int z = 0; z < a.kz; ++z) l += a.partial[(int64_t(z) * a.T + t) * E + e];
-        if (a.logits_out) a.logits_out[int64_t(t) * E + e] = l;
-        const float s = 1.0f / (1.0f + expf(-l));
-        const bool res = (a.resident == nullptr) || (a.resident[e] != 0);
-        ch[e] = res ? (s + a.bias[e]) : -INFINITY;
-        sc[e] = res ? s : 0.0f;
+    const int epg = E / a.n_group;
+    const int64_t zstride = int64_t(a.T) * E;
+    const float* __restrict__ part = a.partial + int64_t(t) * E;
+    float ch[EPL];
+    int grp[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        ch[i] = -INFINITY;
+        grp[i] = 0x7fffffff;
+        if (e < E) {
+            // independent read-only loads, then the fixed-order sum over the K slices
+            float p[8];
+#pragma unroll
+            for (int z = 0; z < 8; ++z) p[z] = (z < a.kz) ? __ldg(part + z * zstride + e) : 0.0f;
+            float l = 0.0f;
+#pragma unroll
+            for (int z = 0; z < 8; ++z)
+                if (z < a.kz) l += p[z];
+            if (a.logits_out) a.logits_out[int64_t(t) * E + e] = l;
+            const float sg = 1.0f / (1.0f + expf(-l));
+            const bool res = (a.resident == nullptr) || (a.resident[e] != 0);
+            ch[i] = res ? (sg + a.bias[e]) : -INFINITY;
+            s_choice[warp][e] = ch[i];
+            s_score[warp][e] = res ? sg : 0.0f;
+            grp[i] = e / epg;
+        }
     }
-    for (int i = lane; i < kMaxE / 32; i += 32) taken[i] = 0u;
     __syncwarp();
     // group scores: sum of the two largest choice values of each group
-    const int epg = E / a.n_group;
-    float gs = -INFINITY;
-    if (lane < a.n_group) {
+    float gs = -INFINITY;  // lane g < n_group ends up holding group g's score
+    if (epg == 32 && (E & 31) == 0) {
+        // group g is exactly register row i = g: a warp top-2 per row
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            if (i < a.n_group) {
+                float m1 = ch[i], m2 = -INFINITY;
+                warp_top2(m1, m2);
+                if (lane == i) gs = m1 + m2;
+            }
+        }
+    } else if (lane < a.n_group) {
         float m1 = -INFINITY, m2 = -INFINITY;
         for (int j = 0; j < epg; ++j) {
-            const float v = ch[lane * epg + j];
+            const float v = s_choice[warp][lane * epg + j];
             if (v > m1) {
                 m2 = m1;
                 m1 = v;
@@ -224,42 +262,43 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(RouterArg
             }
         }
         gs = m1 + m2;
-        s_gs[warp][lane] = gs;
-        if (a.group_scores_out) a.group_scores_out[int64_t(t) * a.n_group + lane] = gs;
     }
-    __syncwarp();
+    if (lane < a.n_group && a.group_scores_out) a.group_scores_out[int64_t(t) * a.n_group + lane] = gs;
     // keep the topk_group best groups (value desc, index asc)
     uint32_t gmask = 0u;
     {
-        float v = (lane < a.n_group) ? gs : -INFINITY;
         bool used = lane >= a.n_group;
         for (int r = 0; r < a.topk_group; ++r) {
-            float bv = used ? -INFINITY : v;
+            float bv = used ? -INFINITY : gs;
             int bi = used ? 0x7fffffff : lane;
             warp_argmax(bv, bi);
             gmask |= 1u << bi;
             if (lane == bi) used = true;
         }
     }
-    // top_k experts over the group-masked choice values
+    // candidates: choice values of experts in kept groups, -inf elsewhere
+    float cand[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) cand[i] = (grp[i] < 32 && ((gmask >> grp[i]) & 1u)) ? ch[i] : -INFINITY;
+    // top_k rounds of warp arg-max over (value desc, index asc)
+    uint32_t taken = 0u;
     float wsel = 0.0f;
     int isel = -1;
     float denom = 0.0f;
     for (int r = 0; r < a.top_k; ++r) {
         float bv = -INFINITY;
         int bi = 0x7fffffff;
-        for (int e = lane; e < E; e += 32) {
-            if (taken[e >> 5] & (1u << (e & 31))) continue;
-            const float v = ((gmask >> (e / epg)) & 1u) ? ch[e] : -INFINITY;
-            if (v > bv || (v == bv && e < bi)) {
-                bv = v;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E && !((taken >> i) & 1u) && (cand[i] > bv || (cand[i] == bv && e < bi))) {
+                bv = cand[i];
                 bi = e;
             }
         }
         warp_argmax(bv, bi);
-        if (lane == 0) taken[bi >> 5] |= 1u << (bi & 31);
-        __syncwarp();
-        const float wv = sc[bi];
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        const float wv = s_score[warp][bi];
         denom += wv;  // sequential sum in selection order
         if (lane == r) {
             isel = bi;
@@ -303,7 +342,12 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
     }
     RouterArgs a{partial, kz, bias, resident, T, E, n_group, topk_group, top_k, norm, scale,
                  topk_idx, topk_w, logits_out, group_scores_out};
-    router_select_kernel<<<(T + kSelWarps - 1) / kSelWarps, kSelWarps * 32, 0, stream>>>(a);
+    const int grid_sel = (T + kSelWarps - 1) / kSelWarps;
+    if (E <= 256) {
+        router_select_kernel<8><<<grid_sel, kSelWarps * 32, 0, stream>>>(a);
+    } else {
+        router_select_kernel<32><<<grid_sel, kSelWarps * 32, 0, stream>>>(a);
+    }
     return cudaGetLastError();
 }
 
