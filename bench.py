@@ -257,6 +257,19 @@ def run_ours(args):
     upg = [s["grouped_up_gate"] for s in stages if s["grouped_up_gate"] > 0]
     dn = [s["grouped_down"] for s in stages if s["grouped_down"] > 0]
     stage_ms = {k: statistics.mean(s[k] for s in stages) for k in stages[0]} if stages else {}
+    # expert-parallel phases (gather / route / experts / reduce-scatter / cast), eager launches
+    ep_phase_ms = None
+    if world > 1:
+        sums: dict = {}
+        for _ in range(nprof):
+            moe.timeline = []
+            moe.forward(x, gw, gb)
+            torch.cuda.synchronize(dev)
+            tl = moe.timeline
+            for (_, e0), (name, e1) in zip(tl[:-1], tl[1:]):
+                sums[name] = sums.get(name, 0.0) + e0.elapsed_time(e1)
+        moe.timeline = None
+        ep_phase_ms = {k: round(v / nprof, 4) for k, v in sums.items()}
 
     # algorithmic bytes of the grouped kernels on this rank
     U_total = touched_experts(torch, ctx, gw, gb, x_all) if world == 1 else None
@@ -316,6 +329,7 @@ def run_ours(args):
         "layer_hbm": {"bytes_per_rank": layer_bytes, "achieved_gbs": round(layer_bytes / (ms_step / 1e3) / 1e9, 1),
                       "frac": round(layer_bytes / (ms_step / 1e3) / 1e9 / peak, 4)},
         "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+        "ep_phase_ms": ep_phase_ms,
         "e2e": {"value": round(T / (ms_e2e / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms_e2e, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,

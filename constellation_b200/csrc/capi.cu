@@ -63,7 +63,7 @@ namespace {
     } while (0)
 
 struct Workspace {
-    float* router_partial = nullptr;  // [kz, max_tokens, E]
+    float* router_logits = nullptr;   // [max_tokens, E]
     int32_t* topk_idx = nullptr;      // [max_tokens, 16]
     float* topk_w = nullptr;
     GroupRec* groups = nullptr;       // [max_rows]
@@ -74,7 +74,7 @@ struct Workspace {
     PackMeta* meta = nullptr;
     uint8_t* xfrag = nullptr;         // [max_rows, H/128, 3072]
     float* xscale = nullptr;          // [max_rows, H/128, 8]
-    float* h = nullptr;               // [max_rows, I]
+    float* h = nullptr;               // up/gate partial sums [part_rows, 2, I]
     uint8_t* hfrag = nullptr;
     float* hscale = nullptr;
     float* y = nullptr;               // [max_rows, H]
@@ -95,6 +95,7 @@ struct cst_ctx {
     std::vector<int32_t> expert_of_slot;  // slot -> router expert, -1 shared, -2 empty
     int32_t shared_slot = -1;
     int max_rows = 0;
+    int part_rows = 0;  // rows of up/gate partial sums the workspace holds (K splits x rows)
     uint8_t* ws_base = nullptr;
     size_t ws_bytes = 0;
     Workspace ws;
@@ -165,7 +166,6 @@ int alloc_workspace(cst_ctx* c) {
     const cst_config& f = c->cfg;
     const int H = f.hidden_dim, I = f.inter_dim, E = f.n_routed_experts;
     const int64_t R = c->max_rows;
-    const int kz = router_k_split(H);
     struct Piece {
         void** p;
         size_t bytes;
@@ -173,7 +173,7 @@ int alloc_workspace(cst_ctx* c) {
     Workspace& w = c->ws;
     const size_t tk = size_t(std::max<int64_t>(int64_t(f.max_tokens) * 16, R));
     std::vector<Piece> pieces = {
-        {reinterpret_cast<void**>(&w.router_partial), size_t(kz) * f.max_tokens * E * 4},
+        {reinterpret_cast<void**>(&w.router_logits), size_t(f.max_tokens) * E * 4},
         {reinterpret_cast<void**>(&w.topk_idx), size_t(f.max_tokens) * 16 * 4},
         {reinterpret_cast<void**>(&w.topk_w), size_t(f.max_tokens) * 16 * 4},
         {reinterpret_cast<void**>(&w.groups), size_t(R) * sizeof(GroupRec)},
@@ -184,7 +184,7 @@ int alloc_workspace(cst_ctx* c) {
         {reinterpret_cast<void**>(&w.meta), sizeof(PackMeta)},
         {reinterpret_cast<void**>(&w.xfrag), size_t(R) * (H / kBlock) * kBTileBytes},
         {reinterpret_cast<void**>(&w.xscale), size_t(R) * (H / kBlock) * kTileCols * 4},
-        {reinterpret_cast<void**>(&w.h), size_t(R) * I * 4},
+        {reinterpret_cast<void**>(&w.h), size_t(c->part_rows) * 2 * I * 4},
         {reinterpret_cast<void**>(&w.hfrag), size_t(R) * (I / kBlock) * kBTileBytes},
         {reinterpret_cast<void**>(&w.hscale), size_t(R) * (I / kBlock) * kTileCols * 4},
         {reinterpret_cast<void**>(&w.y), size_t(R) * H * 4},
@@ -238,12 +238,14 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     up.bscale = w.xscale;
     up.out = w.h;
     up.ld_out = I;
+    up.out_rows = c->part_rows;
+    up.max_split = 4;
     up.row_weight = nullptr;
     up.err = w.err;
     CST_CUDA(launch_grouped_ffn(up, true, c->num_sms, s));
     prof_mark(c, 3, s);
 
-    PackActArgs ph{w.h, CST_DTYPE_FP32, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale};
+    PackActArgs ph{w.h, kSrcUpGatePartials, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale};
     CST_CUDA(launch_pack_act(ph, c->num_sms, s));
     prof_mark(c, 4, s);
 
@@ -259,6 +261,8 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     dn.out = w.y;
     dn.ld_out = H;
     dn.row_weight = w.row_weight;
+    dn.out_rows = c->max_rows;
+    dn.max_split = 1;
     CST_CUDA(launch_grouped_ffn(dn, false, c->num_sms, s));
     prof_mark(c, 5, s);
     return CST_OK;
@@ -301,6 +305,9 @@ int cst_create(int32_t device, const cst_config* cfg, cst_ctx** out) {
     c->device = device;
     c->cfg = f;
     c->max_rows = f.max_rows > 0 ? f.max_rows : f.max_tokens * (f.top_k + 1);
+    // room for a 4-way K split of up/gate while the rows are few (the split is only chosen
+    // when items are scarce, i.e. for a few hundred rows)
+    c->part_rows = std::max(c->max_rows, std::min(4 * c->max_rows, 8192));
     if (c->max_rows > kRoutePackMaxKeys) {
         delete c;
         return fail(CST_ERR_INVALID_ARG, "max_rows=%d exceeds %d", f.max_rows, kRoutePackMaxKeys);
@@ -449,8 +456,9 @@ int cst_route(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float
     if (int rc = ensure_device(c)) return rc;
     const cst_config& f = c->cfg;
     CST_CUDA(launch_router(x, x_dtype, gate_weight, bias, resident, T, f.n_routed_experts, f.hidden_dim, f.n_group,
-                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor, c->ws.router_partial,
-                           topk_idx, topk_weight, logits, group_scores, static_cast<cudaStream_t>(stream)));
+                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor,
+                           logits ? logits : c->ws.router_logits, topk_idx, topk_weight, group_scores,
+                           static_cast<cudaStream_t>(stream)));
     return CST_OK;
 }
 
@@ -542,8 +550,8 @@ int cst_moe_layer(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const f
     const cst_config& f = c->cfg;
     prof_begin(c, s);
     CST_CUDA(launch_router(x, x_dtype, gate_weight, bias, resident, T, f.n_routed_experts, f.hidden_dim, f.n_group,
-                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor, c->ws.router_partial, idx,
-                           wts, nullptr, nullptr, s));
+                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor, c->ws.router_logits, idx,
+                           wts, nullptr, s));
     prof_mark(c, 0, s);
     return moe_routed_impl(c, x, x_dtype, T, idx, wts, top_k, flags, residual, out, out_dtype, s);
 }

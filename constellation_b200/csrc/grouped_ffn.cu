@@ -4,24 +4,28 @@
 // (backend/cuda/down_cuda_v2.cu:18-62), for every resident expert and every token routed to
 // it, in ONE launch per projection.
 //
-// Work item = (group, 128-row block rb of the output dimension); a group is <= 16 packed
-// activation rows of one expert slot (route_pack.cu).  One persistent CTA per SM walks the
-// item list with 6 warps:
+// Work item = (group, 128-row block rb of the output dimension, K split ks); a group is <= 16
+// packed activation rows of one expert slot (route_pack.cu).  The K split S (1, 2 or 4) is
+// chosen on the device from the group count so that small decode batches still give every
+// SM several items; up/gate then writes S raw partial sums that the h packer adds in fixed
+// order (pack_act.cu), the down projection never splits.  One persistent CTA per SM walks
+// the item list with 6 warps:
 //   warp 0, one lane: TMA producer.  Per 128-wide K block kb it bulk-copies the weight tile
 //     (16 KB per matrix: up+gate = 32 KB, down = 16 KB; contiguous in the arena and already in
-//     the swizzled K-major image the tensor cores read, relayout.cu) and the group's B tile
-//     (three E4M3 activation terms x 8 or 16 tokens, 3 or 6 KB, pack_act.cu) into a ring of
-//     STAGES shared-memory stages; it runs ahead across item boundaries.
+//     the swizzled K-major image the tensor cores read, relayout.cu), the group's B tile
+//     (three E4M3 activation terms x 8 or 16 tokens, 3 or 6 KB, pack_act.cu) and the block's
+//     scales (weight scale_inv entries and the tokens' activation scales, <= 96 B) into a
+//     ring of STAGES shared-memory stages; it runs ahead across item boundaries.
 //   warp 1, one lane: MMA issuer.  Per kb: 4 k-steps x MATS of
 //     tcgen05.mma.cta_group::1.kind::f8f6f4, M = 128 weight rows, N = 3 terms x 8/16 tokens,
 //     K = 32, into one of two TMEM accumulator buffers; tcgen05.commit frees the smem stage
 //     and signals the accumulator to the epilogue.
 //   warps 2-5: epilogue.  Each thread owns one weight row (its TMEM lane): per kb it loads the
-//     accumulator (tcgen05.ld), releases the buffer, and promotes
+//     accumulator (tcgen05.ld) and the stage's scales, releases both, and promotes
 //       acc[token] += (D[term0] + D[term1] + D[term2]) * scale_inv[rb, kb] * act_scale[token, kb]
 //     in fp32 -- the block-scaled algebra of dequantize-then-matmul (server/fp8_utils.py:4-39,
 //     server/moe_layer_runtime.py:604-609) with the scales applied once per 128x128 block.
-//     At the end of an item: up/gate -> h = silu(gate) * up (silu(g) = g / (1 + exp(-g))),
+//     At the end of an item: up/gate -> the raw up and gate partial sums of split ks,
 //     down -> y * routing weight, written per packed row in fp32 (coalesced along the rows).
 // TMEM: MATS x 48 fp32 columns per accumulator buffer, double-buffered (256 / 128 columns),
 // allocated by warp 2 and freed on every exit path.
@@ -42,17 +46,32 @@ struct TcShape {
     static constexpr int kABytes = MATS * 16384;                       // weight tile(s) per kb
     static constexpr int kBBytes = kMaxTilesPerGroup * kBTileBytes;     // 6 KB
     static constexpr int kStage = kABytes + kBBytes;                    // multiple of 1024
+    // per-stage scales: 16 B of each weight-scale row (kb rounded down to 4) + act scales
+    static constexpr int kScBytes = 128;
+    static constexpr int kScAct = 32;                                   // act scales at +32
     static constexpr int kColsPerBuf = MATS * 48;
     static constexpr uint32_t kTmemCols = MATS == 2 ? 256 : 128;
     static_assert(kStage % 1024 == 0, "stages must keep 1024-byte alignment");
 };
+
+// K split for this launch: enough (group, row block, split) items to keep every CTA busy
+// (at least 8 per CTA) while each item keeps a whole number of K blocks and the partial sums
+// fit the output buffer.  Every CTA computes the same value from the same inputs.
+__device__ __forceinline__ int choose_split(int base_items, int KB, int max_split, int n_rows, int out_rows) {
+    int S = 1;
+    while (S < max_split && base_items * S < 8 * int(gridDim.x) && KB % (2 * S) == 0 &&
+           int64_t(n_rows) * 2 * S <= out_rows)
+        S *= 2;
+    return S;
+}
 
 template <int MATS, int STAGES>
 __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     using S = TcShape<MATS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStage);
+    uint8_t* sc_base = smem + STAGES * S::kStage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sc_base + STAGES * S::kScBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -63,7 +82,7 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], 1 + 4);  // MMA commit + the four epilogue warps (scales read)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
@@ -79,7 +98,12 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int n_items = a.meta->n_groups * a.n_mb;
+    const int base_items = a.meta->n_groups * a.n_mb;
+    const int n_rows = a.meta->n_rows;
+    const int split = choose_split(base_items, a.KB, a.max_split, n_rows, a.out_rows);
+    const int KBs = a.KB / split;
+    const int n_items = base_items * split;
+    if (blockIdx.x == 0 && threadIdx.x == 0) a.meta->split_k = split;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -87,15 +111,24 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
             uint32_t it = 0;
             bool ok = true;
             for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-                const int gi = item / a.n_mb;
-                const int rb = item - gi * a.n_mb;
+                const int ks = item % split;
+                const int gm = item / split;
+                const int gi = gm / a.n_mb;
+                const int rb = gm - gi * a.n_mb;
                 const GroupRec gr = a.groups[gi];
                 const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
-                const uint8_t* A = a.arena + int64_t(gr.slot) * a.slot_bytes + a.a_off +
-                                   int64_t(rb) * a.KB * S::kABytes;
+                const uint8_t* slot = a.arena + int64_t(gr.slot) * a.slot_bytes;
+                const uint8_t* A = slot + a.a_off + int64_t(rb) * a.KB * S::kABytes;
                 const uint8_t* B = a.bfrag + int64_t(gr.tile_base) * a.KB * kBTileBytes;
+                // scale grids are 256-byte aligned; each stage takes the aligned 16 bytes that
+                // hold entry (rb, kb), so a row that starts off a 16-byte boundary still copies
+                const float* W0 = reinterpret_cast<const float*>(slot + a.s0_off);
+                const float* W1 = reinterpret_cast<const float*>(slot + a.s1_off);
+                const int64_t wrow = int64_t(rb) * a.scale_ld;
+                const float* X = a.bscale + int64_t(gr.tile_base) * a.KB * kTileCols;
                 const uint32_t bbytes = uint32_t(NT) * kBTileBytes;
-                for (int kb = 0; kb < a.KB; ++kb) {
+                const uint32_t xsb = uint32_t(NT) * kTileCols * 4;
+                for (int kb = ks * KBs; kb < (ks + 1) * KBs; ++kb) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) {
@@ -103,9 +136,14 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                         break;
                     }
                     uint8_t* st = smem + s * S::kStage;
-                    mbar_arrive_expect_tx(&full[s], S::kABytes + bbytes);
+                    uint8_t* sc = sc_base + s * S::kScBytes;
+                    mbar_arrive_expect_tx(&full[s], S::kABytes + bbytes + 16 * MATS + xsb);
                     tma_bulk_g2s(st, A + int64_t(kb) * S::kABytes, S::kABytes, &full[s]);
                     tma_bulk_g2s(st + S::kABytes, B + int64_t(kb) * bbytes, bbytes, &full[s]);
+                    const int64_t wi = (wrow + kb) & ~int64_t(3);
+                    tma_bulk_g2s(sc, W0 + wi, 16, &full[s]);
+                    if constexpr (MATS == 2) tma_bulk_g2s(sc + 16, W1 + wi, 16, &full[s]);
+                    tma_bulk_g2s(sc + S::kScAct, X + int64_t(kb) * NT * kTileCols, xsb, &full[s]);
                     ++it;
                 }
             }
@@ -120,11 +158,11 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
             bool ok = true;
             const uint32_t smem_base = smem_u32(smem);
             for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-                const int gi = item / a.n_mb;
+                const int gi = (item / split) / a.n_mb;
                 const GroupRec gr = a.groups[gi];
                 const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
                 const uint32_t idesc = umma_idesc_e4m3(128, kSplits * kTileCols * NT);
-                for (int kb = 0; kb < a.KB; ++kb) {
+                for (int kk = 0; kk < KBs; ++kk) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
                     const int b = it & 1;
@@ -160,24 +198,25 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
         uint32_t it = 0;
         bool ok = true;
         for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-            const int gi = item / a.n_mb;
-            const int rb = item - gi * a.n_mb;
+            const int ks = item % split;
+            const int gm = item / split;
+            const int gi = gm / a.n_mb;
+            const int rb = gm - gi * a.n_mb;
             const GroupRec gr = a.groups[gi];
             const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
-            const uint8_t* slot = a.arena + int64_t(gr.slot) * a.slot_bytes;
-            const float* ws0 = reinterpret_cast<const float*>(slot + a.s0_off) + int64_t(rb) * a.scale_ld;
-            const float* ws1 = reinterpret_cast<const float*>(slot + a.s1_off) + int64_t(rb) * a.scale_ld;
-            const float* xsc = a.bscale + int64_t(gr.tile_base) * a.KB * kTileCols;
             float acc[MATS][kGroupRows];
 #pragma unroll
             for (int m = 0; m < MATS; ++m)
 #pragma unroll
                 for (int t = 0; t < kGroupRows; ++t) acc[m][t] = 0.0f;
 
-            for (int kb = 0; kb < a.KB; ++kb) {
+            for (int kb = ks * KBs; kb < (ks + 1) * KBs; ++kb) {
+                const int s = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1u;
                 const int b = it & 1;
                 const uint32_t bph = (it >> 1) & 1u;
-                if (!mbar_wait(&tfull[b], bph, a.err)) {
+                // full[s] makes the stage's scales (written by the bulk copies) visible here
+                if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tfull[b], bph, a.err)) {
                     ok = false;
                     break;
                 }
@@ -190,58 +229,62 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                     tmem_ld16(base + m * 48 + 16, &d[m][16]);
                     tmem_ld16(base + m * 48 + 32, &d[m][32]);
                 }
+                // scales of this K block, from the stage
+                const float* sc = reinterpret_cast<const float*>(sc_base + s * S::kScBytes);
+                const int wl = int((int64_t(rb) * a.scale_ld + kb) & 3);
+                float wsc[MATS];
+                wsc[0] = sc[wl];
+                if constexpr (MATS == 2) wsc[1] = sc[4 + wl];
+                float xs[kGroupRows];
+#pragma unroll
+                for (int t = 0; t < kGroupRows; ++t) xs[t] = (t < NT * kTileCols) ? sc[S::kScAct / 4 + t] : 0.0f;
                 tmem_wait_ld();
 #pragma unroll
                 for (int m = 0; m < MATS; ++m) tmem_reg_fence(d[m]);
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[b]);
-
-                float wsc[MATS];
-                wsc[0] = __ldg(ws0 + kb);
-                if constexpr (MATS == 2) wsc[1] = __ldg(ws1 + kb);
-                const float* xs = xsc + int64_t(kb) * NT * kTileCols;
+                if (lane == 0) {
+                    mbar_arrive(&tempty[b]);
+                    mbar_arrive(&empty[s]);
+                }
                 if (NT == 1) {
 #pragma unroll
                     for (int t = 0; t < kTileCols; ++t) {
-                        const float sx = __ldg(xs + t);
 #pragma unroll
                         for (int m = 0; m < MATS; ++m) {
                             const float v = __uint_as_float(d[m][t]) + __uint_as_float(d[m][8 + t]) +
                                             __uint_as_float(d[m][16 + t]);
-                            acc[m][t] = fmaf(v, wsc[m] * sx, acc[m][t]);
+                            acc[m][t] = fmaf(v, wsc[m] * xs[t], acc[m][t]);
                         }
                     }
                 } else {
 #pragma unroll
                     for (int t = 0; t < kGroupRows; ++t) {
-                        const float sx = __ldg(xs + t);
 #pragma unroll
                         for (int m = 0; m < MATS; ++m) {
                             const float v = __uint_as_float(d[m][t]) + __uint_as_float(d[m][16 + t]) +
                                             __uint_as_float(d[m][32 + t]);
-                            acc[m][t] = fmaf(v, wsc[m] * sx, acc[m][t]);
+                            acc[m][t] = fmaf(v, wsc[m] * xs[t], acc[m][t]);
                         }
                     }
                 }
                 ++it;
             }
             if (!ok) break;
-            // fused epilogue: one weight row, every token of the group
+            // epilogue: one weight row, every token of the group (coalesced along the rows)
             const int orow = rb * kBlock + row;
 #pragma unroll
             for (int t = 0; t < kGroupRows; ++t) {
                 if (t < gr.n_rows) {
                     const int prow = gr.row_start + t;
-                    float v;
                     if constexpr (MATS == 2) {
-                        const float up = acc[0][t];
-                        const float gate = acc[1][t];
-                        v = (gate / (1.0f + expf(-gate))) * up;
+                        // raw split accumulators; the h packer adds the splits and applies SiLU
+                        float* o = a.out + (int64_t(ks) * n_rows + prow) * 2 * a.ld_out + orow;
+                        o[0] = acc[0][t];
+                        o[a.ld_out] = acc[1][t];
                     } else {
-                        v = acc[0][t] * a.row_weight[prow];
+                        a.out[int64_t(prow) * a.ld_out + orow] = acc[0][t] * a.row_weight[prow];
                     }
-                    a.out[int64_t(prow) * a.ld_out + orow] = v;
                 }
             }
         }
@@ -258,7 +301,8 @@ constexpr int kDownStages = 8;
 
 template <int MATS, int STAGES>
 size_t tc_smem_bytes() {
-    return size_t(STAGES) * TcShape<MATS>::kStage + 1024 /* alignment slack */ + 256 /* barriers */;
+    return size_t(STAGES) * (TcShape<MATS>::kStage + TcShape<MATS>::kScBytes) + 1024 /* alignment slack */ +
+           256 /* barriers */;
 }
 
 cudaError_t grouped_ffn_init_attributes() {

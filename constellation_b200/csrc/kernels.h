@@ -22,11 +22,11 @@ cudaError_t launch_dequant_fp8(const uint8_t* w, const float* s, float* out, int
                                int num_sms, cudaStream_t stream);
 
 // router.cu
-int router_k_split(int H);
+// `logits` receives the [T, E] fp32 logits (workspace, or the caller's aux output)
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
                           int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
-                          float* partial, int32_t* topk_idx, float* topk_w, float* logits_out,
-                          float* group_scores_out, cudaStream_t stream);
+                          float* logits, int32_t* topk_idx, float* topk_w, float* group_scores_out,
+                          cudaStream_t stream);
 
 // route_pack.cu
 struct PackArgs {
@@ -72,24 +72,33 @@ struct PackActArgs {
     uint8_t* bfrag;          // B fragments
     float* bscale;           // per (row, K block) scales
 };
+// src_dtype 4: `src` holds the up/gate kernel's split accumulators (meta->split_k splits of
+// meta->n_rows rows each); the packer adds the splits in order and applies
+// h = silu(gate) * up before quantizing.
+constexpr int kSrcUpGatePartials = 4;
 cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream);
 
 // grouped_ffn.cu
 struct FfnArgs {
     const uint8_t* arena;
     int64_t slot_bytes;
-    int64_t a_off;   // byte offset of this projection's chunks inside a slot
+    int64_t a_off;   // byte offset of this projection's tiles inside a slot
     int64_t s0_off;  // scale grid (up or down)
     int64_t s1_off;  // scale grid (gate), up/gate only
     int KB;          // K / 128
-    int n_mb;        // output rows / 64
+    int n_mb;        // output rows / 128
     int scale_ld;    // columns of the scale grid (= KB)
     const GroupRec* groups;
-    const PackMeta* meta;
+    PackMeta* meta;           // read: n_groups; written (block 0): the K split chosen
     const uint8_t* bfrag;
     const float* bscale;
-    float* out;               // h [rows, I] (up/gate) or y [rows, H] (down)
+    // up/gate: raw fp32 accumulators out[((split * n_rows + row) * 2 + mat) * ld_out + col],
+    //          n_rows = meta->n_rows
+    // down:    out[row * ld_out + col] = accumulator * row_weight[row]
+    float* out;
     int64_t ld_out;
+    int out_rows;             // up/gate: rows `out` holds (split * n_rows * 2 <= out_rows * 2)
+    int max_split;            // largest K split this launch may choose (1 = never split)
     const float* row_weight;  // down only
     int* err;
 };

@@ -67,6 +67,8 @@ struct PackMeta {
     int32_t n_groups;
     int32_t n_tiles;
     int32_t overflow;  // nonzero: the call exceeded the workspace capacity
+    int32_t split_k;   // K split the up/gate kernel chose (read by the h packer)
+    int32_t pad[3];
 };
 
 }  // namespace cst

@@ -1,5 +1,7 @@
-// Activation packer: rows of x (bf16 / fp16 / fp32) or of the SwiGLU intermediate h (fp32)
-// -> E4M3 tensor-core B fragments, three terms per element.
+// Activation packer: rows of x (bf16 / fp16 / fp32) or of the SwiGLU intermediate h -> E4M3
+// tensor-core B fragments, three terms per element.  For h the source is the up/gate
+// kernel's raw split accumulators: the packer adds the K splits in fixed order and applies
+// h = silu(gate) * up (server/moe_layer_runtime.py:604-609) while loading.
 //
 // The grouped FFN kernels multiply FP8 E4M3 weights by activations on the FP8 tensor
 // pipe.  One E4M3 term carries 4 significant bits, so each activation element v of a
@@ -27,12 +29,29 @@
 namespace cst {
 
 
-__device__ __forceinline__ void load4(const PackActArgs& a, int64_t src_row, int k, float (&v)[4]) {
+__device__ __forceinline__ void load4(const PackActArgs& a, int64_t src_row, int k, int split, float (&v)[4]) {
     if (src_row < 0) {
         v[0] = v[1] = v[2] = v[3] = 0.0f;
         return;
     }
-    if (a.src_dtype == 3) {
+    if (a.src_dtype == kSrcUpGatePartials) {
+        // up/gate split accumulators [split][n_rows][2][K]: add the splits in order, then
+        // h = silu(gate) * up with silu(g) = g / (1 + exp(-g))
+        const float* p = static_cast<const float*>(a.src) + src_row * 2 * a.ld + k;
+        const int64_t split_stride = int64_t(a.meta->n_rows) * 2 * a.ld;
+        float4 u = *reinterpret_cast<const float4*>(p);
+        float4 g = *reinterpret_cast<const float4*>(p + a.ld);
+        for (int ks = 1; ks < split; ++ks) {
+            const float4 u2 = *reinterpret_cast<const float4*>(p + ks * split_stride);
+            const float4 g2 = *reinterpret_cast<const float4*>(p + ks * split_stride + a.ld);
+            u.x += u2.x; u.y += u2.y; u.z += u2.z; u.w += u2.w;
+            g.x += g2.x; g.y += g2.y; g.z += g2.z; g.w += g2.w;
+        }
+        v[0] = (g.x / (1.0f + expf(-g.x))) * u.x;
+        v[1] = (g.y / (1.0f + expf(-g.y))) * u.y;
+        v[2] = (g.z / (1.0f + expf(-g.z))) * u.z;
+        v[3] = (g.w / (1.0f + expf(-g.w))) * u.w;
+    } else if (a.src_dtype == 3) {
         const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(a.src) + src_row * a.ld + k);
         v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
     } else if (a.src_dtype == 2) {
@@ -56,6 +75,7 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
     const int KB = a.K / kBlock;
     const int n_chunks = (KB + kPackKbPerTask - 1) / kPackKbPerTask;
     const int n_tiles = a.meta->n_tiles;
+    const int split = a.src_dtype == kSrcUpGatePartials ? a.meta->split_k : 1;
     const int lane = threadIdx.x & 31;
     const int64_t n_tasks = int64_t(n_tiles) * kTileCols * n_chunks;
     const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -82,7 +102,7 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
 #pragma unroll
         for (int i = 0; i < kPackKbPerTask; ++i) {
             if (kb0 + i < KB) {
-                load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, v[i]);
+                load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, split, v[i]);
             } else {
                 v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.0f;
             }

@@ -12,10 +12,9 @@
 //
 // Two kernels:
 //   router_logits_kernel: [T, H] x [E, H]^T in fp32 on CUDA cores (the router needs exact
-//     fp32 products; TF32 tensor cores would change which experts win).  32x32 output
-//     tiles, K split across gridDim.z into fixed slices; partial sums go to
-//     partial[z][T][E] and are added in z order by the select kernel, so results are
-//     bit-identical from run to run.
+//     fp32 products; TF32 tensor cores would change which experts win).  8-token x 8-expert
+//     tiles, one per CTA, K split over the CTA's warps and folded in a fixed order, so
+//     results are bit-identical from run to run; logits [T, E] are written once.
 //   router_select_kernel: one warp per token does the sigmoid / bias / group / top-k
 //     logic with warp-shuffle arg-max reductions.
 #include <cfloat>
@@ -38,135 +37,116 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return
 template <>
 __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
 
-constexpr int kRT = 32;   // tile edge (experts and tokens)
-constexpr int kRK = 128;  // K chunk per shared-memory step
-constexpr int kRKP = kRK + 4;
-
-// 16 consecutive activations of row `t` starting at column `k` (vector loads), as fp32.
+// 4 consecutive activations of one row as fp32 (8- or 16-byte vector load).
 template <typename TX>
-__device__ __forceinline__ void load16(const TX* x, int64_t off, float (&v)[16]);
+__device__ __forceinline__ float4 load4x(const TX* x, int64_t off);
 template <>
-__device__ __forceinline__ void load16<float>(const float* x, int64_t off, float (&v)[16]) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float4 f = *reinterpret_cast<const float4*>(x + off + 4 * i);
-        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-    }
+__device__ __forceinline__ float4 load4x<float>(const float* x, int64_t off) {
+    return __ldg(reinterpret_cast<const float4*>(x + off));
 }
 template <>
-__device__ __forceinline__ void load16<__nv_bfloat16>(const __nv_bfloat16* x, int64_t off, float (&v)[16]) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const uint4 u = *reinterpret_cast<const uint4*>(x + off + 8 * i);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
-            v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
-        }
-    }
+__device__ __forceinline__ float4 load4x<__nv_bfloat16>(const __nv_bfloat16* x, int64_t off) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(x + off));
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
 }
 template <>
-__device__ __forceinline__ void load16<__half>(const __half* x, int64_t off, float (&v)[16]) {
+__device__ __forceinline__ float4 load4x<__half>(const __half* x, int64_t off) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(x + off));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+constexpr int kLT = 8;       // tokens per CTA tile
+constexpr int kLE = 8;       // experts per CTA tile
+constexpr int kLWarps = 4;   // warps per CTA, each over a contiguous quarter of K
+
+// Butterfly half-exchange: after the step with offset o, each lane keeps the half of its
+// N values selected by lane bit o and adds the partner's copy of that half.
+template <int N>
+__device__ __forceinline__ void reduce_half(float* v, int o, int lane) {
+    const bool upper = (lane & o) != 0;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const uint4 u = *reinterpret_cast<const uint4*>(x + off + 8 * i);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
-            v[8 * i + 2 * j] = f.x;
-            v[8 * i + 2 * j + 1] = f.y;
-        }
+    for (int i = 0; i < N / 2; ++i) {
+        const float keep = upper ? v[i + N / 2] : v[i];
+        const float send = upper ? v[i] : v[i + N / 2];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
     }
 }
 
-// 32 experts x 32 tokens per CTA over one K slice, 128-wide chunks staged in shared
-// memory; the next chunk is fetched into registers while the current one is consumed.
+// logits[t][e] = sum_k x[t][k] * w[e][k] in fp32 for an 8-token x 8-expert tile per CTA.
+// Warp q sums k in [q H/4, (q+1) H/4) with lane l taking columns k = 4 l + 128 j: per step
+// one float4 of each expert row and 4 activations of each token row, 256 independent FMA.
+// The 64 per-lane sums are folded across the warp by a fixed butterfly (lane l ends with
+// outputs 2l and 2l+1) and the four warps' sums are added in warp order, so the result is
+// bit-identical from run to run.  No global scratch: the tile is written once.
 template <typename TX>
-__global__ void __launch_bounds__(256) router_logits_kernel(const TX* __restrict__ x, const float* __restrict__ w,
-                                                            float* __restrict__ partial, int T, int E, int H,
-                                                            int k_slice) {
-    __shared__ __align__(16) float xs[kRT][kRKP];
-    __shared__ __align__(16) float ws[kRT][kRKP];
-    const int e0 = blockIdx.x * kRT;
-    const int t0 = blockIdx.y * kRT;
-    const int kz = blockIdx.z;
-    const int k_begin = kz * k_slice;
-    const int tid = threadIdx.x;
-    const int tx = tid & 15;  // expert pair
-    const int ty = tid >> 4;  // token pair
-    const int lr = tid >> 3;         // staged row 0..31
-    const int lc = (tid & 7) * 16;   // staged column 0..112
-    const bool t_ok = (t0 + lr) < T;
-    const bool e_ok = (e0 + lr) < E;
-    const int64_t xoff = int64_t(t0 + lr) * H + lc;
-    const int64_t woff = int64_t(e0 + lr) * H + lc;
-    float rx[16], rw[16];
-    auto fetch = [&](int k0) {
-        if (t_ok) {
-            load16<TX>(x, xoff + k0, rx);
-        } else {
+__global__ void __launch_bounds__(kLWarps * 32) router_logits_kernel(const TX* __restrict__ x,
+                                                                     const float* __restrict__ w,
+                                                                     float* __restrict__ logits, int T, int E,
+                                                                     int H) {
+    __shared__ float s_part[kLWarps][kLT * kLE];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * kLT;
+    const int e0 = blockIdx.y * kLE;
+    const int quarter = H / kLWarps;
+    const int k_begin = warp * quarter;
+    const int k_end = k_begin + quarter;
+    float acc[kLT * kLE];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) rx[i] = 0.0f;
-        }
-        if (e_ok) {
-            load16<float>(w, woff + k0, rw);
-        } else {
+    for (int i = 0; i < kLT * kLE; ++i) acc[i] = 0.0f;
+    const TX* xr[kLT];
+    const float* wr[kLE];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) rw[i] = 0.0f;
-        }
-    };
-    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-    fetch(k_begin);
-    for (int k0 = k_begin; k0 < k_begin + k_slice; k0 += kRK) {
+    for (int t = 0; t < kLT; ++t) xr[t] = x + int64_t(min(t0 + t, T - 1)) * H;
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-            *reinterpret_cast<float4*>(&xs[lr][lc + i]) = make_float4(rx[i], rx[i + 1], rx[i + 2], rx[i + 3]);
-            *reinterpret_cast<float4*>(&ws[lr][lc + i]) = make_float4(rw[i], rw[i + 1], rw[i + 2], rw[i + 3]);
-        }
-        __syncthreads();
-        if (k0 + kRK < k_begin + k_slice) fetch(k0 + kRK);
-#pragma unroll 4
-        for (int c = 0; c < kRK; c += 4) {
-            const float4 x0 = *reinterpret_cast<const float4*>(&xs[2 * ty][c]);
-            const float4 x1 = *reinterpret_cast<const float4*>(&xs[2 * ty + 1][c]);
-            const float4 w0 = *reinterpret_cast<const float4*>(&ws[2 * tx][c]);
-            const float4 w1 = *reinterpret_cast<const float4*>(&ws[2 * tx + 1][c]);
-            const float xa[4] = {x0.x, x0.y, x0.z, x0.w}, xb[4] = {x1.x, x1.y, x1.z, x1.w};
-            const float wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+    for (int e = 0; e < kLE; ++e) wr[e] = w + int64_t(min(e0 + e, E - 1)) * H;
+    for (int k = k_begin + 4 * lane; k < k_end; k += 128) {
+        float4 wv[kLE], xv[kLT];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                acc[0][0] = fmaf(xa[j], wa[j], acc[0][0]);
-                acc[0][1] = fmaf(xa[j], wb[j], acc[0][1]);
-                acc[1][0] = fmaf(xb[j], wa[j], acc[1][0]);
-                acc[1][1] = fmaf(xb[j], wb[j], acc[1][1]);
+        for (int e = 0; e < kLE; ++e) wv[e] = __ldg(reinterpret_cast<const float4*>(wr[e] + k));
+#pragma unroll
+        for (int t = 0; t < kLT; ++t) xv[t] = load4x<TX>(xr[t], k);
+#pragma unroll
+        for (int t = 0; t < kLT; ++t) {
+#pragma unroll
+            for (int e = 0; e < kLE; ++e) {
+                float a = acc[t * kLE + e];
+                a = fmaf(xv[t].x, wv[e].x, a);
+                a = fmaf(xv[t].y, wv[e].y, a);
+                a = fmaf(xv[t].z, wv[e].z, a);
+                a = fmaf(xv[t].w, wv[e].w, a);
+                acc[t * kLE + e] = a;
             }
         }
-        __syncthreads();
     }
+    reduce_half<64>(acc, 16, lane);
+    reduce_half<32>(acc, 8, lane);
+    reduce_half<16>(acc, 4, lane);
+    reduce_half<8>(acc, 2, lane);
+    reduce_half<4>(acc, 1, lane);
+    s_part[warp][2 * lane] = acc[0];
+    s_part[warp][2 * lane + 1] = acc[1];
+    __syncthreads();
+    if (threadIdx.x < kLT * kLE) {
+        const int o = threadIdx.x;
+        float sum = s_part[0][o];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int t = t0 + 2 * ty + i;
-        if (t >= T) continue;
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int e = e0 + 2 * tx + j;
-            if (e < E) partial[(int64_t(kz) * T + t) * E + e] = acc[i][j];
-        }
+        for (int q = 1; q < kLWarps; ++q) sum += s_part[q][o];
+        const int t = t0 + o / kLE, e = e0 + o % kLE;
+        if (t < T && e < E) logits[int64_t(t) * E + e] = sum;
     }
 }
 
 struct RouterArgs {
-    const float* partial;   // [kz][T][E]
-    int kz;
+    const float* logits;    // [T][E]
     const float* bias;      // [E]
     const uint8_t* resident;  // [E] or null (all resident)
     int T, E, n_group, topk_group, top_k, norm;
     float scale;
     int32_t* topk_idx;      // [T, top_k]
     float* topk_w;          // [T, top_k]
-    float* logits_out;      // [T, E] or null
     float* group_scores_out;  // [T, n_group] or null
 };
 
@@ -210,8 +190,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(RouterArg
     if (t >= a.T) return;
     const int E = a.E;
     const int epg = E / a.n_group;
-    const int64_t zstride = int64_t(a.T) * E;
-    const float* __restrict__ part = a.partial + int64_t(t) * E;
+    const float* __restrict__ lg = a.logits + int64_t(t) * E;
     float ch[EPL];
     int grp[EPL];
 #pragma unroll
@@ -220,15 +199,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(RouterArg
         ch[i] = -INFINITY;
         grp[i] = 0x7fffffff;
         if (e < E) {
-            // independent read-only loads, then the fixed-order sum over the K slices
-            float p[8];
-#pragma unroll
-            for (int z = 0; z < 8; ++z) p[z] = (z < a.kz) ? __ldg(part + z * zstride + e) : 0.0f;
-            float l = 0.0f;
-#pragma unroll
-            for (int z = 0; z < 8; ++z)
-                if (z < a.kz) l += p[z];
-            if (a.logits_out) a.logits_out[int64_t(t) * E + e] = l;
+            const float l = __ldg(lg + e);
             const float sg = 1.0f / (1.0f + expf(-l));
             const bool res = (a.resident == nullptr) || (a.resident[e] != 0);
             ch[i] = res ? (sg + a.bias[e]) : -INFINITY;
@@ -314,34 +285,24 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(RouterArg
     }
 }
 
-int router_k_split(int H) {
-    const int chunks = H / kRK;
-    for (int z : {8, 4, 2}) {
-        if (chunks % z == 0) return z;
-    }
-    return 1;
-}
-
-// x_dtype: 1 fp16, 2 bf16, 3 fp32.  partial needs k_split * T * E floats.
+// x_dtype: 1 fp16, 2 bf16, 3 fp32.  `logits` receives [T, E] fp32 (scratch or the caller's).
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
                           int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
-                          float* partial, int32_t* topk_idx, float* topk_w, float* logits_out,
-                          float* group_scores_out, cudaStream_t stream) {
-    const int kz = router_k_split(H);
-    dim3 grid((E + kRT - 1) / kRT, (T + kRT - 1) / kRT, kz);
-    const int k_slice = H / kz;
+                          float* logits, int32_t* topk_idx, float* topk_w, float* group_scores_out,
+                          cudaStream_t stream) {
+    const dim3 grid((T + kLT - 1) / kLT, (E + kLE - 1) / kLE);
     if (x_dtype == 2) {
-        router_logits_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(x), w, partial, T, E, H, k_slice);
+        router_logits_kernel<__nv_bfloat16><<<grid, kLWarps * 32, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), w, logits, T, E, H);
     } else if (x_dtype == 1) {
-        router_logits_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(x), w, partial, T, E, H,
-                                                               k_slice);
+        router_logits_kernel<__half><<<grid, kLWarps * 32, 0, stream>>>(static_cast<const __half*>(x), w, logits, T,
+                                                                         E, H);
     } else {
-        router_logits_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(x), w, partial, T, E, H,
-                                                              k_slice);
+        router_logits_kernel<float><<<grid, kLWarps * 32, 0, stream>>>(static_cast<const float*>(x), w, logits, T, E,
+                                                                        H);
     }
-    RouterArgs a{partial, kz, bias, resident, T, E, n_group, topk_group, top_k, norm, scale,
-                 topk_idx, topk_w, logits_out, group_scores_out};
+    RouterArgs a{logits, bias, resident, T, E, n_group, topk_group, top_k, norm, scale,
+                 topk_idx, topk_w, group_scores_out};
     const int grid_sel = (T + kSelWarps - 1) / kSelWarps;
     if (E <= 256) {
         router_select_kernel<8><<<grid_sel, kSelWarps * 32, 0, stream>>>(a);
@@ -357,8 +318,9 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
 // Some callers of this library cannot call cudaMalloc: a host runtime that has handed all
 // device memory to its own pool before loading the library, code that runs while another
 // component owns the allocator, or a process that must not grow its footprint after
-// start-up.  They still need the router, whose logits kernel writes its K-split partial
-// sums ([kz, T, E] fp32) to global scratch that cst_create would otherwise allocate.
+// start-up.  They still need the router, whose logits kernel writes the [T, E] fp32 logits
+// to global scratch that the select kernel reads and that cst_create would otherwise
+// allocate.
 // This variant keeps that scratch in the file-scope array below instead.  The array is
 // part of the library image: every GPU that loads the library holds it (2 MiB) until the
 // process exits.  Host code cannot use the array's name as a device address, so the first
@@ -395,14 +357,13 @@ extern "C" int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int3
     if (topk_group <= 0 || topk_group > n_group) return set_last_error(3, "invalid topk_group=%d", topk_group);
     if (top_k <= 0 || top_k > 15 || top_k > n_experts) return set_last_error(3, "invalid top_k=%d", top_k);
     if (T < 0) return set_last_error(3, "T=%d < 0", T);
-    const int kz = router_k_split(hidden);
-    const int64_t need = int64_t(kz) * T * n_experts;
+    const int64_t need = int64_t(T) * n_experts;
     if (need > kNoAllocScratchFloats)
         return set_last_error(3,
-                              "cst_route_noalloc: T * n_experts * %d = %lld scratch floats exceed the static "
+                              "cst_route_noalloc: T * n_experts = %lld scratch floats exceed the static "
                               "maximum of %lld (T <= %lld for n_experts = %d); use cst_route",
-                              kz, static_cast<long long>(need), static_cast<long long>(kNoAllocScratchFloats),
-                              static_cast<long long>(kNoAllocScratchFloats / (int64_t(kz) * n_experts)), n_experts);
+                              static_cast<long long>(need), static_cast<long long>(kNoAllocScratchFloats),
+                              static_cast<long long>(kNoAllocScratchFloats / n_experts), n_experts);
     if (T == 0) return 0;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
@@ -421,7 +382,7 @@ extern "C" int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int3
     }
     const cudaError_t e = launch_router(x, x_dtype, gate_weight, bias, resident, T, n_experts, hidden, n_group,
                                         topk_group, top_k, norm_topk_prob, routed_scaling_factor, scratch, topk_idx,
-                                        topk_weight, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+                                        topk_weight, nullptr, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return set_last_error(5, "router launch failed: %s", cudaGetErrorString(e));
     return 0;
 }

@@ -11,9 +11,11 @@ shared expert to its own tokens.
 Two exchange strategies, both deterministic and both behind ``ExpertParallelMoE.forward``:
 
 ``allgather`` (default for decode)
-    all-gather the tokens and their routes, run the rank's own experts on every row routed
-    to them (routes to other ranks' experts are skipped by the packer), reduce-scatter the
-    fp32 partial sums back to the owning ranks, add the shared expert.  Message sizes are
+    all-gather the tokens; every rank routes the whole gathered batch itself (the router is
+    deterministic and its inputs are identical everywhere, so no routes are exchanged), runs
+    its own experts on every row routed to them (routes to other ranks' experts are skipped
+    by the packer) plus the shared expert on its own tokens in the same grouped launches,
+    and reduce-scatters the fp32 partial sums back to the owning ranks.  Message sizes are
     fixed, so nothing waits on the host.  At decode batch the bytes match the all-to-all
     (T x H in, T x H x 4 back) because top_k equals the rank count at 8 GPUs.
 
@@ -72,6 +74,14 @@ class ExpertParallelMoE:
         self.E = n_routed_experts
         self.epr = n_routed_experts // world
         self._slot_map = None
+        #: set to a list to record (phase, CUDA event) pairs at the phase boundaries of forward()
+        self.timeline: list | None = None
+
+    def _mark(self, name: str) -> None:
+        if self.timeline is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.timeline.append((name, ev))
 
     # ------------------------------------------------------------------------------
     def slot_map(self, device) -> torch.Tensor:
@@ -84,35 +94,46 @@ class ExpertParallelMoE:
     def forward(self, x_local: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor, *,
                 residual: torch.Tensor | None = None, resident: torch.Tensor | None = None,
                 out_dtype: torch.dtype | None = None) -> torch.Tensor:
-        topk_idx, topk_w = self.c.route(x_local, gate_weight, bias, resident=resident)
         od = out_dtype or x_local.dtype
         Tl = x_local.shape[0]
+        self._mark("start")
         if self.world == 1:
+            topk_idx, topk_w = self.c.route(x_local, gate_weight, bias, resident=resident)
+            self._mark("route")
             if residual is None:
-                return self.c.moe_routed_range(x_local, topk_idx, topk_w, 0, Tl, out_dtype=od)
-            part = self.c.moe_routed_range(x_local, topk_idx, topk_w, 0, Tl, out_dtype=torch.float32)
-            return self.c.cast_extra(part, residual=residual, out_dtype=od)
+                out = self.c.moe_routed_range(x_local, topk_idx, topk_w, 0, Tl, out_dtype=od)
+            else:
+                part = self.c.moe_routed_range(x_local, topk_idx, topk_w, 0, Tl, out_dtype=torch.float32)
+                out = self.c.cast_extra(part, residual=residual, out_dtype=od)
+            self._mark("experts")
+            return out
         if self.mode == "allgather":
-            return self._allgather(x_local, topk_idx, topk_w, residual, od)
+            return self._allgather(x_local, gate_weight, bias, resident, residual, od)
+        topk_idx, topk_w = self.c.route(x_local, gate_weight, bias, resident=resident)
+        self._mark("route")
         return self._alltoall(x_local, topk_idx, topk_w, residual, od)
 
     # ------------------------------------------------------------------------------
-    def _allgather(self, x_local, topk_idx, topk_w, residual, od) -> torch.Tensor:
-        Tl, K = topk_idx.shape
-        H = x_local.shape[1]
+    def _allgather(self, x_local, gate_weight, bias, resident, residual, od) -> torch.Tensor:
+        Tl, H = x_local.shape
         x_all = torch.empty((self.world * Tl, H), dtype=x_local.dtype, device=x_local.device)
         dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
-        meta = torch.cat([topk_idx.to(torch.int32), topk_w.view(torch.int32)], dim=1).contiguous()
-        meta_all = torch.empty((self.world * Tl, 2 * K), dtype=torch.int32, device=x_local.device)
-        dist.all_gather_into_tensor(meta_all, meta, group=self.group)
-        idx_all = meta_all[:, :K].contiguous()
-        w_all = meta_all[:, K:].contiguous().view(torch.float32)
+        self._mark("all_gather")
+        # Every rank routes the whole gathered batch itself: the router is deterministic and
+        # its inputs are identical on all ranks, so all ranks agree on every route without
+        # exchanging them.
+        idx_all, w_all = self.c.route(x_all, gate_weight, bias, resident=resident)
+        self._mark("route")
         # this rank's experts on every gathered row, the shared expert on its own tokens only
         lo = self.rank * Tl
         partial = self.c.moe_routed_range(x_all, idx_all, w_all, lo, lo + Tl, out_dtype=torch.float32)
+        self._mark("experts")
         mine = torch.empty((Tl, H), dtype=torch.float32, device=x_local.device)
         dist.reduce_scatter_tensor(mine, partial, op=dist.ReduceOp.SUM, group=self.group)
-        return self.c.cast_extra(mine, residual=residual, out_dtype=od)
+        self._mark("reduce_scatter")
+        out = self.c.cast_extra(mine, residual=residual, out_dtype=od)
+        self._mark("cast")
+        return out
 
     def _alltoall(self, x_local, topk_idx, topk_w, residual, od) -> torch.Tensor:
         Tl, K = topk_idx.shape

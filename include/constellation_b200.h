@@ -129,11 +129,11 @@ int cst_route(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, const flo
  * already handed the device memory to its own pool, code running while another component
  * owns the allocator, or a process that must not grow after start-up -- and therefore
  * cannot create a context.  The caller passes every input and output (device pointers,
- * same meaning as cst_route plus the router hyper-parameters); the router's scratch (its
- * K-split partial logits) lives in a 2 MiB static device array inside this library,
+ * same meaning as cst_route plus the router hyper-parameters); the router's scratch (the
+ * [T, n_experts] fp32 logits) lives in a 2 MiB static device array inside this library,
  * which every GPU that loads the library holds until the process exits.  Limit:
- * kz * T * n_experts <= 524288 floats, where kz = 8 for hidden = 7168 -- T <= 256 at 256
- * experts; larger calls return CST_ERR_INVALID_ARG with a message naming the limit.
+ * T * n_experts <= 524288 floats -- T <= 2048 at 256 experts; larger calls return
+ * CST_ERR_INVALID_ARG with a message naming the limit.
  * The first call on a device looks the array's device address up (cudaGetSymbolAddress
  * with that device current) and caches it, so make that first call before any stream
  * capture.  All calls share the one array: calls that overlap on the GPU (other streams,

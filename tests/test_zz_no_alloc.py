@@ -58,7 +58,7 @@ def test_route_noalloc_rejects_sizes_beyond_its_static_scratch():
     from constellation_b200 import _lib
 
     dev = torch.device("cuda", 0)
-    T = 257  # 8 * 257 * 256 floats > 2 MiB
+    T = 2049  # 2049 * 256 floats > 2 MiB
     x = torch.zeros((T, H), dtype=torch.bfloat16, device=dev)
     w = torch.zeros((E, H), dtype=torch.float32, device=dev)
     b = torch.zeros(E, dtype=torch.float32, device=dev)
@@ -66,4 +66,4 @@ def test_route_noalloc_rejects_sizes_beyond_its_static_scratch():
     wt = torch.empty((T, K), dtype=torch.float32, device=dev)
     rc = _noalloc(_lib.lib, x, w, b, T, idx, wt, torch.cuda.current_stream(dev).cuda_stream)
     assert rc == _lib.CST_ERR_INVALID_ARG
-    assert "T <= 256" in _lib.last_error()
+    assert "T <= 2048" in _lib.last_error()
