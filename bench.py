@@ -145,9 +145,11 @@ def setup_layer(torch, rank, world, T_total, dev, resident=E):
     return ctx, gw, gb, x, x_all
 
 
-def touched_experts(torch, ctx, gw, gb, x_all):
+def touched_experts(torch, ctx, gw, gb, x_all, resident=E):
+    """Distinct routed experts the batch reaches among those with weights on the device."""
     idx, _ = ctx.route(x_all, gw, gb)
-    return int(torch.unique(idx).numel())
+    u = torch.unique(idx)
+    return int((u < resident).sum().item())
 
 
 def run_ours(args):
@@ -272,7 +274,7 @@ def run_ours(args):
         ep_phase_ms = {k: round(v / nprof, 4) for k, v in sums.items()}
 
     # algorithmic bytes of the grouped kernels on this rank
-    U_total = touched_experts(torch, ctx, gw, gb, x_all) if world == 1 else None
+    U_total = touched_experts(torch, ctx, gw, gb, x_all, args.resident_experts) if world == 1 else None
     if world > 1:
         idx, _ = ctx.route(x_all, gw, gb)
         lo, hi = rank * (E // world), (rank + 1) * (E // world)

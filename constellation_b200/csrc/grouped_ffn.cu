@@ -8,8 +8,9 @@
 // packed activation rows of one expert slot (route_pack.cu).  The K split S (1, 2 or 4) is
 // chosen on the device from the group count so that small decode batches still give every
 // SM several items; up/gate then writes S raw partial sums that the h packer adds in fixed
-// order (pack_act.cu), the down projection never splits.  One persistent CTA per SM walks
-// the item list with 6 warps:
+// order (pack_act.cu), the down projection never splits; instead a down item takes two
+// consecutive 128-row blocks when H / 128 is even, so both projections stream 32 KB of
+// weights per K block.  One persistent CTA per SM walks the item list with 6 warps:
 //   warp 0, one lane: TMA producer.  Per 128-wide K block kb it bulk-copies the weight tile
 //     (16 KB per matrix: up+gate = 32 KB, down = 16 KB; contiguous in the arena and already in
 //     the swizzled K-major image the tensor cores read, relayout.cu), the group's B tile
@@ -18,7 +19,7 @@
 //     ring of STAGES shared-memory stages; it runs ahead across item boundaries.
 //   warp 1, one lane: MMA issuer.  Per kb: 4 k-steps x MATS of
 //     tcgen05.mma.cta_group::1.kind::f8f6f4, M = 128 weight rows, N = 3 terms x 8/16 tokens,
-//     K = 32, into one of two TMEM accumulator buffers; tcgen05.commit frees the smem stage
+//     K = 32, into one of four TMEM accumulator buffers; tcgen05.commit frees the smem stage
 //     and signals the accumulator to the epilogue.
 //   warps 2-5: epilogue.  Each thread owns one weight row (its TMEM lane): per kb it loads the
 //     accumulator (tcgen05.ld) and the stage's scales, releases both, and promotes
@@ -27,7 +28,7 @@
 //     server/moe_layer_runtime.py:604-609) with the scales applied once per 128x128 block.
 //     At the end of an item: up/gate -> the raw up and gate partial sums of split ks,
 //     down -> y * routing weight, written per packed row in fp32 (coalesced along the rows).
-// TMEM: MATS x 48 fp32 columns per accumulator buffer, double-buffered (256 / 128 columns),
+// TMEM: MATS x 48 fp32 columns per accumulator buffer, four buffers (512 / 256 columns),
 // allocated by warp 2 and freed on every exit path.
 //
 // Every mbarrier wait is bounded (cst_common.cuh).  On a timeout the role records the
@@ -50,7 +51,11 @@ struct TcShape {
     static constexpr int kScBytes = 128;
     static constexpr int kScAct = 32;                                   // act scales at +32
     static constexpr int kColsPerBuf = MATS * 48;
-    static constexpr uint32_t kTmemCols = MATS == 2 ? 256 : 128;
+    // four accumulator buffers let the MMA issuer run up to four K blocks ahead of the
+    // epilogue (4 x 96 -> 512 columns for two accumulators, 4 x 48 -> 256 for one)
+    static constexpr int kTmemBufs = 4;
+    static constexpr uint32_t kTmemCols = MATS == 2 ? 512 : 256;
+    static_assert(kTmemBufs * kColsPerBuf <= int(kTmemCols), "accumulators exceed the TMEM allocation");
     static_assert(kStage % 1024 == 0, "stages must keep 1024-byte alignment");
 };
 
@@ -65,7 +70,10 @@ __device__ __forceinline__ int choose_split(int base_items, int KB, int max_spli
     return S;
 }
 
-template <int MATS, int STAGES>
+// MATS accumulators per item: up/gate (DOWN false) -> mat 0 = w_up, mat 1 = w_gate of one
+// 128-row block; down (DOWN true) -> MATS consecutive 128-row blocks of w_down (so the down
+// projection streams 32 KB per K block too when its row-block count is even).
+template <int MATS, int STAGES, bool DOWN>
 __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     using S = TcShape<MATS>;
     extern __shared__ uint8_t smem_raw[];
@@ -74,8 +82,8 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(sc_base + STAGES * S::kScBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
-    uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* tempty = tfull + S::kTmemBufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + S::kTmemBufs);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
@@ -84,7 +92,7 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1 + 4);  // MMA commit + the four epilogue warps (scales read)
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < S::kTmemBufs; ++b) {
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 4);
         }
@@ -118,13 +126,14 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 const GroupRec gr = a.groups[gi];
                 const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
                 const uint8_t* slot = a.arena + int64_t(gr.slot) * a.slot_bytes;
-                const uint8_t* A = slot + a.a_off + int64_t(rb) * a.KB * S::kABytes;
+                // up/gate: [rb][kb][up | gate] 32 KB per kb; down: [rb][kb] 16 KB per kb
+                const uint8_t* A = slot + a.a_off + int64_t(DOWN ? rb * MATS : rb) * a.KB * (DOWN ? 16384 : S::kABytes);
                 const uint8_t* B = a.bfrag + int64_t(gr.tile_base) * a.KB * kBTileBytes;
                 // scale grids are 256-byte aligned; each stage takes the aligned 16 bytes that
                 // hold entry (rb, kb), so a row that starts off a 16-byte boundary still copies
                 const float* W0 = reinterpret_cast<const float*>(slot + a.s0_off);
                 const float* W1 = reinterpret_cast<const float*>(slot + a.s1_off);
-                const int64_t wrow = int64_t(rb) * a.scale_ld;
+                const int64_t wrow = int64_t(DOWN ? rb * MATS : rb) * a.scale_ld;
                 const float* X = a.bscale + int64_t(gr.tile_base) * a.KB * kTileCols;
                 const uint32_t bbytes = uint32_t(NT) * kBTileBytes;
                 const uint32_t xsb = uint32_t(NT) * kTileCols * 4;
@@ -138,11 +147,20 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                     uint8_t* st = smem + s * S::kStage;
                     uint8_t* sc = sc_base + s * S::kScBytes;
                     mbar_arrive_expect_tx(&full[s], S::kABytes + bbytes + 16 * MATS + xsb);
-                    tma_bulk_g2s(st, A + int64_t(kb) * S::kABytes, S::kABytes, &full[s]);
+                    if constexpr (DOWN) {
+#pragma unroll
+                        for (int m = 0; m < MATS; ++m)
+                            tma_bulk_g2s(st + m * 16384, A + (int64_t(m) * a.KB + kb) * 16384, 16384, &full[s]);
+                    } else {
+                        tma_bulk_g2s(st, A + int64_t(kb) * S::kABytes, S::kABytes, &full[s]);
+                    }
                     tma_bulk_g2s(st + S::kABytes, B + int64_t(kb) * bbytes, bbytes, &full[s]);
-                    const int64_t wi = (wrow + kb) & ~int64_t(3);
-                    tma_bulk_g2s(sc, W0 + wi, 16, &full[s]);
-                    if constexpr (MATS == 2) tma_bulk_g2s(sc + 16, W1 + wi, 16, &full[s]);
+#pragma unroll
+                    for (int m = 0; m < MATS; ++m) {
+                        // down: scale row of block rb*MATS+m; up/gate: the same row of two grids
+                        const int64_t wi = (wrow + (DOWN ? m * a.scale_ld : 0) + kb) & ~int64_t(3);
+                        tma_bulk_g2s(sc + 16 * m, (DOWN || m == 0 ? W0 : W1) + wi, 16, &full[s]);
+                    }
                     tma_bulk_g2s(sc + S::kScAct, X + int64_t(kb) * NT * kTileCols, xsb, &full[s]);
                     ++it;
                 }
@@ -165,8 +183,8 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 for (int kk = 0; kk < KBs; ++kk) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
-                    const int b = it & 1;
-                    const uint32_t bph = (it >> 1) & 1u;
+                    const int b = it % S::kTmemBufs;
+                    const uint32_t bph = (it / S::kTmemBufs) & 1u;
                     if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tempty[b], bph ^ 1u, a.err)) {
                         ok = false;
                         break;
@@ -188,7 +206,7 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 }
             }
             // the MMAs issued last must have finished before TMEM is released
-            if (it > 0) mbar_wait(&tfull[(it - 1) & 1], ((it - 1) >> 1) & 1u, a.err);
+            if (it > 0) mbar_wait(&tfull[(it - 1) % S::kTmemBufs], ((it - 1) / S::kTmemBufs) & 1u, a.err);
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
@@ -213,8 +231,8 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
             for (int kb = ks * KBs; kb < (ks + 1) * KBs; ++kb) {
                 const int s = it % STAGES;
                 const uint32_t ph = (it / STAGES) & 1u;
-                const int b = it & 1;
-                const uint32_t bph = (it >> 1) & 1u;
+                const int b = it % S::kTmemBufs;
+                const uint32_t bph = (it / S::kTmemBufs) & 1u;
                 // full[s] makes the stage's scales (written by the bulk copies) visible here
                 if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tfull[b], bph, a.err)) {
                     ok = false;
@@ -231,10 +249,12 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 }
                 // scales of this K block, from the stage
                 const float* sc = reinterpret_cast<const float*>(sc_base + s * S::kScBytes);
-                const int wl = int((int64_t(rb) * a.scale_ld + kb) & 3);
                 float wsc[MATS];
-                wsc[0] = sc[wl];
-                if constexpr (MATS == 2) wsc[1] = sc[4 + wl];
+#pragma unroll
+                for (int m = 0; m < MATS; ++m) {
+                    const int64_t wr = int64_t(DOWN ? rb * MATS + m : rb) * a.scale_ld;
+                    wsc[m] = sc[4 * m + int((wr + kb) & 3)];
+                }
                 float xs[kGroupRows];
 #pragma unroll
                 for (int t = 0; t < kGroupRows; ++t) xs[t] = (t < NT * kTileCols) ? sc[S::kScAct / 4 + t] : 0.0f;
@@ -272,18 +292,20 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
             }
             if (!ok) break;
             // epilogue: one weight row, every token of the group (coalesced along the rows)
-            const int orow = rb * kBlock + row;
 #pragma unroll
             for (int t = 0; t < kGroupRows; ++t) {
                 if (t < gr.n_rows) {
                     const int prow = gr.row_start + t;
-                    if constexpr (MATS == 2) {
+                    if constexpr (!DOWN) {
                         // raw split accumulators; the h packer adds the splits and applies SiLU
-                        float* o = a.out + (int64_t(ks) * n_rows + prow) * 2 * a.ld_out + orow;
+                        float* o = a.out + (int64_t(ks) * n_rows + prow) * 2 * a.ld_out + rb * kBlock + row;
                         o[0] = acc[0][t];
                         o[a.ld_out] = acc[1][t];
                     } else {
-                        a.out[int64_t(prow) * a.ld_out + orow] = acc[0][t] * a.row_weight[prow];
+                        const float rw = a.row_weight[prow];
+#pragma unroll
+                        for (int m = 0; m < MATS; ++m)
+                            a.out[int64_t(prow) * a.ld_out + (rb * MATS + m) * kBlock + row] = acc[m][t] * rw;
                     }
                 }
             }
@@ -306,20 +328,31 @@ size_t tc_smem_bytes() {
 }
 
 cudaError_t grouped_ffn_init_attributes() {
-    cudaError_t e = cudaFuncSetAttribute(grouped_ffn_tc_kernel<2, kUpGateStages>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const cudaFuncAttribute attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    cudaError_t e = cudaFuncSetAttribute(grouped_ffn_tc_kernel<2, kUpGateStages, false>, attr,
                                          int(tc_smem_bytes<2, kUpGateStages>()));
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(grouped_ffn_tc_kernel<1, kDownStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(tc_smem_bytes<1, kDownStages>()));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(grouped_ffn_tc_kernel<2, kUpGateStages, true>, attr,
+                                 int(tc_smem_bytes<2, kUpGateStages>()));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(grouped_ffn_tc_kernel<1, kDownStages, true>, attr,
+                                 int(tc_smem_bytes<1, kDownStages>()));
+    return e;
 }
 
+// up/gate: a.n_mb = I / 128 row blocks.  down: a.n_mb = H / 128 row blocks; pairs of blocks per
+// item when that count is even (32 KB of weights per stage, as up/gate), else one.
 cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream) {
     if (upgate) {
-        grouped_ffn_tc_kernel<2, kUpGateStages>
+        grouped_ffn_tc_kernel<2, kUpGateStages, false>
             <<<num_sms, 192, tc_smem_bytes<2, kUpGateStages>(), stream>>>(a);
+    } else if (a.n_mb % 2 == 0) {
+        FfnArgs p = a;
+        p.n_mb = a.n_mb / 2;
+        grouped_ffn_tc_kernel<2, kUpGateStages, true>
+            <<<num_sms, 192, tc_smem_bytes<2, kUpGateStages>(), stream>>>(p);
     } else {
-        grouped_ffn_tc_kernel<1, kDownStages><<<num_sms, 192, tc_smem_bytes<1, kDownStages>(), stream>>>(a);
+        grouped_ffn_tc_kernel<1, kDownStages, true><<<num_sms, 192, tc_smem_bytes<1, kDownStages>(), stream>>>(a);
     }
     return cudaGetLastError();
 }
