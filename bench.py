@@ -56,6 +56,9 @@ def parse():
     p.add_argument("--cpu-sample-tokens", type=int, default=2)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=["config2", "config1"], default="config2",
+                   help="config2: the full layer (default); config1: grouped FP8 expert matvec only, "
+                        "32 resident experts with n_e ~ U{1..16} rows each, 1 GPU")
     p.add_argument("--resident-experts", type=int, default=E,
                    help="upload only the first N routed experts of each rank (small profiling case; "
                         "routes to the others contribute nothing)")
@@ -354,6 +357,208 @@ def run_ours(args):
 
 
 # ---------------------------------------------------------------------------------------
+C1_EXPERTS = 32
+
+
+def config1_rows(torch, seed=0):
+    """Config 1's seeded batch: n_e ~ U{1..16} rows for each of the 32 experts, rows of
+    one expert contiguous, bf16 N(0, 1) activations, routing weights U(0.05, 0.3)."""
+    g = torch.Generator().manual_seed(seed)
+    n_e = torch.randint(1, 17, (C1_EXPERTS,), generator=g)
+    row_slot = torch.repeat_interleave(torch.arange(C1_EXPERTS, dtype=torch.int32), n_e)
+    R = int(n_e.sum())
+    x = torch.randn((R, H), generator=g).to(torch.bfloat16)
+    w = 0.05 + 0.25 * torch.rand((R,), generator=g)
+    return n_e, row_slot, x, w
+
+
+def config1_bytes(R):
+    """Algorithmic bytes of one config-1 call: every resident expert's weights and scales
+    once, plus the bf16 rows read and the fp32 weighted rows written."""
+    return C1_EXPERTS * EXPERT_BYTES + R * (H * 2 + H * 4)
+
+
+def run_config1(args):
+    import torch
+
+    from constellation_b200 import synthetic
+    from constellation_b200.context import ExpertContext, MoEConfig
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1 or args.gpus != 1:
+        raise SystemExit("--workload config1 is a single-GPU configuration")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_e, row_slot_h, x_h, w_h = config1_rows(torch)
+    R = x_h.shape[0]
+    ctx = ExpertContext(dev, MoEConfig(), n_slots=C1_EXPERTS, max_tokens=64, max_rows=max(R, 64 * (K + 1)))
+    for j in range(C1_EXPERTS):
+        ex = synthetic.make_expert(H, I, seed=1000 + j, device=dev)
+        ctx.upload_expert(j, j, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
+        del ex
+    x = x_h.to(dev)
+    row_slot = row_slot_h.to(dev)
+    rw = w_h.to(dev)
+    y = torch.empty((R, H), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+
+    def step():
+        ctx.grouped_ffn(x, row_slot, rw, out=y)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    graph = None
+    if not args.no_graph:
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+    run = graph.replay if graph is not None else step
+
+    def timed(fn, k):
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(k):
+            fn()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b)
+
+    with ClockSampler(0) as clk:
+        ms_step = timed(run, args.steps) / args.steps
+    clocks = clk.summary()
+    nbytes = config1_bytes(R)
+    value = nbytes / (ms_step / 1e3) / 1e9
+
+    x_host = x_h.pin_memory()
+    y_host = torch.empty((R, H), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        x.copy_(x_host, non_blocking=True)
+        run()
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    ms_e2e = timed(e2e_step, args.steps) / args.steps
+
+    ctx.profile(True)
+    for _ in range(10):
+        step()
+    torch.cuda.synchronize(dev)
+    stages = ctx.profile_read()
+    ctx.profile(False)
+    stage_ms = {k: statistics.mean(st[k] for st in stages) for k in stages[0]}
+    upg_ms, dn_ms = stage_ms["grouped_up_gate"], stage_ms["grouped_down"]
+    grid = (I // 128) * (H // 128) * 4
+    upg_bytes = C1_EXPERTS * (2 * I * H + 2 * grid) + R * (H * 2 + I * 4)
+    pair_bytes = nbytes
+    peak, peak_kind = measured_peaks()
+    ach_upg = upg_bytes / (upg_ms / 1e3) / 1e9
+    ach_pair = pair_bytes / ((upg_ms + dn_ms) / 1e3) / 1e9
+    line = {
+        "metric": "expert-matvec HBM GB/s (grouped FP8 SwiGLU, 32 resident experts, n_e ~ U{1..16})",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3 weights x e4m3(3-term) activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, 128x128 block E4M3; N(0,1) bf16 rows)",
+        "config": {"workload": "config1_grouped_matvec_32experts", "experts": C1_EXPERTS, "rows": R,
+                   "rows_per_expert": [int(v) for v in n_e], "hidden": H, "inter": I,
+                   "bytes_per_step": nbytes, "cuda_graph": graph is not None,
+                   "l2": "no flush: 1.41 GB of expert weights exceed the 126 MB L2"},
+        "roofline": {"kernel": "grouped_ffn_tc up/gate (tcgen05 kind::f8f6f4, TMEM accumulators, TMA bulk ring)",
+                     "bound": "hbm", "achieved": round(ach_upg, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(ach_upg / peak, 4), "peak_source": peak_kind,
+                     "bytes_per_launch": upg_bytes, "ms_per_launch": round(upg_ms, 4), "traffic": None},
+        "expert_matvec": {"kernels": "grouped up/gate + down", "bytes": pair_bytes,
+                          "ms": round(upg_ms + dn_ms, 4), "achieved_gbs": round(ach_pair, 1),
+                          "frac": round(ach_pair / peak, 4)},
+        "frac_of_peak": round(value / peak, 4),
+        "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+        "e2e": {"value": round(nbytes / (ms_e2e / 1e3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 4),
+                "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 4},
+        # route_pack, pack x, up/gate, pack h, down, combine
+        "gpu_launches": 6 * args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = cpu_config1_rate(args.cpu_seconds)
+        except Exception as exc:
+            line["cpu_baseline"] = {"value": None, "error": f"{type(exc).__name__}: {exc}"}
+    if graph is not None:
+        graph.reset()
+    emit(line)
+
+
+def cpu_config1_rate(seconds: float, sample_rows: int = 4):
+    """The reference node's OpenMP FP8 CPU kernels at batch 1 on a sample of config-1 rows;
+    the GB/s figure is config 1's algorithmic bytes over the extrapolated call time."""
+    import numpy as np
+    import torch
+
+    from constellation_b200 import synthetic
+    from oracle import refbuild
+
+    threads = os.cpu_count() or 1
+    kind = "reference" if refbuild.ref_available() else "port"
+    n_e, row_slot, x, _ = config1_rows(torch)
+    R = x.shape[0]
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    experts = {}
+    starts = [0] + torch.cumsum(n_e, 0).tolist()[:-1]
+    sample = [int(r) for r in starts[:sample_rows]]  # one row each of the first experts
+    for r in sample:
+        j = int(row_slot[r])
+        if j not in experts:
+            ex = synthetic.make_expert(H, I, seed=1000 + j, device="cpu")
+            experts[j] = refbuild.ExpertBytes(ex.w_up.numpy(), ex.s_up.numpy(), ex.w_gate.numpy(),
+                                              ex.s_gate.numpy(), ex.w_down.numpy(), ex.s_down.numpy())
+
+    def one(r):
+        ex = experts[int(row_slot[r])]
+        if kind == "reference":
+            refbuild.ref_expert_cpu(ex, xb[r:r + 1], 2, 2, threads)
+        else:
+            xf = (xb[r].astype(np.uint32) << 16).view(np.float32)
+            refbuild.oracle_expert_lut(ex, xf[None])
+
+    one(sample[0])
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        for r in sample:
+            one(r)
+        n += len(sample)
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    ms_row = dt / n * 1e3
+    ms_call = ms_row * R
+    return {"value": round(config1_bytes(R) / (ms_call / 1e3) / 1e9, 4), "unit": "GB/s", "cores": threads,
+            "kind": kind, "sample": f"{n} batch-1 expert calls over one row each of experts 0..{len(sample) - 1} ({dt:.1f} s); "
+                                   f"one config-1 step = {R} such calls = {ms_call:.0f} ms (extrapolated)",
+            "ms_per_row": round(ms_row, 2)}
+
+
+# ---------------------------------------------------------------------------------------
 class CpuReferenceLayer:
     """The reference CPU path for a sample of tokens: router (CPU restatement of
     route_token_real), one batch-1 call of the reference node's OpenMP FP8 expert kernels
@@ -437,6 +642,16 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if args.workload == "config1":
+        base = cpu_config1_rate(args.cpu_seconds)
+        emit({"impl": "reference", "metric": "expert-matvec HBM GB/s (grouped FP8 SwiGLU, 32 resident experts, "
+              "n_e ~ U{1..16})", "value": base["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+              "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+              "dtype": "fp32 (FP8 LUT decode x block scale)", "data": "synthetic",
+              "config": {"workload": "config1_grouped_matvec_32experts", "parallelism": "cpu"},
+              "cpu_baseline": base,
+              "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+        return
     threads = os.cpu_count() or 1
     layer = CpuReferenceLayer(args.cpu_sample_tokens, threads)
     for _ in range(max(1, args.warmup)):
@@ -490,6 +705,8 @@ def main():
     os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "config1":
+        run_config1(args)
     else:
         run_ours(args)
 
