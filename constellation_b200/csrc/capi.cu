@@ -239,7 +239,7 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     up.out = w.h;
     up.ld_out = I;
     up.out_rows = c->part_rows;
-    up.max_split = 4;
+    up.max_split = kMaxUpGateSplit;
     up.row_weight = nullptr;
     up.err = w.err;
     CST_CUDA(launch_grouped_ffn(up, true, c->num_sms, s));

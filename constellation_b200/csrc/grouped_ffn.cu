@@ -179,7 +179,10 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 const int gi = (item / split) / a.n_mb;
                 const GroupRec gr = a.groups[gi];
                 const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
-                const uint32_t idesc = umma_idesc_e4m3(128, kSplits * kTileCols * NT);
+                // N = 3 terms x 8 NT tokens = 24 / 48 columns; with M = 128 the MMA takes N in
+                // steps of 16, so one n-tile runs at N = 32: B rows 24..31 are whatever the
+                // stage holds there and only feed accumulator columns no one reads
+                const uint32_t idesc = umma_idesc_e4m3(128, NT == 1 ? 32 : kSplits * kTileCols * NT);
                 for (int kk = 0; kk < KBs; ++kk) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;

@@ -76,6 +76,7 @@ struct PackActArgs {
 // meta->n_rows rows each); the packer adds the splits in order and applies
 // h = silu(gate) * up before quantizing.
 constexpr int kSrcUpGatePartials = 4;
+constexpr int kMaxUpGateSplit = 4;  // largest K split of the up/gate launch
 cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream);
 
 // grouped_ffn.cu

@@ -17,7 +17,7 @@
 //
 // One warp per (packed row, 8 consecutive K blocks): the row's metadata is read once and
 // the 8 source loads are issued together; per K block 128 elements, 4 per lane, one 32-bit
-// store per term.  Rows of a group's last n-tile beyond its row count are written as zeros.
+// store per term.  Rows of a group's last n-tile beyond its row count are not written.
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -41,11 +41,14 @@ __device__ __forceinline__ void load4(const PackActArgs& a, int64_t src_row, int
         const int64_t split_stride = int64_t(a.meta->n_rows) * 2 * a.ld;
         float4 u = *reinterpret_cast<const float4*>(p);
         float4 g = *reinterpret_cast<const float4*>(p + a.ld);
-        for (int ks = 1; ks < split; ++ks) {
-            const float4 u2 = *reinterpret_cast<const float4*>(p + ks * split_stride);
-            const float4 g2 = *reinterpret_cast<const float4*>(p + ks * split_stride + a.ld);
-            u.x += u2.x; u.y += u2.y; u.z += u2.z; u.w += u2.w;
-            g.x += g2.x; g.y += g2.y; g.z += g2.z; g.w += g2.w;
+#pragma unroll
+        for (int ks = 1; ks < kMaxUpGateSplit; ++ks) {
+            if (ks < split) {
+                const float4 u2 = *reinterpret_cast<const float4*>(p + ks * split_stride);
+                const float4 g2 = *reinterpret_cast<const float4*>(p + ks * split_stride + a.ld);
+                u.x += u2.x; u.y += u2.y; u.z += u2.z; u.w += u2.w;
+                g.x += g2.x; g.y += g2.y; g.z += g2.z; g.w += g2.w;
+            }
         }
         v[0] = (g.x / (1.0f + expf(-g.x))) * u.x;
         v[1] = (g.y / (1.0f + expf(-g.y))) * u.y;
@@ -69,11 +72,13 @@ __device__ __forceinline__ void load4(const PackActArgs& a, int64_t src_row, int
     }
 }
 
-constexpr int kPackKbPerTask = 8;  // K blocks one warp packs for one row
+constexpr int kPackKbPerTask = 8;  // K blocks one warp packs for one row (at most)
 
 __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
     const int KB = a.K / kBlock;
-    const int n_chunks = (KB + kPackKbPerTask - 1) / kPackKbPerTask;
+    // split partials read up to 8 loads per element: smaller tasks, more warps in flight
+    const int kbpt = a.src_dtype == kSrcUpGatePartials ? 2 : kPackKbPerTask;
+    const int n_chunks = (KB + kbpt - 1) / kbpt;
     const int n_tiles = a.meta->n_tiles;
     const int split = a.src_dtype == kSrcUpGatePartials ? a.meta->split_k : 1;
     const int lane = threadIdx.x & 31;
@@ -91,17 +96,17 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
         const int nt = tile - gr.tile_base;
         const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
         const int r = nt * kTileCols + j;
-        int64_t src_row = -1;
-        if (r < gr.n_rows) {
-            const int prow = gr.row_start + r;
-            src_row = a.row_map ? a.row_map[prow] : prow;
-        }
-        const int kb0 = chunk * kPackKbPerTask;
+        // columns of a group's last n-tile beyond its rows are left as they are: each feeds
+        // only its own accumulator column, which the grouped kernel never reads
+        if (r >= gr.n_rows) continue;
+        const int prow = gr.row_start + r;
+        const int64_t src_row = a.row_map ? a.row_map[prow] : prow;
+        const int kb0 = chunk * kbpt;
         // all source loads of the chunk first
         float v[kPackKbPerTask][4];
 #pragma unroll
         for (int i = 0; i < kPackKbPerTask; ++i) {
-            if (kb0 + i < KB) {
+            if (i < kbpt && kb0 + i < KB) {
                 load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, split, v[i]);
             } else {
                 v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.0f;
@@ -113,7 +118,7 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
 #pragma unroll
         for (int i = 0; i < kPackKbPerTask; ++i) {
             const int kb = kb0 + i;
-            if (kb >= KB) break;
+            if (i >= kbpt || kb >= KB) break;
             float amax = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
             amax = warp_max(amax);
             const float s = pow2_scale_for(amax);

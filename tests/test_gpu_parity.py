@@ -66,7 +66,9 @@ def test_expert_forward_vs_oracle(dev, H, I, n):
     y = ctx.expert_forward(7, xt, out_dtype=torch.float32)
     ref = DequantExpert(e).forward(x)
     err = rowwise_rel(y.cpu().numpy(), ref)
-    assert err < 2e-3, err
+    # three E4M3 activation terms give ~2e-5; a product that dropped the third term would
+    # land near 1e-3, so this bound also checks that every term reaches the accumulator
+    assert err < 2e-4, err
     yb = ctx.expert_forward(7, xt, out_dtype=torch.bfloat16)
     assert rowwise_rel(yb.float().cpu().numpy(), ref) < REL_TOL
 
