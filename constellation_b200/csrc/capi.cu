@@ -79,6 +79,8 @@ struct Workspace {
     float* hscale = nullptr;
     float* y = nullptr;               // [max_rows, H]
     int* err = nullptr;
+    int* hist = nullptr;              // packer counting-sort scratch
+    int64_t hist_cap = 0;
 };
 
 }  // namespace
@@ -172,6 +174,8 @@ int alloc_workspace(cst_ctx* c) {
     };
     Workspace& w = c->ws;
     const size_t tk = size_t(std::max<int64_t>(int64_t(f.max_tokens) * 16, R));
+    const int64_t max_routes = std::max<int64_t>(int64_t(f.max_tokens) * (f.top_k + 1), R);
+    w.hist_cap = ((max_routes + 1023) / 1024) * std::max(f.n_slots, 1);
     std::vector<Piece> pieces = {
         {reinterpret_cast<void**>(&w.router_logits), size_t(f.max_tokens) * E * 4},
         {reinterpret_cast<void**>(&w.topk_idx), size_t(f.max_tokens) * 16 * 4},
@@ -189,6 +193,7 @@ int alloc_workspace(cst_ctx* c) {
         {reinterpret_cast<void**>(&w.hscale), size_t(R) * (I / kBlock) * kTileCols * 4},
         {reinterpret_cast<void**>(&w.y), size_t(R) * H * 4},
         {reinterpret_cast<void**>(&w.err), 256},
+        {reinterpret_cast<void**>(&w.hist), size_t(w.hist_cap) * 4},
     };
     size_t total = 0;
     for (auto& p : pieces) total += (p.bytes + 255) / 256 * 256;
@@ -216,6 +221,9 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     pa.row_weight = w.row_weight;
     pa.tk_row = w.tk_row;
     pa.meta = w.meta;
+    pa.group_rows = kGroupRows;
+    pa.hist = w.hist;
+    pa.hist_cap = w.hist_cap;
     CST_CUDA(launch_route_pack(pa, s));
     prof_mark(c, 1, s);
 
@@ -308,9 +316,9 @@ int cst_create(int32_t device, const cst_config* cfg, cst_ctx** out) {
     // room for a 4-way K split of up/gate while the rows are few (the split is only chosen
     // when items are scarce, i.e. for a few hundred rows)
     c->part_rows = std::max(c->max_rows, std::min(4 * c->max_rows, 8192));
-    if (c->max_rows > kRoutePackMaxKeys) {
+    if (c->max_rows > kRoutePackMaxRows) {
         delete c;
-        return fail(CST_ERR_INVALID_ARG, "max_rows=%d exceeds %d", f.max_rows, kRoutePackMaxKeys);
+        return fail(CST_ERR_INVALID_ARG, "max_rows=%d exceeds %d", c->max_rows, kRoutePackMaxRows);
     }
     c->geo = ArenaGeom::make(f.hidden_dim, f.inter_dim);
     c->slot_of_expert.assign(f.n_routed_experts, -1);

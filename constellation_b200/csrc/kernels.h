@@ -54,8 +54,11 @@ struct PackArgs {
     float* row_weight;    // [max_rows]
     int32_t* tk_row;      // [T, K + 1] (mode A) or [T] (mode B); -1 = not here
     PackMeta* meta;
+    int group_rows;   // rows per group: 16 (decode kernels) or 64 (prefill kernels)
+    int* hist;        // counting-sort scratch for calls of more than 2048 routes
+    int64_t hist_cap; // ints available at hist (>= ceil(routes / 1024) * n_slots)
 };
-constexpr int kRoutePackMaxKeys = 32768;
+constexpr int kRoutePackMaxRows = 1 << 18;  // packed rows per call
 cudaError_t route_pack_init_attributes();
 cudaError_t launch_route_pack(const PackArgs& a, cudaStream_t stream);
 

@@ -8,12 +8,14 @@
 // slot are cut into groups of at most 16 rows (two 8-wide MMA n-tiles) that the grouped
 // FFN kernels consume.
 //
-// One CTA of 1024 threads.  Each route is encoded as a 31-bit key
+// Decode-sized calls (<= 2048 routes): one CTA of 1024 threads.  Each route is encoded as
+// a 31-bit key
 //   slot << 18 | token << 4 | k        (k == top_k marks the shared expert)
-// and the keys are bitonic-sorted in shared memory, which makes the packing fully
+// and every key's rank is counted in shared memory, which makes the packing fully
 // deterministic (no atomics decide an order).  Routes whose expert is not resident
 // here get key 0x7fffffff and sort to the end (under expert parallelism they belong to
-// another rank).
+// another rank).  Larger calls take the three-launch counting sort below, which yields
+// the same rows in the same order.
 #include <cstdint>
 
 #include "cst_common.cuh"
@@ -24,12 +26,8 @@ namespace cst {
 
 constexpr int kPackThreads = 1024;
 constexpr uint32_t kInvalidKey = 0x7fffffffu;
-constexpr int kRoutePackMaxSmem = kRoutePackMaxKeys * 4 + 8192 * 4;
-constexpr int kRankSortMaxKeys = 2048;  // up to here keys are ranked by counting, beyond by bitonic sort
-
-__host__ __device__ constexpr int route_pack_key_area(int n_keys_pow2) {
-    return n_keys_pow2 <= kRankSortMaxKeys ? 2 * kRankSortMaxKeys : n_keys_pow2;
-}
+constexpr int kRankSortMaxKeys = 2048;  // up to here one CTA ranks the keys; beyond, the counting sort
+constexpr int kRoutePackMaxSmem = 2 * kRankSortMaxKeys * 4 + 8192 * 4;
 
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* total) {
@@ -59,11 +57,30 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* tot
     return warp_prefix + x - v;
 }
 
+// Route i -> (token t, k, slot); slot -1 when the route has no row on this device.
+__device__ __forceinline__ int route_slot(const PackArgs& a, bool mode_rows, int K1, int i, int* t, int* k) {
+    int slot;
+    if (mode_rows) {
+        *t = i;
+        *k = 0;
+        slot = a.row_slot ? a.row_slot[i] : a.single_slot;
+    } else {
+        *t = i / K1;
+        *k = i % K1;
+        if (*k < a.K) {
+            const int e = a.topk_idx[*t * a.K + *k];
+            slot = (e >= 0 && e < a.E) ? a.slot_of_expert[e] : -1;
+        } else {
+            slot = (*t >= a.shared_t_begin && *t < a.shared_t_end) ? a.shared_slot : -1;
+        }
+    }
+    return (slot >= 0 && slot < a.n_slots) ? slot : -1;
+}
+
 __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, int n_keys_pow2) {
-    // keys (n_keys_pow2, or 2 x kRankSortMaxKeys when the rank sort needs its output
-    // buffer), then n_slots ints
+    // keys and the ranked output (2 x kRankSortMaxKeys), then n_slots ints
     extern __shared__ uint32_t s_keys[];
-    int* s_first = reinterpret_cast<int*>(s_keys + route_pack_key_area(n_keys_pow2));
+    int* s_first = reinterpret_cast<int*>(s_keys + 2 * kRankSortMaxKeys);
     __shared__ int s_warp[32];
     const int tid = threadIdx.x;
     const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
@@ -76,30 +93,16 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, in
     for (int i = tid; i < n_keys_pow2; i += kPackThreads) {
         uint32_t key = kInvalidKey;
         if (i < n_routes) {
-            int t, k, slot = -1;
-            if (mode_rows) {
-                t = i;
-                k = 0;
-                slot = a.row_slot ? a.row_slot[i] : a.single_slot;
-            } else {
-                t = i / K1;
-                k = i % K1;
-                if (k < a.K) {
-                    const int e = a.topk_idx[t * a.K + k];
-                    slot = (e >= 0 && e < a.E) ? a.slot_of_expert[e] : -1;
-                } else {
-                    slot = (t >= a.shared_t_begin && t < a.shared_t_end) ? a.shared_slot : -1;
-                }
-            }
-            if (slot >= 0 && slot < a.n_slots)
-                key = (uint32_t(slot) << 18) | (uint32_t(t) << 4) | uint32_t(k);
+            int t, k;
+            const int slot = route_slot(a, mode_rows, K1, i, &t, &k);
+            if (slot >= 0) key = (uint32_t(slot) << 18) | (uint32_t(t) << 4) | uint32_t(k);
         }
         s_keys[i] = key;
     }
     __syncthreads();
-    if (n_keys_pow2 <= kRankSortMaxKeys) {
-        // decode-sized batches: every valid key's position is the number of smaller keys
-        // (keys are unique), one pass of n compares per key instead of log^2 n barriers
+    {
+        // every valid key's position is the number of smaller keys (keys are unique): one
+        // pass of n compares per key instead of log^2 n barriers of a sorting network
         uint32_t* s_out = s_keys + kRankSortMaxKeys;
         for (int i = tid; i < n_keys_pow2; i += kPackThreads) s_out[i] = kInvalidKey;
         __syncthreads();
@@ -113,23 +116,6 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, in
         __syncthreads();
         for (int i = tid; i < n_keys_pow2; i += kPackThreads) s_keys[i] = s_out[i];
         __syncthreads();
-    } else {
-        // bitonic sort, ascending
-        for (int size = 2; size <= n_keys_pow2; size <<= 1) {
-            for (int stride = size >> 1; stride > 0; stride >>= 1) {
-                for (int i = tid; i < (n_keys_pow2 >> 1); i += kPackThreads) {
-                    const int lo = 2 * i - (i & (stride - 1));
-                    const int hi = lo + stride;
-                    const bool asc = (lo & size) == 0;
-                    const uint32_t a0 = s_keys[lo], a1 = s_keys[hi];
-                    if ((a0 > a1) == asc) {
-                        s_keys[lo] = a1;
-                        s_keys[hi] = a0;
-                    }
-                }
-                __syncthreads();
-            }
-        }
     }
     // number of valid rows and the first row of each slot
     int valid_local = 0;
@@ -150,7 +136,7 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, in
     int starts = 0;
     for (int p = r0; p < r1; ++p) {
         const int slot = int(s_keys[p] >> 18);
-        if (((p - s_first[slot]) % kGroupRows) == 0) ++starts;
+        if (((p - s_first[slot]) % a.group_rows) == 0) ++starts;
     }
     int n_groups;
     int g = block_exclusive_scan(starts, s_warp, &n_groups);
@@ -158,9 +144,9 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, in
     int tiles_local = 0;
     for (int p = r0; p < r1; ++p) {
         const int slot = int(s_keys[p] >> 18);
-        if (((p - s_first[slot]) % kGroupRows) == 0) {
+        if (((p - s_first[slot]) % a.group_rows) == 0) {
             int end = p + 1;
-            while (end < n_rows && end < p + kGroupRows && int(s_keys[end] >> 18) == slot) ++end;
+            while (end < n_rows && end < p + a.group_rows && int(s_keys[end] >> 18) == slot) ++end;
             tiles_local += (end - p + kTileCols - 1) / kTileCols;
         }
     }
@@ -182,9 +168,9 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, in
             }
             a.row_weight[p] = wt;
             a.tk_row[t * K1 + k] = p;
-            if (((p - s_first[slot]) % kGroupRows) == 0) {
+            if (((p - s_first[slot]) % a.group_rows) == 0) {
                 int end = p + 1;
-                while (end < n_rows && end < p + kGroupRows && int(s_keys[end] >> 18) == slot) ++end;
+                while (end < n_rows && end < p + a.group_rows && int(s_keys[end] >> 18) == slot) ++end;
                 const int nt = (end - p + kTileCols - 1) / kTileCols;
                 a.groups[g] = GroupRec{slot, p, end - p, tile};
                 for (int j = 0; j < nt; ++j) a.tile_group[tile + j] = g;
@@ -201,6 +187,124 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, in
     }
 }
 
+// ---------------------------------------------------------------------------------------
+// Large batches (more than kRankSortMaxKeys routes, e.g. a 4096-token prefill chunk): a
+// three-launch counting sort over slots instead of one CTA sorting every key.
+//   count:   chunk c of kPackThreads routes -> hist[c][slot] (shared-memory histogram)
+//   scan:    one CTA turns hist into each (chunk, slot)'s first packed row, numbers the
+//            groups slot by slot and writes the group records, tile map and meta
+//   scatter: each route's row = hist[c][slot] + the number of earlier routes of chunk c
+//            with the same slot
+// Rows of one slot therefore come in (token, k) order, as the sort gives them, and the
+// result is identical to the single-CTA path: same rows, same groups, same order.
+
+__global__ void __launch_bounds__(kPackThreads) route_count_kernel(PackArgs a) {
+    extern __shared__ int s_hist[];
+    const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
+    const int K1 = mode_rows ? 1 : a.K + 1;
+    const int n_routes = mode_rows ? a.T : a.T * K1;
+    for (int s = threadIdx.x; s < a.n_slots; s += kPackThreads) s_hist[s] = 0;
+    __syncthreads();
+    const int i = blockIdx.x * kPackThreads + threadIdx.x;
+    if (i < n_routes) {
+        int t, k;
+        const int slot = route_slot(a, mode_rows, K1, i, &t, &k);
+        if (slot >= 0) atomicAdd(&s_hist[slot], 1);  // a count: the order of adds is immaterial
+    }
+    __syncthreads();
+    for (int s = threadIdx.x; s < a.n_slots; s += kPackThreads)
+        a.hist[int64_t(blockIdx.x) * a.n_slots + s] = s_hist[s];
+}
+
+__global__ void __launch_bounds__(kPackThreads) route_scan_kernel(PackArgs a, int n_chunks) {
+    extern __shared__ int s_tot[];  // per slot: routes, then (reused) first row
+    __shared__ int s_warp[32];
+    const int tid = threadIdx.x;
+    // per slot: running count over chunks (exclusive, in place) and the slot total
+    for (int s = tid; s < a.n_slots; s += kPackThreads) {
+        int run = 0;
+        for (int c = 0; c < n_chunks; ++c) {
+            int* h = &a.hist[int64_t(c) * a.n_slots + s];
+            const int v = *h;
+            *h = run;
+            run += v;
+        }
+        s_tot[s] = run;
+    }
+    __syncthreads();
+    // each thread owns a contiguous range of slots for the block scans
+    const int per = (a.n_slots + kPackThreads - 1) / kPackThreads;
+    const int s0 = min(a.n_slots, tid * per), s1 = min(a.n_slots, s0 + per);
+    const int G = a.group_rows;
+    int rows_l = 0, groups_l = 0, tiles_l = 0;
+    for (int s = s0; s < s1; ++s) {
+        const int n = s_tot[s];
+        rows_l += n;
+        groups_l += (n + G - 1) / G;
+        tiles_l += (n / G) * ((G + kTileCols - 1) / kTileCols) + ((n % G) + kTileCols - 1) / kTileCols;
+    }
+    int n_rows, n_groups, n_tiles;
+    int row = block_exclusive_scan(rows_l, s_warp, &n_rows);
+    int g = block_exclusive_scan(groups_l, s_warp, &n_groups);
+    int tile = block_exclusive_scan(tiles_l, s_warp, &n_tiles);
+    const bool overflow = (n_rows > a.max_rows) || (n_groups > a.max_groups);
+    for (int s = s0; s < s1; ++s) {
+        const int n = s_tot[s];
+        s_tot[s] = row;  // first row of slot s
+        if (!overflow) {
+            for (int j = 0; j * G < n; ++j) {
+                const int rows = min(G, n - j * G);
+                const int nt = (rows + kTileCols - 1) / kTileCols;
+                a.groups[g] = GroupRec{s, row + j * G, rows, tile};
+                for (int q = 0; q < nt; ++q) a.tile_group[tile + q] = g;
+                ++g;
+                tile += nt;
+            }
+        }
+        row += n;
+    }
+    __syncthreads();
+    for (int s = tid; s < a.n_slots; s += kPackThreads) {
+        const int first = s_tot[s];
+        for (int c = 0; c < n_chunks; ++c) a.hist[int64_t(c) * a.n_slots + s] += first;
+    }
+    if (tid == 0) {
+        a.meta->n_rows = overflow ? 0 : n_rows;
+        a.meta->n_groups = overflow ? 0 : n_groups;
+        a.meta->n_tiles = overflow ? 0 : n_tiles;
+        a.meta->overflow = overflow ? 1 : 0;
+    }
+}
+
+__global__ void __launch_bounds__(kPackThreads) route_scatter_kernel(PackArgs a) {
+    __shared__ int s_slot[kPackThreads];
+    const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
+    const int K1 = mode_rows ? 1 : a.K + 1;
+    const int n_routes = mode_rows ? a.T : a.T * K1;
+    const int i = blockIdx.x * kPackThreads + threadIdx.x;
+    int t = 0, k = 0, slot = -1;
+    if (i < n_routes) slot = route_slot(a, mode_rows, K1, i, &t, &k);
+    s_slot[threadIdx.x] = slot;
+    __syncthreads();
+    if (i >= n_routes) return;
+    if (slot < 0 || a.meta->overflow) {
+        a.tk_row[i] = -1;
+        return;
+    }
+    int rank = 0;
+    for (int j = 0; j < int(threadIdx.x); ++j) rank += s_slot[j] == slot;
+    const int p = a.hist[int64_t(blockIdx.x) * a.n_slots + slot] + rank;
+    a.row_token[p] = t;
+    float wt = 1.0f;
+    if (mode_rows) {
+        if (a.row_weight_in) wt = a.row_weight_in[t];
+    } else if (k < a.K) {
+        wt = a.topk_w[t * a.K + k];
+    }
+    a.row_weight[p] = wt;
+    a.tk_row[i] = p;  // i = t * K1 + k
+}
+
 cudaError_t route_pack_init_attributes() {
     return cudaFuncSetAttribute(route_pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kRoutePackMaxSmem);
@@ -213,12 +317,24 @@ int route_pack_pow2(int n) {
 }
 
 size_t route_pack_smem(int n_keys_pow2, int n_slots) {
-    return size_t(route_pack_key_area(n_keys_pow2)) * 4 + size_t(n_slots) * 4;
+    (void)n_keys_pow2;
+    return size_t(2 * kRankSortMaxKeys) * 4 + size_t(n_slots) * 4;
 }
+
+int route_pack_chunks(int n_routes) { return (n_routes + kPackThreads - 1) / kPackThreads; }
 
 cudaError_t launch_route_pack(const PackArgs& a, cudaStream_t stream) {
     const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
     const int n_routes = mode_rows ? a.T : a.T * (a.K + 1);
+    if (n_routes > kRankSortMaxKeys) {
+        const int chunks = route_pack_chunks(n_routes);
+        if (int64_t(chunks) * a.n_slots > a.hist_cap) return cudaErrorInvalidValue;
+        const size_t hs = size_t(a.n_slots) * sizeof(int);
+        route_count_kernel<<<chunks, kPackThreads, hs, stream>>>(a);
+        route_scan_kernel<<<1, kPackThreads, hs, stream>>>(a, chunks);
+        route_scatter_kernel<<<chunks, kPackThreads, 0, stream>>>(a);
+        return cudaGetLastError();
+    }
     const int p2 = route_pack_pow2(n_routes);
     const size_t smem = route_pack_smem(p2, a.n_slots);
     route_pack_kernel<<<1, kPackThreads, smem, stream>>>(a, p2);

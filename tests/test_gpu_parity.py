@@ -161,7 +161,8 @@ def _layer_setup(dev, seed, T, E, H, I, G, TG, K, shared=True, max_tokens=None):
     return ctx, x, w, b, experts, sh
 
 
-@pytest.mark.parametrize("T", [1, 4, 37])
+# T = 600 gives 3000 routes: more than one CTA packs, through the three-launch counting sort
+@pytest.mark.parametrize("T", [1, 4, 37, 600])
 def test_moe_layer_vs_oracle(dev, golden, T):
     E, H, I, G, TG, K = 16, 256, 128, 4, 2, 4
     ctx, x, w, b, experts, sh = _layer_setup(dev, 51 + T, T, E, H, I, G, TG, K)
@@ -198,6 +199,16 @@ def test_moe_layer_repeat_bit_stable(dev):
     args = (torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev))
     o0 = ctx.moe_layer(*args)
     for _ in range(10):
+        assert torch.equal(ctx.moe_layer(*args), o0)
+
+
+def test_moe_layer_large_batch_repeat_bit_stable(dev):
+    """The multi-CTA packer (3000 routes) is as deterministic as the single-CTA one."""
+    E, H, I, G, TG, K = 16, 256, 128, 4, 2, 4
+    ctx, x, w, b, _, _ = _layer_setup(dev, 78, 600, E, H, I, G, TG, K)
+    args = (torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev))
+    o0 = ctx.moe_layer(*args)
+    for _ in range(5):
         assert torch.equal(ctx.moe_layer(*args), o0)
 
 
