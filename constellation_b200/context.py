@@ -164,6 +164,14 @@ class ExpertContext:
     def set_shared_slot(self, slot: int) -> None:
         check(_lib.lib.cst_set_shared_slot(self.handle, int(slot)))
 
+    def set_gemm_mode(self, mode: str) -> None:
+        """Grouped-kernel shape: "auto" (prefill kernels from 32 rows per expert on),
+        "decode" (16-row groups, 3 activation terms) or "prefill" (64-row groups, 2 terms)."""
+        codes = {"auto": _lib.CST_GEMM_AUTO, "decode": _lib.CST_GEMM_DECODE, "prefill": _lib.CST_GEMM_PREFILL}
+        if mode not in codes:
+            raise ValueError(f"gemm mode must be one of {sorted(codes)}, got {mode!r}")
+        check(_lib.lib.cst_set_gemm_mode(self.handle, codes[mode]))
+
     # -- hot path ---------------------------------------------------------------------
     def _check_x(self, x: torch.Tensor) -> torch.Tensor:
         if not isinstance(x, torch.Tensor):

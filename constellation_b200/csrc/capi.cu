@@ -98,6 +98,7 @@ struct cst_ctx {
     int32_t shared_slot = -1;
     int max_rows = 0;
     int part_rows = 0;  // rows of up/gate partial sums the workspace holds (K splits x rows)
+    int gemm_mode = CST_GEMM_AUTO;  // cst_set_gemm_mode
     uint8_t* ws_base = nullptr;
     size_t ws_bytes = 0;
     Workspace ws;
@@ -208,10 +209,34 @@ int alloc_workspace(cst_ctx* c) {
     return CST_OK;
 }
 
+// Prefill-shaped kernels once a call averages >= 32 rows per expert: groups of 64 rows
+// spread each weight tile over more tokens and two activation terms cut the tensor work.
+constexpr int kPrefillMinRowsPerExpert = 32;
+
+bool use_prefill(const cst_ctx* c, const PackArgs& pa) {
+    if (c->gemm_mode == CST_GEMM_DECODE) return false;
+    if (c->gemm_mode == CST_GEMM_PREFILL) return true;
+    int64_t rows, experts;
+    if (pa.row_slot == nullptr && pa.single_slot >= 0) {
+        rows = pa.T;
+        experts = 1;
+    } else if (pa.row_slot != nullptr) {
+        rows = pa.T;
+        experts = std::max(1, c->cfg.n_slots);
+    } else {
+        rows = int64_t(pa.T) * pa.K;
+        experts = std::max(1, c->cfg.n_routed_experts);
+    }
+    return rows >= kPrefillMinRowsPerExpert * experts;
+}
+
 // route_pack -> pack x -> up/gate -> pack h -> down.  Leaves y rows and tk_row filled.
 int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_t s) {
     const int H = c->cfg.hidden_dim, I = c->cfg.inter_dim;
     Workspace& w = c->ws;
+    const bool pf = use_prefill(c, pa);
+    const int terms = pf ? 2 : kSplits;
+    auto grouped = pf ? launch_grouped_prefill : launch_grouped_ffn;
     pa.n_slots = c->cfg.n_slots;
     pa.max_rows = c->max_rows;
     pa.max_groups = c->max_rows;
@@ -221,13 +246,13 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     pa.row_weight = w.row_weight;
     pa.tk_row = w.tk_row;
     pa.meta = w.meta;
-    pa.group_rows = kGroupRows;
+    pa.group_rows = pf ? kPrefillGroupRows : kGroupRows;
     pa.hist = w.hist;
     pa.hist_cap = w.hist_cap;
     CST_CUDA(launch_route_pack(pa, s));
     prof_mark(c, 1, s);
 
-    PackActArgs px{x, x_dtype, H, w.row_token, w.groups, w.tile_group, w.meta, H, w.xfrag, w.xscale};
+    PackActArgs px{x, x_dtype, H, w.row_token, w.groups, w.tile_group, w.meta, H, w.xfrag, w.xscale, terms};
     CST_CUDA(launch_pack_act(px, c->num_sms, s));
     prof_mark(c, 2, s);
 
@@ -250,10 +275,10 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     up.max_split = kMaxUpGateSplit;
     up.row_weight = nullptr;
     up.err = w.err;
-    CST_CUDA(launch_grouped_ffn(up, true, c->num_sms, s));
+    CST_CUDA(grouped(up, true, c->num_sms, s));
     prof_mark(c, 3, s);
 
-    PackActArgs ph{w.h, kSrcUpGatePartials, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale};
+    PackActArgs ph{w.h, kSrcUpGatePartials, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale, terms};
     CST_CUDA(launch_pack_act(ph, c->num_sms, s));
     prof_mark(c, 4, s);
 
@@ -271,7 +296,7 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     dn.row_weight = w.row_weight;
     dn.out_rows = c->max_rows;
     dn.max_split = 1;
-    CST_CUDA(launch_grouped_ffn(dn, false, c->num_sms, s));
+    CST_CUDA(grouped(dn, false, c->num_sms, s));
     prof_mark(c, 5, s);
     return CST_OK;
 }
@@ -339,7 +364,8 @@ int cst_create(int32_t device, const cst_config* cfg, cst_ctx** out) {
     if (major != 10 || minor != 0)
         return bail(fail(CST_ERR_CUDA, "this library is built for sm_100a (B200); device %d is sm_%d%d", device,
                          major, minor));
-    if (route_pack_init_attributes() != cudaSuccess || grouped_ffn_init_attributes() != cudaSuccess)
+    if (route_pack_init_attributes() != cudaSuccess || grouped_ffn_init_attributes() != cudaSuccess ||
+        grouped_prefill_init_attributes() != cudaSuccess)
         return bail(fail(CST_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(cudaGetLastError())));
     const size_t arena = size_t(f.n_slots) * size_t(c->geo.slot_bytes);
     if (cudaMalloc(&c->arena, arena) != cudaSuccess)
@@ -439,6 +465,15 @@ int cst_free_expert(cst_ctx* c, int32_t slot) {
 int32_t cst_find_slot(const cst_ctx* c, int32_t expert_id) {
     if (c == nullptr || expert_id < 0 || expert_id >= c->cfg.n_routed_experts) return -1;
     return c->slot_of_expert[expert_id];
+}
+
+int cst_set_gemm_mode(cst_ctx* c, int32_t mode) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (mode != CST_GEMM_AUTO && mode != CST_GEMM_DECODE && mode != CST_GEMM_PREFILL)
+        return fail(CST_ERR_INVALID_ARG, "gemm mode %d is not one of 0 (auto), 1 (decode), 2 (prefill)", mode);
+    c->gemm_mode = mode;
+    return CST_OK;
 }
 
 int cst_set_shared_slot(cst_ctx* c, int32_t slot) {

@@ -74,6 +74,7 @@ struct PackActArgs {
     int K;                   // H (x) or I (h)
     uint8_t* bfrag;          // B fragments
     float* bscale;           // per (row, K block) scales
+    int terms;               // E4M3 terms per element: 3 (decode kernels) or 2 (prefill kernels)
 };
 // src_dtype 4: `src` holds the up/gate kernel's split accumulators (meta->split_k splits of
 // meta->n_rows rows each); the packer adds the splits in order and applies
@@ -108,6 +109,10 @@ struct FfnArgs {
 };
 cudaError_t grouped_ffn_init_attributes();
 cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream);
+
+// grouped_prefill.cu: the same contract for groups of up to 64 rows and 2-term activations
+cudaError_t grouped_prefill_init_attributes();
+cudaError_t launch_grouped_prefill(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream);
 
 // combine.cu
 struct CombineArgs {

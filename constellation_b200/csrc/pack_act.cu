@@ -7,6 +7,7 @@
 // pipe.  One E4M3 term carries 4 significant bits, so each activation element v of a
 // (row, 128-wide K block) is written as
 //     v = s * (q1 + q2 + q3),  q1 = e4m3(v/s), q2 = e4m3(v/s - q1), q3 = e4m3(v/s - q1 - q2)
+// (decode kernels; the prefill kernels take the first two terms only)
 // with s the smallest power of two that maps the block's max |v| to <= 448.  The three
 // terms reproduce v/s to ~2^-12 relative (absolute floor 2^-10 in the scaled domain, i.e.
 // about 2e-6 of the block max), far inside the bf16 resolution of the inputs, and the
@@ -129,17 +130,21 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
                 float rsd = v[i][e] * inv;
 #pragma unroll
                 for (int sp = 0; sp < kSplits; ++sp) {
-                    const uint8_t b = e4m3_rn(rsd);
-                    q[sp] |= uint32_t(b) << (8 * e);
-                    rsd -= e4m3_to_f32(b);
+                    if (sp < a.terms) {
+                        const uint8_t b = e4m3_rn(rsd);
+                        q[sp] |= uint32_t(b) << (8 * e);
+                        rsd -= e4m3_to_f32(b);
+                    }
                 }
             }
-            // K-major, 128-byte swizzled placement: B row n = split * TP + token (TP = 8 NT),
-            // 128 bytes of K per row, 16-byte chunk c of row n stored at chunk c ^ (n & 7).
+            // K-major, 128-byte swizzled placement: B row n = term * TP + token (TP = 8 NT),
+            // 128 bytes of K per row, 16-byte chunk c of row n stored at chunk c ^ (n & 7);
+            // the (group, kb) tile is terms x TP rows (3 terms: decode, 2 terms: prefill).
             const int64_t gk = int64_t(gr.tile_base) * KB + int64_t(kb) * NT;  // (group, kb) tile
-            uint8_t* base = a.bfrag + gk * kBTileBytes;
+            uint8_t* base = a.bfrag + gk * (a.terms * kTileCols * kBlock);
 #pragma unroll
             for (int sp = 0; sp < kSplits; ++sp) {
+                if (sp >= a.terms) break;
                 const int n = sp * TP + tok;
                 const int pc = c ^ (n & 7);
                 *reinterpret_cast<uint32_t*>(base + n * kBlock + pc * 16 + 4 * (lane & 3)) = q[sp];

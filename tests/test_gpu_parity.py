@@ -166,6 +166,7 @@ def _layer_setup(dev, seed, T, E, H, I, G, TG, K, shared=True, max_tokens=None):
 def test_moe_layer_vs_oracle(dev, golden, T):
     E, H, I, G, TG, K = 16, 256, 128, 4, 2, 4
     ctx, x, w, b, experts, sh = _layer_setup(dev, 51 + T, T, E, H, I, G, TG, K)
+    ctx.set_gemm_mode("decode")  # T = 600 would choose the prefill kernels (tests/test_gpu_prefill.py)
     out, idx, wt = ctx.moe_layer(torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev),
                                  torch.from_numpy(b).to(dev), return_routes=True, out_dtype=torch.float32)
     de = {e: DequantExpert(v) for e, v in experts.items()}

@@ -1,0 +1,116 @@
+"""Prefill-shaped grouped kernels (64-row groups, two E4M3 activation terms) against the
+oracle: the dequantize-then-matmul path of the reference (server/fp8_utils.py:4-39,
+server/moe_layer_runtime.py:581-611) in fp32.
+
+Two activation terms carry ~1e-3 row-wise relative error on a full-size expert (three
+terms, the decode kernels: ~2e-5), so the fp32 bound here is 3e-3; bf16 outputs keep the
+1e-2 bar of the other layer tests.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import cases
+from oracle.expert import DequantExpert
+from oracle.layer import moe_layer
+
+pytestmark = pytest.mark.gpu
+
+PF_TOL = 3e-3
+REL_TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def rowwise_rel(a, ref):
+    a = np.atleast_2d(a).astype(np.float64)
+    ref = np.atleast_2d(ref).astype(np.float64)
+    return float((np.abs(a - ref).max(axis=1) / np.maximum(np.abs(ref).max(axis=1), 1e-30)).max())
+
+
+def make_ctx(dev, H, I, E=32, G=4, TG=2, K=4, n_slots=2, max_tokens=64, max_rows=0, mode="prefill"):
+    from constellation_b200.context import ExpertContext, MoEConfig
+
+    cfg = MoEConfig(hidden_size=H, moe_intermediate_size=I, n_routed_experts=E, n_group=G, topk_group=TG,
+                    num_experts_per_tok=K)
+    ctx = ExpertContext(dev, cfg, n_slots=n_slots, max_tokens=max_tokens, max_rows=max_rows)
+    ctx.set_gemm_mode(mode)
+    return ctx
+
+
+# every group size class: one n-tile, odd tile counts (N padded to 16), a full 64-row group,
+# and more rows than one group; H = 384 has an odd number of down row blocks
+@pytest.mark.parametrize("H,I,n", [(256, 128, 1), (256, 128, 9), (512, 256, 24), (384, 256, 64), (256, 384, 100)])
+def test_expert_forward_prefill_vs_oracle(dev, H, I, n):
+    ctx = make_ctx(dev, H, I, max_tokens=128, max_rows=128)
+    e = cases.expert(900 + n, H, I)
+    ctx.upload_bundle(1, 7, e)
+    x = cases.activations(950 + n, n, H)
+    xt = torch.from_numpy(x).to(dev, torch.bfloat16)
+    y = ctx.expert_forward(7, xt, out_dtype=torch.float32)
+    ref = DequantExpert(e).forward(x)
+    assert rowwise_rel(y.cpu().numpy(), ref) < PF_TOL
+    yb = ctx.expert_forward(7, xt, out_dtype=torch.bfloat16)
+    assert rowwise_rel(yb.float().cpu().numpy(), ref) < REL_TOL
+
+
+def test_grouped_ffn_prefill_full_size(dev):
+    """Two DeepSeek-shaped experts with 64 and 50 rows (one full group, one partial)."""
+    H, I = 7168, 2048
+    ctx = make_ctx(dev, H, I, E=256, n_slots=2, max_tokens=128, max_rows=128)
+    es = [cases.expert(960 + i, H, I) for i in range(2)]
+    for i, e in enumerate(es):
+        ctx.upload_bundle(i, i, e)
+    counts = [64, 50]
+    rows = sum(counts)
+    x = cases.activations(970, rows, H)
+    slot = np.repeat(np.arange(2), counts).astype(np.int32)
+    wts = np.linspace(0.5, 1.5, rows).astype(np.float32)
+    y = ctx.grouped_ffn(torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(slot).to(dev),
+                        torch.from_numpy(wts).to(dev)).cpu().numpy()
+    r0 = 0
+    for i, n in enumerate(counts):
+        ref = DequantExpert(es[i]).forward(x[r0:r0 + n]) * wts[r0:r0 + n, None]
+        assert rowwise_rel(y[r0:r0 + n], ref) < PF_TOL
+        r0 += n
+
+
+@pytest.mark.parametrize("mode,T", [("prefill", 4), ("prefill", 37), ("auto", 600), ("decode", 600)])
+def test_moe_layer_modes_vs_oracle(dev, mode, T):
+    """The full layer in both kernel shapes; T = 600 at 16 experts / top-4 averages 150 rows
+    per expert, which the automatic choice sends to the prefill kernels."""
+    E, H, I, G, TG, K = 16, 256, 128, 4, 2, 4
+    seed = 61 + T
+    x = cases.activations(seed, T, H)
+    w, b = cases.router(seed, E, H, bias_std=0.05)
+    experts = {e: cases.expert(1000 * seed + e, H, I) for e in range(E)}
+    sh = cases.expert(1000 * seed + 999, H, I)
+    ctx = make_ctx(dev, H, I, E=E, G=G, TG=TG, K=K, n_slots=E + 1, max_tokens=T, mode=mode)
+    for e in range(E):
+        ctx.upload_bundle(e, e, experts[e])
+    ctx.upload_bundle(E, -1, sh)
+    args = (torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev))
+    out, idx, _ = ctx.moe_layer(*args, return_routes=True, out_dtype=torch.float32)
+    de = {e: DequantExpert(v) for e, v in experts.items()}
+    ref = moe_layer(x, w, b, de, DequantExpert(sh), n_group=G, topk_group=TG, top_k=K)
+    ok = ref.route.margin > 1e-5
+    np.testing.assert_array_equal(idx.cpu().numpy()[ok], ref.route.topk_idx[ok])
+    tol = 2e-3 if mode == "decode" else PF_TOL
+    assert rowwise_rel(out.cpu().numpy()[ok], ref.out_f32[ok]) < tol
+    # bit-identical on repeat
+    o2 = ctx.moe_layer(*args, out_dtype=torch.float32)
+    assert torch.equal(out, o2)
+
+
+def test_gemm_mode_rejects_unknown(dev):
+    from constellation_b200 import _lib
+
+    ctx = make_ctx(dev, 256, 128, mode="auto")
+    with pytest.raises(ValueError):
+        ctx.set_gemm_mode("fast")
+    assert _lib.lib.cst_set_gemm_mode(ctx.handle, 7) == _lib.CST_ERR_INVALID_ARG
