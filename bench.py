@@ -50,15 +50,17 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--tokens", type=int, default=64, help="decode batch T (whole job)")
+    p.add_argument("--tokens", type=int, default=None,
+                   help="tokens T of the whole job (default 64 for config2, 4096 for config4)")
     p.add_argument("--ep-mode", choices=["allgather", "alltoall"], default="allgather")
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     p.add_argument("--cpu-sample-tokens", type=int, default=2)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=["config2", "config1"], default="config2",
-                   help="config2: the full layer (default); config1: grouped FP8 expert matvec only, "
-                        "32 resident experts with n_e ~ U{1..16} rows each, 1 GPU")
+    p.add_argument("--workload", choices=["config2", "config1", "config4"], default="config2",
+                   help="config2: the full decode layer, T=64 (default); config1: grouped FP8 expert matvec "
+                        "only, 32 resident experts with n_e ~ U{1..16} rows each, 1 GPU; config4: one layer "
+                        "over a 4096-token prefill chunk with a Zipf-skewed router bias")
     p.add_argument("--resident-experts", type=int, default=E,
                    help="upload only the first N routed experts of each rank (small profiling case; "
                         "routes to the others contribute nothing)")
@@ -74,6 +76,19 @@ def measured_peaks():
         except Exception:
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def fp8_peak_tflops():
+    """Dense FP8 tensor peak: twice the measured bf16 GEMM rate (the FP8 rate itself is not
+    in the measured file; B200's FP8 dense rate is twice its bf16 rate), else nominal."""
+    f = REPO / "MEASURED_PEAKS.json"
+    if f.is_file():
+        try:
+            d = json.loads(f.read_text())
+            return 2.0 * float(d["bf16_tflops"]), "2 x measured bf16 (fp8 not measured)"
+        except Exception:
+            pass
+    return 4500.0, "nominal fp8 dense"
 
 
 class ClockSampler:
@@ -124,7 +139,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------
-def setup_layer(torch, rank, world, T_total, dev, resident=E):
+def setup_layer(torch, rank, world, T_total, dev, resident=E, zipf=False):
     from constellation_b200 import synthetic
     from constellation_b200.context import ExpertContext, MoEConfig
 
@@ -140,6 +155,8 @@ def setup_layer(torch, rank, world, T_total, dev, resident=E):
     ctx.upload_expert(epr, -1, sh.w_up, sh.s_up, sh.w_gate, sh.s_gate, sh.w_down, sh.s_down)
     del sh
     gw, gb = synthetic.make_router(H, E, seed=7, device=dev)
+    if zipf:  # config 4: router bias = 2.0 * log-Zipf(1.2) over a seeded permutation
+        gb = synthetic.zipf_bias(E, seed=7, device=dev)
     x_all = synthetic.make_activations(T_total, H, seed=11, device=dev)
     Tl = T_total // world
     x = x_all[rank * Tl:(rank + 1) * Tl].contiguous()
@@ -170,12 +187,13 @@ def run_ours(args):
         import datetime
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=datetime.timedelta(seconds=120))
-    T = args.tokens
+    prefill = args.workload == "config4"
+    T = args.tokens or (4096 if prefill else 64)
     if T % world:
         raise SystemExit(f"T={T} does not shard over {world} ranks")
     from constellation_b200.ep import ExpertParallelMoE
 
-    ctx, gw, gb, x, x_all = setup_layer(torch, rank, world, T, dev, args.resident_experts)
+    ctx, gw, gb, x, x_all = setup_layer(torch, rank, world, T, dev, args.resident_experts, zipf=prefill)
     moe = ExpertParallelMoE(ctx, rank=rank, world=world, n_routed_experts=E, mode=args.ep_mode)
     out = torch.empty_like(x)
 
@@ -207,7 +225,8 @@ def run_ours(args):
             graph.replay()
         torch.cuda.synchronize(dev)
     # kernels of this library per layer (NCCL and torch copy kernels not counted)
-    launches_per_step = 8 if world == 1 else 9
+    # (the packer is one launch up to 2048 routes and three beyond)
+    launches_per_step = (8 if world == 1 else 9) + (2 if T * (K + 1) > 2048 else 0)
 
     def timed(fn, k):
         if world > 1:
@@ -303,6 +322,19 @@ def run_ours(args):
     ach_pair = pair_bytes / ((upg_ms + dn_ms) / 1e3) / 1e9
     layer_bytes = pair_bytes + ROUTER_BYTES + (T // world) * H * 4
 
+    # config 4 is tensor-bound: natural FLOP (one product per weight element and row, the
+    # activation terms not counted) against the FP8 dense peak
+    flop_rank = rows_incl_shared * 3 * 2 * H * I
+    flop_upg = rows_incl_shared * 2 * 2 * H * I
+    fp8_peak, fp8_kind = fp8_peak_tflops()
+    rows_t = torch.tensor([rows_incl_shared], device=dev, dtype=torch.float64)
+    if world > 1:
+        rows_all = [torch.zeros_like(rows_t) for _ in range(world)]
+        dist.all_gather(rows_all, rows_t)
+        rows_per_rank = [int(r.item()) for r in rows_all]
+    else:
+        rows_per_rank = [rows_incl_shared]
+    imbalance = max(rows_per_rank) / (sum(rows_per_rank) / len(rows_per_rank))
     line = {
         "metric": "MoE-layer decode tokens/s (1 DeepSeek-V3 MoE layer, T=64, 256 FP8 experts + shared)",
         "value": round(value, 1),
@@ -340,9 +372,27 @@ def run_ours(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
+    if prefill:
+        tflops_upg = flop_upg / (upg_ms / 1e3) / 1e12
+        tflops_layer = flop_rank / (ms_step / 1e3) / 1e12
+        line["metric"] = f"MoE-layer prefill tokens/s (1 DeepSeek-V3 MoE layer, T={T}, Zipf-skewed routing)"
+        line["dtype"] = "e4m3 weights x e4m3(2-term) activations, fp32 accumulate"
+        line["config"]["workload"] = "config4_prefill_T4096_one_layer" if T == 4096 else f"config4_shape_T{T}"
+        line["config"]["router_bias"] = "2.0 * log-Zipf(s=1.2) over a seeded permutation of the 256 experts"
+        line["config"]["gemm_kernels"] = "prefill (64-row groups, 2 activation terms)"
+        line["config"]["l2"] = ("no flush: 11.3 GB of expert weights (1.4 GB per GPU at N=8) and a "
+                                f"{T * H * 2 / 1e6:.0f} MB activation batch exceed the 126 MB L2")
+        line["roofline"] = {"kernel": "grouped_prefill up/gate (tcgen05 kind::f8f6f4, 64-row groups)",
+                            "bound": "tensor", "achieved": round(tflops_upg, 1), "peak": round(fp8_peak, 1),
+                            "unit": "TFLOP/s", "frac": round(tflops_upg / fp8_peak, 4), "peak_source": fp8_kind,
+                            "flop_per_launch": flop_upg, "ms_per_launch": round(upg_ms, 4), "traffic": None}
+        line["tensor_util"] = {"flop_per_rank": flop_rank, "layer_tflops_per_gpu": round(tflops_layer, 1),
+                               "frac_of_fp8_peak": round(tflops_layer / fp8_peak, 4),
+                               "flop_whole_job": int((K + 1) * T * 3 * 2 * H * I)}
+        line["load_imbalance"] = {"rows_per_rank": rows_per_rank, "max_over_mean": round(imbalance, 3)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            line["cpu_baseline"] = cpu_reference_rate(args.cpu_sample_tokens, args.cpu_seconds)
+            line["cpu_baseline"] = cpu_reference_rate(args.cpu_sample_tokens, args.cpu_seconds, T=T, zipf=prefill)
         except Exception as exc:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": f"{type(exc).__name__}: {exc}"}
     if graph is not None:
@@ -564,7 +614,7 @@ class CpuReferenceLayer:
     route_token_real), one batch-1 call of the reference node's OpenMP FP8 expert kernels
     per (token, expert) and for the shared expert, fp32 combine (combine_outputs_torch)."""
 
-    def __init__(self, sample_tokens: int, threads: int):
+    def __init__(self, sample_tokens: int, threads: int, zipf: bool = False):
         import numpy as np
         import torch
 
@@ -577,6 +627,8 @@ class CpuReferenceLayer:
         self.refbuild = refbuild
         torch.manual_seed(0)
         gw, gb = synthetic.make_router(H, E, seed=7, device="cpu")
+        if zipf:
+            gb = synthetic.zipf_bias(E, seed=7, device="cpu")
         self.gw, self.gb = gw.numpy(), gb.numpy()
         x = synthetic.make_activations(sample_tokens, H, seed=11, device="cpu")
         self.x_bits = x.view(torch.int16).numpy().view(np.uint16)
@@ -618,9 +670,9 @@ class CpuReferenceLayer:
         return y[0]
 
 
-def cpu_reference_rate(sample_tokens: int, seconds: float):
+def cpu_reference_rate(sample_tokens: int, seconds: float, T: int = 64, zipf: bool = False):
     threads = os.cpu_count() or 1
-    layer = CpuReferenceLayer(sample_tokens, threads)
+    layer = CpuReferenceLayer(sample_tokens, threads, zipf=zipf)
     layer.run()  # warm-up (page in the weights)
     n = 0
     t0 = time.perf_counter()
@@ -632,7 +684,7 @@ def cpu_reference_rate(sample_tokens: int, seconds: float):
             break
     tok_s = n * sample_tokens / dt
     return {"value": round(tok_s, 3), "unit": "tokens/s", "cores": threads, "kind": layer.kind,
-            "sample": f"{sample_tokens} tokens of the T=64 batch through router + 8 routed + shared experts at "
+            "sample": f"{sample_tokens} tokens of the T={T} batch through router + 8 routed + shared experts at "
                       f"batch 1 per (token, expert), {n} repetitions, {dt:.1f} s",
             "ms_per_token": round(dt / (n * sample_tokens) * 1e3, 2)}
 
@@ -653,7 +705,9 @@ def run_reference(args):
               "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return
     threads = os.cpu_count() or 1
-    layer = CpuReferenceLayer(args.cpu_sample_tokens, threads)
+    prefill = args.workload == "config4"
+    T = args.tokens or (4096 if prefill else 64)
+    layer = CpuReferenceLayer(args.cpu_sample_tokens, threads, zipf=prefill)
     for _ in range(max(1, args.warmup)):
         layer.run()
     t0 = time.perf_counter()
@@ -664,7 +718,8 @@ def run_reference(args):
     ms = dt / args.steps * 1e3
     line = {
         "impl": "reference",
-        "metric": "MoE-layer decode tokens/s (1 DeepSeek-V3 MoE layer, T=64, 256 FP8 experts + shared)",
+        "metric": ("MoE-layer prefill tokens/s (1 DeepSeek-V3 MoE layer, T=4096, Zipf-skewed routing)" if prefill
+                   else "MoE-layer decode tokens/s (1 DeepSeek-V3 MoE layer, T=64, 256 FP8 experts + shared)"),
         "value": round(value, 3),
         "unit": "tokens/s",
         "n_gpus": world,
@@ -676,11 +731,12 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "fp32 (FP8 LUT decode x block scale)",
         "data": "synthetic (seeded N(0,0.02) weights, 128x128 block E4M3; RMS-normalised N(0,1) bf16 hidden)",
-        "config": {"workload": "config2_decode_T64_one_layer", "tokens": args.tokens, "routed_experts": E,
+        "config": {"workload": "config4_prefill_T4096_one_layer" if prefill else "config2_decode_T64_one_layer",
+                   "tokens": T, "routed_experts": E,
                    "shared_expert": True, "hidden": H, "inter": I, "top_k": K, "parallelism": "cpu",
                    "sample_tokens_per_step": args.cpu_sample_tokens},
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": layer.kind,
-                         "sample": f"{args.cpu_sample_tokens} tokens of the T={args.tokens} batch per step, batch 1 "
+                         "sample": f"{args.cpu_sample_tokens} tokens of the T={T} batch per step, batch 1 "
                                    "per (token, expert) through the reference node's OpenMP FP8 CPU kernels"},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
