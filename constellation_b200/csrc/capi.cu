@@ -253,7 +253,7 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     prof_mark(c, 1, s);
 
     PackActArgs px{x, x_dtype, H, w.row_token, w.groups, w.tile_group, w.meta, H, w.xfrag, w.xscale, terms};
-    CST_CUDA(launch_pack_act(px, c->num_sms, s));
+    CST_CUDA(pf ? launch_pack_rows(px, c->num_sms, s) : launch_pack_act(px, c->num_sms, s));
     prof_mark(c, 2, s);
 
     FfnArgs up{};
@@ -279,7 +279,7 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     prof_mark(c, 3, s);
 
     PackActArgs ph{w.h, kSrcUpGatePartials, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale, terms};
-    CST_CUDA(launch_pack_act(ph, c->num_sms, s));
+    CST_CUDA(pf ? launch_pack_rows(ph, c->num_sms, s) : launch_pack_act(ph, c->num_sms, s));
     prof_mark(c, 4, s);
 
     FfnArgs dn = up;

@@ -22,7 +22,7 @@ constexpr int kSplits = 3;           // E4M3 terms per activation element
 constexpr int kTileCols = 8;         // tokens per n-tile
 constexpr int kMaxTilesPerGroup = 2; // routed groups carry at most 16 rows
 constexpr int kGroupRows = kMaxTilesPerGroup * kTileCols;
-constexpr int kPrefillMaxTiles = 8;  // prefill groups carry at most 64 rows
+constexpr int kPrefillMaxTiles = 16;  // prefill groups carry at most 128 rows
 constexpr int kPrefillGroupRows = kPrefillMaxTiles * kTileCols;
 // B bytes of one n-tile for one 128-wide K block: 3 terms x 8 rows x 128 bytes
 constexpr int kBTileBytes = kSplits * kTileCols * kBlock;  // 3072

@@ -82,6 +82,10 @@ struct PackActArgs {
 constexpr int kSrcUpGatePartials = 4;
 constexpr int kMaxUpGateSplit = 4;  // largest K split of the up/gate launch
 cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream);
+// Prefill packing: two E4M3 terms and ONE power-of-two scale per packed row (written to
+// bscale[row]), so the prefill kernel promotes each K block with the weight scale alone and
+// applies the row scale once per output.  terms must be 2.
+cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t stream);
 
 // grouped_ffn.cu
 struct FfnArgs {

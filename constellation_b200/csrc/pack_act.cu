@@ -154,6 +154,84 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
     }
 }
 
+// One warp per packed row (task = (n-tile, token column)): pass 1 finds the row's max
+// |v| over all K, pass 2 writes the two terms of every K block with that row's scale.  The
+// second pass re-reads the row from L2.
+__global__ void __launch_bounds__(256) pack_rows_kernel(PackActArgs a) {
+    const int KB = a.K / kBlock;
+    const int n_tiles = a.meta->n_tiles;
+    const int split = a.src_dtype == kSrcUpGatePartials ? a.meta->split_k : 1;
+    const int lane = threadIdx.x & 31;
+    const int64_t n_tasks = int64_t(n_tiles) * kTileCols;
+    const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t task = warp_global; task < n_tasks; task += n_warps) {
+        const int tile = static_cast<int>(task / kTileCols);
+        const int j = static_cast<int>(task % kTileCols);
+        const GroupRec gr = a.groups[a.tile_group[tile]];
+        const int nt = tile - gr.tile_base;
+        const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
+        const int r = nt * kTileCols + j;
+        if (r >= gr.n_rows) continue;  // unread accumulator columns need no data
+        const int prow = gr.row_start + r;
+        const int64_t src_row = a.row_map ? a.row_map[prow] : prow;
+        float amax = 0.0f;
+        for (int kb0 = 0; kb0 < KB; kb0 += 4) {
+            float v[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (kb0 + i < KB) load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, split, v[i]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (kb0 + i < KB)
+                    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3]))));
+        }
+        amax = warp_max(amax);
+        const float s = pow2_scale_for(amax);
+        const float inv = 1.0f / s;  // exact: s is a power of two
+        const int tok = r;
+        const int TP = NT * kTileCols;
+        const int c = lane >> 2;
+        for (int kb0 = 0; kb0 < KB; kb0 += 4) {
+            float v[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (kb0 + i < KB) load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, split, v[i]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int kb = kb0 + i;
+                if (kb >= KB) break;
+                uint32_t q[2] = {0u, 0u};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float rsd = v[i][e] * inv;
+#pragma unroll
+                    for (int sp = 0; sp < 2; ++sp) {
+                        const uint8_t b = e4m3_rn(rsd);
+                        q[sp] |= uint32_t(b) << (8 * e);
+                        rsd -= e4m3_to_f32(b);
+                    }
+                }
+                // (group, kb) tile: 2 terms x TP rows x 128 B, swizzled as in pack_act_kernel
+                const int64_t gk = int64_t(gr.tile_base) * KB + int64_t(kb) * NT;
+                uint8_t* base = a.bfrag + gk * (2 * kTileCols * kBlock);
+#pragma unroll
+                for (int sp = 0; sp < 2; ++sp) {
+                    const int n = sp * TP + tok;
+                    *reinterpret_cast<uint32_t*>(base + n * kBlock + ((c ^ (n & 7)) * 16) + 4 * (lane & 3)) = q[sp];
+                }
+            }
+        }
+        if (lane == 0) a.bscale[prow] = s;
+    }
+}
+
+cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t stream) {
+    if (a.terms != 2) return cudaErrorInvalidValue;
+    pack_rows_kernel<<<num_sms * 8, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream) {
     pack_act_kernel<<<num_sms * 8, 256, 0, stream>>>(a);
     return cudaGetLastError();

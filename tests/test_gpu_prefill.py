@@ -1,4 +1,5 @@
-"""Prefill-shaped grouped kernels (64-row groups, two E4M3 activation terms) against the
+"""Prefill-shaped grouped kernels (128-row groups, two E4M3 activation terms, one scale per
+row) against the
 oracle: the dequantize-then-matmul path of the reference (server/fp8_utils.py:4-39,
 server/moe_layer_runtime.py:581-611) in fp32.
 
@@ -43,11 +44,12 @@ def make_ctx(dev, H, I, E=32, G=4, TG=2, K=4, n_slots=2, max_tokens=64, max_rows
     return ctx
 
 
-# every group size class: one n-tile, odd tile counts (N padded to 16), a full 64-row group,
+# every group size class: one n-tile, odd tile counts (N padded to 16), a full 128-row group,
 # and more rows than one group; H = 384 has an odd number of down row blocks
-@pytest.mark.parametrize("H,I,n", [(256, 128, 1), (256, 128, 9), (512, 256, 24), (384, 256, 64), (256, 384, 100)])
+@pytest.mark.parametrize("H,I,n", [(256, 128, 1), (256, 128, 9), (512, 256, 24), (384, 256, 64), (256, 384, 100),
+                                   (256, 128, 128), (512, 128, 200)])
 def test_expert_forward_prefill_vs_oracle(dev, H, I, n):
-    ctx = make_ctx(dev, H, I, max_tokens=128, max_rows=128)
+    ctx = make_ctx(dev, H, I, max_tokens=256, max_rows=256)
     e = cases.expert(900 + n, H, I)
     ctx.upload_bundle(1, 7, e)
     x = cases.activations(950 + n, n, H)
@@ -60,7 +62,7 @@ def test_expert_forward_prefill_vs_oracle(dev, H, I, n):
 
 
 def test_grouped_ffn_prefill_full_size(dev):
-    """Two DeepSeek-shaped experts with 64 and 50 rows (one full group, one partial)."""
+    """Two DeepSeek-shaped experts with 64 and 50 rows (partial groups, even and odd tiles)."""
     H, I = 7168, 2048
     ctx = make_ctx(dev, H, I, E=256, n_slots=2, max_tokens=128, max_rows=128)
     es = [cases.expert(960 + i, H, I) for i in range(2)]
