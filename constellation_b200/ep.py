@@ -64,7 +64,7 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, compute, *, rank: int, world: int, n_routed_experts: int, group=None,
-                 mode: str = "allgather"):
+                 mode: str = "allgather", local_route_min: int = 128):
         if n_routed_experts % world:
             raise ValueError(f"{n_routed_experts} experts do not shard over {world} ranks")
         if mode not in ("allgather", "alltoall"):
@@ -74,6 +74,10 @@ class ExpertParallelMoE:
         self.E = n_routed_experts
         self.epr = n_routed_experts // world
         self._slot_map = None
+        #: all-gather mode: from this many tokens per rank on, each rank routes only its own
+        #: tokens and the routes are gathered with the activations (a 2K-int row per token);
+        #: below it every rank routes the whole gathered batch and no routes move
+        self.local_route_min = int(local_route_min)
         #: set to a list to record (phase, CUDA event) pairs at the phase boundaries of forward()
         self.timeline: list | None = None
 
@@ -117,13 +121,26 @@ class ExpertParallelMoE:
     def _allgather(self, x_local, gate_weight, bias, resident, residual, od) -> torch.Tensor:
         Tl, H = x_local.shape
         x_all = torch.empty((self.world * Tl, H), dtype=x_local.dtype, device=x_local.device)
-        dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
-        self._mark("all_gather")
-        # Every rank routes the whole gathered batch itself: the router is deterministic and
-        # its inputs are identical on all ranks, so all ranks agree on every route without
-        # exchanging them.
-        idx_all, w_all = self.c.route(x_all, gate_weight, bias, resident=resident)
-        self._mark("route")
+        if Tl >= self.local_route_min:
+            # prefill-sized batches: route the own tokens, gather routes with the rows
+            idx_l, w_l = self.c.route(x_local, gate_weight, bias, resident=resident)
+            self._mark("route")
+            K = idx_l.shape[1]
+            meta = torch.cat([idx_l.to(torch.int32), w_l.view(torch.int32)], dim=1).contiguous()
+            meta_all = torch.empty((self.world * Tl, 2 * K), dtype=torch.int32, device=x_local.device)
+            dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
+            dist.all_gather_into_tensor(meta_all, meta, group=self.group)
+            idx_all = meta_all[:, :K].contiguous()
+            w_all = meta_all[:, K:].contiguous().view(torch.float32)
+            self._mark("all_gather")
+        else:
+            dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
+            self._mark("all_gather")
+            # Every rank routes the whole gathered batch itself: the router is deterministic
+            # per token and its inputs are identical on all ranks, so all ranks agree on every
+            # route without exchanging them.
+            idx_all, w_all = self.c.route(x_all, gate_weight, bias, resident=resident)
+            self._mark("route")
         # this rank's experts on every gathered row, the shared expert on its own tokens only
         lo = self.rank * Tl
         partial = self.c.moe_routed_range(x_all, idx_all, w_all, lo, lo + Tl, out_dtype=torch.float32)

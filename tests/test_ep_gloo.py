@@ -111,7 +111,11 @@ def _worker(rank, world, port, mode, q):
         shared = cases.expert(2999, H, I)
         epr = E // world
         comp = OracleCompute(rank * epr, (rank + 1) * epr, experts, shared)
-        moe = ExpertParallelMoE(comp, rank=rank, world=world, n_routed_experts=E, mode=mode)
+        # "allgather_local": each rank routes its own tokens and the routes are gathered
+        # (the prefill-sized path), forced here by a one-token threshold
+        local = mode == "allgather_local"
+        moe = ExpertParallelMoE(comp, rank=rank, world=world, n_routed_experts=E,
+                                mode="allgather" if local else mode, local_route_min=1 if local else 128)
         Tl = T // world
         out = moe.forward(x[rank * Tl:(rank + 1) * Tl].to(torch.bfloat16), gw, gb, out_dtype=torch.float32)
         q.put((rank, out.numpy()))
@@ -119,7 +123,7 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["allgather", "alltoall"])
+@pytest.mark.parametrize("mode", ["allgather", "allgather_local", "alltoall"])
 def test_ep_two_ranks_matches_single_process_oracle(mode):
     from oracle import cases
     from oracle.expert import DequantExpert

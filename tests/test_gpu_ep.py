@@ -55,8 +55,11 @@ def _rank_main(rank, world, port, q):
         Tl = T // world
         xl = x[rank * Tl:(rank + 1) * Tl].contiguous()
         res = {}
-        for mode in ("allgather", "alltoall"):
-            moe = ExpertParallelMoE(ctx, rank=rank, world=world, n_routed_experts=E, mode=mode)
+        for mode in ("allgather", "allgather_local", "alltoall"):
+            # allgather_local: own-token routing + gathered routes (the prefill-sized path)
+            local = mode == "allgather_local"
+            moe = ExpertParallelMoE(ctx, rank=rank, world=world, n_routed_experts=E,
+                                    mode="allgather" if local else mode, local_route_min=1 if local else 128)
             res[mode] = moe.forward(xl, gw, gb, out_dtype=torch.float32).cpu().numpy()
         torch.cuda.synchronize()
         ctx.device_error()
@@ -92,8 +95,11 @@ def test_ep_two_gpus_both_modes():
     x = cases.activations(82, T, H)
     ref = moe_layer(x, w, b, {e: DequantExpert(cases.expert(3000 + e, H, I)) for e in range(E)},
                     DequantExpert(cases.expert(3999, H, I)), n_group=G, topk_group=TG, top_k=K)
-    for mode in ("allgather", "alltoall"):
+    for mode in ("allgather", "allgather_local", "alltoall"):
         out = np.concatenate([got[r][mode] for r in range(world)])
         num = np.abs(out - ref.out_f32).max(axis=1)
         den = np.abs(ref.out_f32).max(axis=1)
         assert float((num / den).max()) < 2e-3, mode
+    # routing locally and gathering the routes gives the same routes, hence the same bits
+    for r in range(world):
+        assert np.array_equal(got[r]["allgather"], got[r]["allgather_local"])
