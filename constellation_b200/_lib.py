@@ -32,7 +32,7 @@ EXPORTED = (
     "cst_set_shared_slot", "cst_route", "cst_moe_routed", "cst_moe_layer", "cst_grouped_ffn",
     "cst_expert_forward", "cst_device_error", "cst_ctx_info", "cst_last_error", "cst_abi_version",
     "cst_profile_enable", "cst_profile_read", "cst_shared_combine", "cst_combine_rows", "cst_dequant_fp8",
-    "cst_route_noalloc", "cst_moe_routed_range", "cst_set_gemm_mode",
+    "cst_route_noalloc", "cst_moe_routed_range", "cst_set_gemm_mode", "cst_rmsnorm",
 )
 CST_GEMM_AUTO, CST_GEMM_DECODE, CST_GEMM_PREFILL = 0, 1, 2
 CST_N_STAGES = 7
@@ -92,6 +92,7 @@ def _load() -> ctypes.CDLL:
         "cst_find_slot": (I32, [P, I32]),
         "cst_set_shared_slot": (ctypes.c_int, [P, I32]),
         "cst_set_gemm_mode": (ctypes.c_int, [P, I32]),
+        "cst_rmsnorm": (ctypes.c_int, [P, I32, I32, I32, P, ctypes.c_float, P, I32, P]),
         "cst_route": (ctypes.c_int, [P, P, I32, I32, P, P, P, I32, P, P, P, P, P]),
         "cst_moe_routed": (ctypes.c_int, [P, P, I32, I32, P, P, I32, U32, P, I32, P]),
         "cst_moe_routed_range": (ctypes.c_int, [P, P, I32, I32, P, P, I32, I32, I32, P, I32, P]),

@@ -63,6 +63,26 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def rms_norm(x: torch.Tensor, weight: torch.Tensor | None = None, eps: float = 1e-6, *,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """``torch.nn.functional.rms_norm(x, (H,), weight, eps)`` on ``x [T, H]`` (``cst_rmsnorm``:
+    fp32 math, one rounding); the prenorm before each sparse FFN
+    (server/full_model_runtime.py:271-276).  ``weight`` is fp32 ``[H]`` or None."""
+    if not isinstance(x, torch.Tensor) or x.dim() != 2 or not x.is_cuda:
+        raise TypeError("rms_norm expects a 2-D CUDA tensor")
+    x = x.contiguous()
+    if weight is not None:
+        if weight.dtype != torch.float32 or weight.shape != (x.shape[1],) or weight.device != x.device:
+            raise RuntimeError("weight must be fp32 [H] on the device of x")
+        weight = weight.contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        check(_lib.lib.cst_rmsnorm(x.data_ptr(), dtype_code(x.dtype), x.shape[0], x.shape[1], _ptr(weight),
+                                   ctypes.c_float(eps), out.data_ptr(), dtype_code(out.dtype), _stream(x.device)))
+    return out
+
+
 class ExpertContext:
     """Expert arena + workspace of one CUDA device (``cst_create``)."""
 

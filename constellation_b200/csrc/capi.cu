@@ -726,6 +726,18 @@ int cst_dequant_fp8(const uint8_t* w, const float* scale_inv, int32_t rows, int3
     return CST_OK;
 }
 
+int cst_rmsnorm(const void* x, int32_t x_dtype, int32_t T, int32_t H, const float* weight, float eps, void* out,
+                int32_t out_dtype, void* stream) {
+    g_last_error.clear();
+    if (!x || !out) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
+    if (T < 0 || H <= 0 || H % 8) return fail(CST_ERR_INVALID_ARG, "bad shape (T=%d, H=%d; H must be a multiple of 8)", T, H);
+    if (!(eps >= 0.0f)) return fail(CST_ERR_INVALID_ARG, "eps must be >= 0");
+    if (!aligned16(x) || !aligned16(out)) return fail(CST_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+    CST_CUDA(launch_rmsnorm(x, x_dtype, T, H, weight, eps, out, out_dtype, static_cast<cudaStream_t>(stream)));
+    return CST_OK;
+}
+
 int cst_device_error(cst_ctx* c) {
     g_last_error.clear();
     if (int rc = check_ctx(c)) return rc;

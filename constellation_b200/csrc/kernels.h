@@ -118,6 +118,11 @@ cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaS
 cudaError_t grouped_prefill_init_attributes();
 cudaError_t launch_grouped_prefill(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream);
 
+// norm.cu: out = x * rsqrt(mean(x^2) + eps) * weight (weight may be null), per row of H
+// (H a multiple of 8, 16-byte aligned rows)
+cudaError_t launch_rmsnorm(const void* x, int x_dtype, int T, int H, const float* weight, float eps, void* out,
+                           int out_dtype, cudaStream_t stream);
+
 // combine.cu
 struct CombineArgs {
     const float* y;         // [rows, H] fp32 weighted expert outputs

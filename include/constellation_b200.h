@@ -218,6 +218,14 @@ int cst_combine_rows(cst_ctx* ctx, const float* rows, int64_t ld_rows, const int
 int cst_dequant_fp8(const uint8_t* w, const float* scale_inv, int32_t rows, int32_t cols, int32_t block,
                     float* out, void* stream);
 
+/* out[t, :] = x[t, :] * rsqrt(mean(x[t, :]^2) + eps) * weight on the current device: the
+ * prenorm before the sparse FFN, torch.nn.functional.rms_norm(h, (H,), weight, 1e-6)
+ * (server/full_model_runtime.py:271-276), fp32 math and one final RNE cast.  x, out
+ * [T, H] in x_dtype / out_dtype (16-byte aligned, H a multiple of 8); weight [H] fp32 or
+ * NULL (all ones).  x == out is allowed. */
+int cst_rmsnorm(const void* x, int32_t x_dtype, int32_t T, int32_t H, const float* weight, float eps, void* out,
+                int32_t out_dtype, void* stream);
+
 /* Synchronises the context's device, then returns CST_OK or CST_ERR_DEVICE_TIMEOUT if a
  * kernel's bounded wait gave up since the last call (and clears the flag). */
 int cst_device_error(cst_ctx* ctx);

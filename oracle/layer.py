@@ -75,4 +75,19 @@ def rms_norm(x: np.ndarray, weight: np.ndarray | None = None, eps: float = 1e-6)
     return y
 
 
-__all__ = ["LayerResult", "moe_layer", "bf16_round", "rms_norm", "DequantExpert"]
+def moe_stack(h: np.ndarray, layers, *, n_group: int, topk_group: int, top_k: int, eps: float = 1e-6,
+              routed_scaling_factor: float = 2.5) -> np.ndarray:
+    """Stacked sparse layers without attention: per layer ``xn = bf16(rms_norm(h, w))``
+    (the prenorm, ``server/full_model_runtime.py:271-276``) and ``h = bf16(h + routed +
+    shared)`` (``:348-355``), every sum in fp32 and one bf16 rounding per tensor handed on.
+    ``layers``: sequence of ``(gate_weight, bias, experts, shared, norm_weight)``."""
+    h = bf16_round(np.atleast_2d(np.asarray(h, dtype=np.float32)))
+    for gate_weight, bias, experts, shared, norm_weight in layers:
+        xn = bf16_round(rms_norm(h, norm_weight, eps))
+        r = moe_layer(xn, gate_weight, bias, experts, shared, n_group=n_group, topk_group=topk_group, top_k=top_k,
+                      routed_scaling_factor=routed_scaling_factor)
+        h = bf16_round((h + r.out_f32).astype(np.float32))
+    return h
+
+
+__all__ = ["LayerResult", "moe_layer", "moe_stack", "bf16_round", "rms_norm", "DequantExpert"]

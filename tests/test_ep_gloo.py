@@ -164,3 +164,66 @@ def test_plan_dispatch_orders_by_owner_and_inverts():
 def test_ep_rejects_uneven_sharding():
     with pytest.raises(ValueError):
         ExpertParallelMoE(object(), rank=0, world=3, n_routed_experts=16)
+
+
+# ---------------------------------------------------------------------------------------
+def _cpu_rms_norm(h, weight, eps):
+    hf = h.float()
+    y = hf * torch.rsqrt(hf.pow(2).mean(dim=-1, keepdim=True) + eps)
+    if weight is not None:
+        y = y * weight
+    return y.to(h.dtype)
+
+
+def _stack_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from constellation_b200.stack import MoEStack, StackLayer
+        from oracle import cases
+
+        T, L = 6, 2
+        epr = E // world
+        layers = []
+        for l in range(L):
+            gw, gb = (torch.from_numpy(a) for a in cases.router(70 + l, E, H, bias_std=0.05))
+            experts = {e: cases.expert(5000 + 100 * l + e, H, I) for e in range(E)}
+            comp = OracleCompute(rank * epr, (rank + 1) * epr, experts, cases.expert(5099 + 100 * l, H, I))
+            nw = torch.from_numpy(1.0 + 0.1 * cases.activations(80 + l, 1, H)[0])
+            layers.append(StackLayer(comp, gw, gb, nw))
+        stack = MoEStack(layers, rank=rank, world=world, n_routed_experts=E, norm=_cpu_rms_norm)
+        h = torch.from_numpy(cases.activations(90, T, H)).to(torch.bfloat16)
+        Tl = T // world
+        out = stack.forward(h[rank * Tl:(rank + 1) * Tl].contiguous())
+        q.put((rank, out.float().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_moe_stack_two_ranks_matches_oracle():
+    """Two stacked layers (prenorm + MoE + residual) over 2 gloo ranks = the oracle stack."""
+    from oracle import cases
+    from oracle.expert import DequantExpert
+    from oracle.layer import moe_stack
+
+    world, T, L = 2, 6, 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_stack_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    out = np.concatenate([got[r] for r in range(world)])
+    layers = []
+    for l in range(L):
+        w, b = cases.router(70 + l, E, H, bias_std=0.05)
+        ex = {e: DequantExpert(cases.expert(5000 + 100 * l + e, H, I)) for e in range(E)}
+        nw = (1.0 + 0.1 * cases.activations(80 + l, 1, H)[0]).astype(np.float32)
+        layers.append((w, b, ex, DequantExpert(cases.expert(5099 + 100 * l, H, I)), nw))
+    ref = moe_stack(cases.activations(90, T, H), layers, n_group=G, topk_group=TG, top_k=K)
+    rel = np.abs(out - ref).max(axis=1) / np.abs(ref).max(axis=1)
+    assert float(rel.max()) < 1e-2
