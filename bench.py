@@ -877,6 +877,21 @@ def run_reference(args):
               "cpu_baseline": base,
               "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return
+    if args.workload == "config3":
+        # one token through one layer of the reference CPU path, times the layer count
+        base = cpu_reference_rate(args.cpu_sample_tokens, args.cpu_seconds, T=args.tokens or 128)
+        L, T3 = args.layers, args.tokens or 128
+        v = base["value"] / L
+        emit({"impl": "reference", "metric": f"MoE decode step tokens/s ({L} stacked DeepSeek-V3 MoE layers, "
+              f"T={T3})", "value": round(v, 4), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+              "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+              "dtype": "fp32 (FP8 LUT decode x block scale)", "data": "synthetic",
+              "config": {"workload": "config3_decode_stack" if L == 58 else f"config3_shape_{L}_layers",
+                         "layers": L, "tokens": T3, "parallelism": "cpu"},
+              "cpu_baseline": dict(base, value=round(v, 4),
+                                   sample=base["sample"] + f"; per step x {L} layers (extrapolated)"),
+              "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+        return
     threads = os.cpu_count() or 1
     prefill = args.workload == "config4"
     T = args.tokens or (4096 if prefill else 64)
