@@ -285,6 +285,92 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(RouterArg
     }
 }
 
+// One CTA per token, one thread per expert (blockDim = E rounded up to a warp).  The same
+// arithmetic as router_select_kernel, reorganised so that no step is a long chain of
+// dependent shuffles: group top-2 is one warp reduction per group (epg == 32) or a short
+// scan, the kept groups and the top-k experts are found by RANK -- an entry's position in
+// (value desc, index asc) order is the number of entries ahead of it -- and the k chosen
+// experts are written in rank order.  The normaliser adds the chosen unbiased scores in
+// that order, as the warp version does, so both give bit-identical results.
+__global__ void __launch_bounds__(1024) router_select_rank_kernel(RouterArgs a) {
+    __shared__ float s_choice[kMaxE];
+    __shared__ float s_score[kMaxE];
+    __shared__ float s_gs[32];
+    __shared__ int s_keep[32];
+    __shared__ int s_sel[16];
+    const int t = blockIdx.x;
+    const int e = threadIdx.x;
+    const int E = a.E;
+    const int epg = E / a.n_group;
+    const int lane = e & 31, warp = e >> 5;
+    float ch = -INFINITY;
+    if (e < E) {
+        const float l = a.logits[int64_t(t) * E + e];
+        const float sg = 1.0f / (1.0f + expf(-l));
+        const bool res = (a.resident == nullptr) || (a.resident[e] != 0);
+        ch = res ? (sg + a.bias[e]) : -INFINITY;
+        s_choice[e] = ch;
+        s_score[e] = res ? sg : 0.0f;
+    }
+    // group scores: sum of the two largest choice values of each group
+    if (epg == 32 && (E & 31) == 0) {
+        float m1 = ch, m2 = -INFINITY;
+        warp_top2(m1, m2);
+        if (lane == 0 && warp < a.n_group) s_gs[warp] = m1 + m2;
+        __syncthreads();
+    } else {
+        __syncthreads();
+        if (e < a.n_group) {
+            float m1 = -INFINITY, m2 = -INFINITY;
+            for (int j = 0; j < epg; ++j) {
+                const float v = s_choice[e * epg + j];
+                if (v > m1) {
+                    m2 = m1;
+                    m1 = v;
+                } else if (v > m2) {
+                    m2 = v;
+                }
+            }
+            s_gs[e] = m1 + m2;
+        }
+        __syncthreads();
+    }
+    // keep the topk_group best groups (value desc, index asc)
+    if (e < a.n_group) {
+        const float g = s_gs[e];
+        int rank = 0;
+        for (int j = 0; j < a.n_group; ++j) {
+            const float o = s_gs[j];
+            rank += (o > g) || (o == g && j < e);
+        }
+        s_keep[e] = rank < a.topk_group;
+        if (a.group_scores_out) a.group_scores_out[int64_t(t) * a.n_group + e] = g;
+    }
+    __syncthreads();
+    // candidates: choice values of experts in kept groups, -inf elsewhere; rank each one
+    if (e < E) s_choice[e] = s_keep[e / epg] ? ch : -INFINITY;
+    __syncthreads();
+    if (e < E) {
+        const float c = s_choice[e];
+        int rank = 0;
+        for (int j = 0; j < E; ++j) {
+            const float o = s_choice[j];
+            rank += (o > c) || (o == c && j < e);
+        }
+        if (rank < a.top_k) s_sel[rank] = e;
+    }
+    __syncthreads();
+    if (e < a.top_k) {
+        float denom = 0.0f;
+        for (int r = 0; r < a.top_k; ++r) denom += s_score[s_sel[r]];  // in selection order
+        float wv = s_score[s_sel[e]];
+        if (a.norm && a.top_k > 1) wv = wv / (denom + 1e-20f);
+        wv = wv * a.scale;
+        a.topk_idx[int64_t(t) * a.top_k + e] = s_sel[e];
+        a.topk_w[int64_t(t) * a.top_k + e] = wv;
+    }
+}
+
 // x_dtype: 1 fp16, 2 bf16, 3 fp32.  `logits` receives [T, E] fp32 (scratch or the caller's).
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
                           int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
@@ -303,11 +389,17 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
     }
     RouterArgs a{logits, bias, resident, T, E, n_group, topk_group, top_k, norm, scale,
                  topk_idx, topk_w, group_scores_out};
-    const int grid_sel = (T + kSelWarps - 1) / kSelWarps;
-    if (E <= 256) {
-        router_select_kernel<8><<<grid_sel, kSelWarps * 32, 0, stream>>>(a);
+    if (T <= 2048) {
+        // decode-sized batches: one CTA per token, short dependency chains
+        router_select_rank_kernel<<<T, (E + 31) / 32 * 32, 0, stream>>>(a);
     } else {
-        router_select_kernel<32><<<grid_sel, kSelWarps * 32, 0, stream>>>(a);
+        // large batches: one warp per token keeps the grid small
+        const int grid_sel = (T + kSelWarps - 1) / kSelWarps;
+        if (E <= 256) {
+            router_select_kernel<8><<<grid_sel, kSelWarps * 32, 0, stream>>>(a);
+        } else {
+            router_select_kernel<32><<<grid_sel, kSelWarps * 32, 0, stream>>>(a);
+        }
     }
     return cudaGetLastError();
 }
