@@ -8,14 +8,16 @@
 // slot are cut into groups of at most 16 rows (two 8-wide MMA n-tiles) that the grouped
 // FFN kernels consume.
 //
-// Decode-sized calls (<= 2048 routes): one CTA of 1024 threads.  Each route is encoded as
-// a 31-bit key
-//   slot << 18 | token << 4 | k        (k == top_k marks the shared expert)
-// and every key's rank is counted in shared memory, which makes the packing fully
-// deterministic (no atomics decide an order).  Routes whose expert is not resident
-// here get key 0x7fffffff and sort to the end (under expert parallelism they belong to
-// another rank).  Larger calls take the three-launch counting sort below, which yields
-// the same rows in the same order.
+// Decode-sized calls (<= 2048 routes, <= 1024 slots): one CTA of 1024 threads runs a stable
+// counting sort by slot.  Warp w owns a contiguous block of routes and counts its routes per
+// slot; one pass over the slots turns the per-warp counts into running offsets (warp order)
+// and block scans give every slot's first row, group and tile; each warp then places its
+// routes in order -- __match_any_sync groups the lanes of a 32-route chunk by slot, and a
+// lane's position is its slot's running offset plus the number of lower peer lanes.  Rows
+// are therefore sorted by (slot, token, k); no atomic decides an order (they only count).
+// Routes whose expert is not resident here get no row (under expert parallelism they
+// belong to another rank).  Larger calls take the three-launch counting sort below, which
+// yields the same rows in the same order.
 #include <cstdint>
 
 #include "cst_common.cuh"
@@ -25,9 +27,10 @@
 namespace cst {
 
 constexpr int kPackThreads = 1024;
-constexpr uint32_t kInvalidKey = 0x7fffffffu;
-constexpr int kRankSortMaxKeys = 2048;  // up to here one CTA ranks the keys; beyond, the counting sort
-constexpr int kRoutePackMaxSmem = 2 * kRankSortMaxKeys * 4 + 8192 * 4;
+constexpr int kRankSortMaxKeys = 2048;  // up to here one CTA packs; beyond, the three-launch counting sort
+constexpr int kPackWarps = kPackThreads / 32;
+constexpr int kPackMaxSlotsOneCta = 1024;  // more slots: the multi-CTA counting sort
+constexpr int kRoutePackMaxSmem = (kRankSortMaxKeys + (kPackWarps + 2) * kPackMaxSlotsOneCta) * 4;
 
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* total) {
@@ -77,106 +80,104 @@ __device__ __forceinline__ int route_slot(const PackArgs& a, bool mode_rows, int
     return (slot >= 0 && slot < a.n_slots) ? slot : -1;
 }
 
-__global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a, int n_keys_pow2) {
-    // keys and the ranked output (2 x kRankSortMaxKeys), then n_slots ints
-    extern __shared__ uint32_t s_keys[];
-    int* s_first = reinterpret_cast<int*>(s_keys + 2 * kRankSortMaxKeys);
+__global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a) {
+    // shared: route slots [kRankSortMaxKeys]; per (warp, slot) counts, then running offsets
+    // [32][n_slots]; per slot: count, first row
+    extern __shared__ int s_mem[];
+    int* s_slot = s_mem;
+    int* s_wcnt = s_slot + kRankSortMaxKeys;
+    int* s_cnt = s_wcnt + kPackWarps * a.n_slots;
+    int* s_first = s_cnt + a.n_slots;
     __shared__ int s_warp[32];
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
     const int K1 = mode_rows ? 1 : a.K + 1;
     const int n_routes = mode_rows ? a.T : a.T * K1;
-
-    for (int i = tid; i < a.n_slots; i += kPackThreads) s_first[i] = 0x7fffffff;
-    for (int i = tid; i < a.T * K1; i += kPackThreads) a.tk_row[i] = -1;
-    // build keys
-    for (int i = tid; i < n_keys_pow2; i += kPackThreads) {
-        uint32_t key = kInvalidKey;
-        if (i < n_routes) {
-            int t, k;
-            const int slot = route_slot(a, mode_rows, K1, i, &t, &k);
-            if (slot >= 0) key = (uint32_t(slot) << 18) | (uint32_t(t) << 4) | uint32_t(k);
-        }
-        s_keys[i] = key;
+    const int G = a.group_rows;
+    // warp w owns the contiguous routes [w B, w B + B): keeping them in order inside the
+    // warp and the warps in order keeps every slot's rows in route order
+    const int B = (n_routes + kPackWarps - 1) / kPackWarps;
+    const int r_begin = warp * B, r_end = min(n_routes, r_begin + B);
+    for (int i = tid; i < kPackWarps * a.n_slots; i += kPackThreads) s_wcnt[i] = 0;
+    for (int i = tid; i < n_routes; i += kPackThreads) {
+        int t, k;
+        s_slot[i] = route_slot(a, mode_rows, K1, i, &t, &k);
     }
     __syncthreads();
-    {
-        // every valid key's position is the number of smaller keys (keys are unique): one
-        // pass of n compares per key instead of log^2 n barriers of a sorting network
-        uint32_t* s_out = s_keys + kRankSortMaxKeys;
-        for (int i = tid; i < n_keys_pow2; i += kPackThreads) s_out[i] = kInvalidKey;
-        __syncthreads();
-        for (int i = tid; i < n_routes; i += kPackThreads) {
-            const uint32_t key = s_keys[i];
-            if (key == kInvalidKey) continue;
-            int rank = 0;
-            for (int j = 0; j < n_routes; ++j) rank += s_keys[j] < key;
-            s_out[rank] = key;
+    for (int i = r_begin + lane; i < r_end; i += 32) {
+        const int sl = s_slot[i];
+        if (sl >= 0) atomicAdd(&s_wcnt[warp * a.n_slots + sl], 1);  // counts: order immaterial
+    }
+    __syncthreads();
+    // per slot: total, and each warp's running offset inside the slot (warp order)
+    for (int sl = tid; sl < a.n_slots; sl += kPackThreads) {
+        int run = 0;
+        for (int w = 0; w < kPackWarps; ++w) {
+            const int v = s_wcnt[w * a.n_slots + sl];
+            s_wcnt[w * a.n_slots + sl] = run;
+            run += v;
         }
-        __syncthreads();
-        for (int i = tid; i < n_keys_pow2; i += kPackThreads) s_keys[i] = s_out[i];
-        __syncthreads();
+        s_cnt[sl] = run;
     }
-    // number of valid rows and the first row of each slot
-    int valid_local = 0;
-    for (int i = tid; i < n_keys_pow2; i += kPackThreads) {
-        const uint32_t key = s_keys[i];
-        if (key != kInvalidKey) {
-            ++valid_local;
-            const int slot = int(key >> 18);
-            if (i == 0 || (s_keys[i - 1] >> 18) != uint32_t(slot)) s_first[slot] = i;
-        }
+    __syncthreads();
+    // first row / group / tile of every slot: block scans over contiguous slot ranges
+    const int per = (a.n_slots + kPackThreads - 1) / kPackThreads;
+    const int s0 = min(a.n_slots, tid * per), s1 = min(a.n_slots, s0 + per);
+    int rows_l = 0, groups_l = 0, tiles_l = 0;
+    for (int sl = s0; sl < s1; ++sl) {
+        const int n = s_cnt[sl];
+        rows_l += n;
+        groups_l += (n + G - 1) / G;
+        tiles_l += (n / G) * ((G + kTileCols - 1) / kTileCols) + ((n % G) + kTileCols - 1) / kTileCols;
     }
-    int n_rows;
-    block_exclusive_scan(valid_local, s_warp, &n_rows);
-    // group starts: every 16th row of a slot run, in row order.  Each thread owns a
-    // contiguous range of rows so that one block scan numbers the groups.
-    const int per = (n_rows + kPackThreads - 1) / kPackThreads;
-    const int r0 = tid * per, r1 = min(n_rows, r0 + per);
-    int starts = 0;
-    for (int p = r0; p < r1; ++p) {
-        const int slot = int(s_keys[p] >> 18);
-        if (((p - s_first[slot]) % a.group_rows) == 0) ++starts;
-    }
-    int n_groups;
-    int g = block_exclusive_scan(starts, s_warp, &n_groups);
-    // per-group row counts -> tile counts; each group start writes its record
-    int tiles_local = 0;
-    for (int p = r0; p < r1; ++p) {
-        const int slot = int(s_keys[p] >> 18);
-        if (((p - s_first[slot]) % a.group_rows) == 0) {
-            int end = p + 1;
-            while (end < n_rows && end < p + a.group_rows && int(s_keys[end] >> 18) == slot) ++end;
-            tiles_local += (end - p + kTileCols - 1) / kTileCols;
-        }
-    }
-    int n_tiles;
-    int tile = block_exclusive_scan(tiles_local, s_warp, &n_tiles);
+    int n_rows, n_groups, n_tiles;
+    int row = block_exclusive_scan(rows_l, s_warp, &n_rows);
+    int g = block_exclusive_scan(groups_l, s_warp, &n_groups);
+    int tile = block_exclusive_scan(tiles_l, s_warp, &n_tiles);
     const bool overflow = (n_rows > a.max_rows) || (n_groups > a.max_groups);
-    if (!overflow) {
-        for (int p = r0; p < r1; ++p) {
-            const uint32_t key = s_keys[p];
-            const int slot = int(key >> 18);
-            const int t = int((key >> 4) & 0x3fff);
-            const int k = int(key & 15);
-            a.row_token[p] = t;
-            float wt = 1.0f;
-            if (mode_rows) {
-                if (a.row_weight_in) wt = a.row_weight_in[t];
-            } else if (k < a.K) {
-                wt = a.topk_w[t * a.K + k];
-            }
-            a.row_weight[p] = wt;
-            a.tk_row[t * K1 + k] = p;
-            if (((p - s_first[slot]) % a.group_rows) == 0) {
-                int end = p + 1;
-                while (end < n_rows && end < p + a.group_rows && int(s_keys[end] >> 18) == slot) ++end;
-                const int nt = (end - p + kTileCols - 1) / kTileCols;
-                a.groups[g] = GroupRec{slot, p, end - p, tile};
-                for (int j = 0; j < nt; ++j) a.tile_group[tile + j] = g;
+    for (int sl = s0; sl < s1; ++sl) {
+        const int n = s_cnt[sl];
+        s_first[sl] = row;
+        if (!overflow) {
+            for (int j = 0; j * G < n; ++j) {
+                const int rows = min(G, n - j * G);
+                const int nt = (rows + kTileCols - 1) / kTileCols;
+                a.groups[g] = GroupRec{sl, row + j * G, rows, tile};
+                for (int q = 0; q < nt; ++q) a.tile_group[tile + q] = g;
                 ++g;
                 tile += nt;
             }
+        }
+        row += n;
+    }
+    __syncthreads();
+    // place every route: slot order, then route (= token, k) order inside a slot
+    for (int i = tid; i < n_routes; i += kPackThreads)
+        if (s_slot[i] < 0 || overflow) a.tk_row[i] = -1;
+    if (!overflow) {
+        for (int c = r_begin; c < r_end; c += 32) {
+            const int i = c + lane;
+            const int sl = i < r_end ? s_slot[i] : -1;
+            const uint32_t peers = __match_any_sync(0xffffffffu, sl);
+            int base = 0;
+            if (sl >= 0) {
+                base = s_wcnt[warp * a.n_slots + sl];
+                const int p = s_first[sl] + base + __popc(peers & ((1u << lane) - 1u));
+                const int t = mode_rows ? i : i / K1;
+                const int k = mode_rows ? 0 : i % K1;
+                a.row_token[p] = t;
+                float wt = 1.0f;
+                if (mode_rows) {
+                    if (a.row_weight_in) wt = a.row_weight_in[t];
+                } else if (k < a.K) {
+                    wt = a.topk_w[t * a.K + k];
+                }
+                a.row_weight[p] = wt;
+                a.tk_row[i] = p;  // i = t * K1 + k
+            }
+            __syncwarp();
+            if (sl >= 0 && lane == __ffs(peers) - 1) s_wcnt[warp * a.n_slots + sl] = base + __popc(peers);
+            __syncwarp();
         }
     }
     if (tid == 0) {
@@ -310,23 +311,12 @@ cudaError_t route_pack_init_attributes() {
                                 kRoutePackMaxSmem);
 }
 
-int route_pack_pow2(int n) {
-    int p = 1;
-    while (p < n) p <<= 1;
-    return p < 64 ? 64 : p;
-}
-
-size_t route_pack_smem(int n_keys_pow2, int n_slots) {
-    (void)n_keys_pow2;
-    return size_t(2 * kRankSortMaxKeys) * 4 + size_t(n_slots) * 4;
-}
-
 int route_pack_chunks(int n_routes) { return (n_routes + kPackThreads - 1) / kPackThreads; }
 
 cudaError_t launch_route_pack(const PackArgs& a, cudaStream_t stream) {
     const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
     const int n_routes = mode_rows ? a.T : a.T * (a.K + 1);
-    if (n_routes > kRankSortMaxKeys) {
+    if (n_routes > kRankSortMaxKeys || a.n_slots > kPackMaxSlotsOneCta) {
         const int chunks = route_pack_chunks(n_routes);
         if (int64_t(chunks) * a.n_slots > a.hist_cap) return cudaErrorInvalidValue;
         const size_t hs = size_t(a.n_slots) * sizeof(int);
@@ -335,9 +325,8 @@ cudaError_t launch_route_pack(const PackArgs& a, cudaStream_t stream) {
         route_scatter_kernel<<<chunks, kPackThreads, 0, stream>>>(a);
         return cudaGetLastError();
     }
-    const int p2 = route_pack_pow2(n_routes);
-    const size_t smem = route_pack_smem(p2, a.n_slots);
-    route_pack_kernel<<<1, kPackThreads, smem, stream>>>(a, p2);
+    const size_t smem = size_t(kRankSortMaxKeys + (kPackWarps + 2) * a.n_slots) * sizeof(int);
+    route_pack_kernel<<<1, kPackThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
