@@ -63,7 +63,8 @@ namespace {
     } while (0)
 
 struct Workspace {
-    float* router_logits = nullptr;   // [max_tokens, E]
+    float* router_logits = nullptr;   // router partial logits (router_cap floats)
+    int64_t router_cap = 0;
     int32_t* topk_idx = nullptr;      // [max_tokens, 16]
     float* topk_w = nullptr;
     GroupRec* groups = nullptr;       // [max_rows]
@@ -176,9 +177,12 @@ int alloc_workspace(cst_ctx* c) {
     Workspace& w = c->ws;
     const size_t tk = size_t(std::max<int64_t>(int64_t(f.max_tokens) * 16, R));
     const int64_t max_routes = std::max<int64_t>(int64_t(f.max_tokens) * (f.top_k + 1), R);
+    // the router's largest K split of any batch up to max_tokens (bf16 activations)
+    w.router_cap = int64_t(f.max_tokens) * E;
+    for (int t = 1; t <= f.max_tokens; ++t) w.router_cap = std::max(w.router_cap, router_scratch_floats(2, t, E, H));
     w.hist_cap = ((max_routes + 1023) / 1024) * std::max(f.n_slots, 1);
     std::vector<Piece> pieces = {
-        {reinterpret_cast<void**>(&w.router_logits), size_t(f.max_tokens) * E * 4},
+        {reinterpret_cast<void**>(&w.router_logits), size_t(w.router_cap) * 4},
         {reinterpret_cast<void**>(&w.topk_idx), size_t(f.max_tokens) * 16 * 4},
         {reinterpret_cast<void**>(&w.topk_w), size_t(f.max_tokens) * 16 * 4},
         {reinterpret_cast<void**>(&w.groups), size_t(R) * sizeof(GroupRec)},
@@ -500,8 +504,9 @@ int cst_route(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float
     const cst_config& f = c->cfg;
     CST_CUDA(launch_router(x, x_dtype, gate_weight, bias, resident, T, f.n_routed_experts, f.hidden_dim, f.n_group,
                            f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor,
-                           logits ? logits : c->ws.router_logits, topk_idx, topk_weight, group_scores,
-                           static_cast<cudaStream_t>(stream)));
+                           logits ? logits : c->ws.router_logits,
+                           logits ? int64_t(T) * f.n_routed_experts : c->ws.router_cap, topk_idx, topk_weight,
+                           group_scores, c->ws.err, static_cast<cudaStream_t>(stream)));
     return CST_OK;
 }
 
@@ -593,8 +598,8 @@ int cst_moe_layer(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const f
     const cst_config& f = c->cfg;
     prof_begin(c, s);
     CST_CUDA(launch_router(x, x_dtype, gate_weight, bias, resident, T, f.n_routed_experts, f.hidden_dim, f.n_group,
-                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor, c->ws.router_logits, idx,
-                           wts, nullptr, s));
+                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor, c->ws.router_logits,
+                           c->ws.router_cap, idx, wts, nullptr, c->ws.err, s));
     prof_mark(c, 0, s);
     return moe_routed_impl(c, x, x_dtype, T, idx, wts, top_k, flags, residual, out, out_dtype, s);
 }

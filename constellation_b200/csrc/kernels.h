@@ -22,11 +22,14 @@ cudaError_t launch_dequant_fp8(const uint8_t* w, const float* s, float* out, int
                                int num_sms, cudaStream_t stream);
 
 // router.cu
-// `logits` receives the [T, E] fp32 logits (workspace, or the caller's aux output)
+// `logits` holds `cap` floats: scratch for the partial logits of a K split, or the caller's
+// [T, E] logits when cap == T * E (no split).  err: device error word or null.
+int router_tc_split(int T, int E, int H, int64_t cap);
+int64_t router_scratch_floats(int x_dtype, int T, int E, int H);  // scratch a call of T tokens may use
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
                           int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
-                          float* logits, int32_t* topk_idx, float* topk_w, float* group_scores_out,
-                          cudaStream_t stream);
+                          float* logits, int64_t cap, int32_t* topk_idx, float* topk_w, float* group_scores_out,
+                          int* err, cudaStream_t stream);
 
 // route_pack.cu
 struct PackArgs {

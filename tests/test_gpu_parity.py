@@ -110,6 +110,25 @@ def test_dummy_fixture_full_size_vs_reference(dev, golden):
         assert cos >= 0.9999, cos
 
 
+@pytest.mark.parametrize("T", [2100])
+def test_router_tensor_core_path_vs_oracle(dev, T):
+    """Above 2048 bf16 tokens the logits run on the tensor cores (gate weight split into
+    three bf16 terms, per-block fp32 promotion): same tolerances as the SIMT path."""
+    E, H, G, TG, K = 256, 7168, 8, 4, 8
+    x = cases.activations(400 + T, T, H)
+    w, b = cases.router(401, E, H, bias_std=0.01)
+    ctx = make_ctx(dev, H, 128, E=E, G=G, TG=TG, K=K, n_slots=0, max_tokens=T)
+    args = (torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev))
+    idx, wt = ctx.route(*args)
+    r = router.route_batched(x, w, b, n_group=G, topk_group=TG, top_k=K)
+    ok = r.margin > 1e-5
+    assert ok.mean() > 0.9
+    np.testing.assert_array_equal(idx.cpu().numpy()[ok], r.topk_idx[ok])
+    np.testing.assert_allclose(wt.cpu().numpy()[ok], r.topk_weight[ok], rtol=2e-6, atol=1e-7)
+    i2, w2 = ctx.route(*args)
+    assert torch.equal(i2, idx) and torch.equal(w2, wt)  # deterministic
+
+
 @pytest.mark.parametrize("case", ["small", "bias_heavy", "restricted", "g4_k6", "full"])
 def test_router_vs_oracle(dev, golden, case):
     g = golden("router_golden")
