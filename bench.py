@@ -57,8 +57,6 @@ def parse():
     p.add_argument("--cpu-sample-tokens", type=int, default=2)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--graph-timeline", action="store_true",
-                   help="N > 1: also time the exchange phases inside a captured CUDA graph")
     p.add_argument("--layers", type=int, default=58, help="config3: stacked layers")
     p.add_argument("--workload", choices=["config2", "config1", "config3", "config4"], default="config2",
                    help="config2: the full decode layer, T=64 (default); config1: grouped FP8 expert matvec "
@@ -297,27 +295,6 @@ def run_ours(args):
                 sums[name] = sums.get(name, 0.0) + e0.elapsed_time(e1)
         moe.timeline = None
         ep_phase_ms = {k: round(v / nprof, 4) for k, v in sums.items()}
-        if graph is not None and args.graph_timeline:
-            # the same phases inside a CUDA graph (event records are graph nodes): no launch gaps
-            moe.timeline = []
-            s2 = torch.cuda.Stream(dev)
-            s2.wait_stream(torch.cuda.current_stream(dev))
-            g2 = torch.cuda.CUDAGraph()
-            dist.barrier()
-            with torch.cuda.graph(g2, stream=s2):
-                moe.forward(x, gw, gb)
-            tl = moe.timeline
-            moe.timeline = None
-            gsums: dict = {}
-            for _ in range(nprof):
-                g2.replay()
-                torch.cuda.synchronize(dev)
-                for (_, e0), (name, e1) in zip(tl[:-1], tl[1:]):
-                    gsums[name] = gsums.get(name, 0.0) + e0.elapsed_time(e1)
-            torch.cuda.synchronize(dev)
-            g2.reset()
-            del g2
-            ep_phase_ms = {"eager": ep_phase_ms, "graph": {k: round(v / nprof, 4) for k, v in gsums.items()}}
 
     # algorithmic bytes of the grouped kernels on this rank
     U_total = touched_experts(torch, ctx, gw, gb, x_all, args.resident_experts) if world == 1 else None
