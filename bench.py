@@ -227,7 +227,7 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
     # kernels of this library per layer (NCCL and torch copy kernels not counted)
     # (the packer is one launch up to 2048 routes and three beyond)
-    launches_per_step = (8 if world == 1 else 9) + (2 if T * (K + 1) > 2048 else 0)
+    launches_per_step = (8 if world == 1 else 9) + (2 if T * (K + 1) > 2048 else 0) + (1 if prefill else 0)
 
     def timed(fn, k):
         if world > 1:

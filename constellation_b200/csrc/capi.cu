@@ -80,6 +80,7 @@ struct Workspace {
     float* hscale = nullptr;
     float* y = nullptr;               // [max_rows, H]
     int* err = nullptr;
+    float* tok_scale = nullptr;       // prefill: per x row scale [max(max_tokens, max_rows)]
     int* hist = nullptr;              // packer counting-sort scratch
     int64_t hist_cap = 0;
 };
@@ -199,6 +200,7 @@ int alloc_workspace(cst_ctx* c) {
         {reinterpret_cast<void**>(&w.y), size_t(R) * H * 4},
         {reinterpret_cast<void**>(&w.err), 256},
         {reinterpret_cast<void**>(&w.hist), size_t(w.hist_cap) * 4},
+        {reinterpret_cast<void**>(&w.tok_scale), size_t(std::max<int64_t>(f.max_tokens, R)) * 4},
     };
     size_t total = 0;
     for (auto& p : pieces) total += (p.bytes + 255) / 256 * 256;
@@ -257,7 +259,14 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     prof_mark(c, 1, s);
 
     PackActArgs px{x, x_dtype, H, w.row_token, w.groups, w.tile_group, w.meta, H, w.xfrag, w.xscale, terms};
-    CST_CUDA(pf ? launch_pack_rows(px, c->num_sms, s) : launch_pack_act(px, c->num_sms, s));
+    if (pf) {
+        // every token's scale once, then one pass per packed row
+        CST_CUDA(launch_row_scale(px, pa.T, w.tok_scale, c->num_sms, s));
+        px.src_scale = w.tok_scale;
+        CST_CUDA(launch_pack_rows(px, c->num_sms, s));
+    } else {
+        CST_CUDA(launch_pack_act(px, c->num_sms, s));
+    }
     prof_mark(c, 2, s);
 
     FfnArgs up{};

@@ -78,6 +78,7 @@ struct PackActArgs {
     uint8_t* bfrag;          // B fragments
     float* bscale;           // per (row, K block) scales
     int terms;               // E4M3 terms per element: 3 (decode kernels) or 2 (prefill kernels)
+    const float* src_scale = nullptr;  // prefill: per source row scale (row_scale_kernel), or null
 };
 // src_dtype 4: `src` holds the up/gate kernel's split accumulators (meta->split_k splits of
 // meta->n_rows rows each); the packer adds the splits in order and applies
@@ -89,6 +90,8 @@ cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stre
 // bscale[row]), so the prefill kernel promotes each K block with the weight scale alone and
 // applies the row scale once per output.  terms must be 2.
 cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t stream);
+// out[r] = the scale pack_rows_kernel would compute for source row r (r < n_src_rows)
+cudaError_t launch_row_scale(const PackActArgs& a, int n_src_rows, float* out, int num_sms, cudaStream_t stream);
 
 // grouped_ffn.cu
 struct FfnArgs {

@@ -175,19 +175,24 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackActArgs a) {
         if (r >= gr.n_rows) continue;  // unread accumulator columns need no data
         const int prow = gr.row_start + r;
         const int64_t src_row = a.row_map ? a.row_map[prow] : prow;
-        float amax = 0.0f;
-        for (int kb0 = 0; kb0 < KB; kb0 += 4) {
-            float v[4][4];
+        float s;
+        if (a.src_scale) {
+            s = a.src_scale[src_row];  // the source row's scale, computed once (row_scale_kernel)
+        } else {
+            float amax = 0.0f;
+            for (int kb0 = 0; kb0 < KB; kb0 += 4) {
+                float v[4][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                if (kb0 + i < KB) load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, split, v[i]);
+                for (int i = 0; i < 4; ++i)
+                    if (kb0 + i < KB) load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, split, v[i]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                if (kb0 + i < KB)
-                    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3]))));
+                for (int i = 0; i < 4; ++i)
+                    if (kb0 + i < KB)
+                        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3]))));
+            }
+            amax = warp_max(amax);
+            s = pow2_scale_for(amax);
         }
-        amax = warp_max(amax);
-        const float s = pow2_scale_for(amax);
         const float inv = 1.0f / s;  // exact: s is a power of two
         const int tok = r;
         const int TP = NT * kTileCols;
@@ -224,6 +229,38 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackActArgs a) {
         }
         if (lane == 0) a.bscale[prow] = s;
     }
+}
+
+// One warp per source row: the power-of-two scale pack_rows_kernel would find for it
+// (max |v| over the row -> pow2_scale_for).  Lets the x packer run one pass when a token
+// appears in several packed rows.
+__global__ void __launch_bounds__(256) row_scale_kernel(PackActArgs a, int n_src_rows, float* out) {
+    const int KB = a.K / kBlock;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t row = warp_global; row < n_src_rows; row += n_warps) {
+        float amax = 0.0f;
+        for (int kb0 = 0; kb0 < KB; kb0 += 4) {
+            float v[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (kb0 + i < KB) load4(a, row, (kb0 + i) * kBlock + 4 * lane, 1, v[i]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (kb0 + i < KB)
+                    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3]))));
+        }
+        amax = warp_max(amax);
+        if (lane == 0) out[row] = pow2_scale_for(amax);
+    }
+}
+
+cudaError_t launch_row_scale(const PackActArgs& a, int n_src_rows, float* out, int num_sms, cudaStream_t stream) {
+    if (a.src_dtype == kSrcUpGatePartials) return cudaErrorInvalidValue;
+    if (n_src_rows == 0) return cudaSuccess;
+    row_scale_kernel<<<num_sms * 4, 256, 0, stream>>>(a, n_src_rows, out);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t stream) {
