@@ -60,11 +60,12 @@ struct TcShape {
 };
 
 // K split for this launch: enough (group, row block, split) items to keep every CTA busy
-// (at least 8 per CTA) while each item keeps a whole number of K blocks and the partial sums
-// fit the output buffer.  Every CTA computes the same value from the same inputs.
+// (at least 16 per CTA, so the last round is a small share) while each item keeps a whole
+// number of K blocks and the partial sums fit the output buffer.  Every CTA computes the
+// same value from the same inputs.
 __device__ __forceinline__ int choose_split(int base_items, int KB, int max_split, int n_rows, int out_rows) {
     int S = 1;
-    while (S < max_split && base_items * S < 8 * int(gridDim.x) && KB % (2 * S) == 0 &&
+    while (S < max_split && base_items * S < 16 * int(gridDim.x) && KB % (2 * S) == 0 &&
            int64_t(n_rows) * 2 * S <= out_rows)
         S *= 2;
     return S;
