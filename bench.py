@@ -52,7 +52,9 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--tokens", type=int, default=None,
                    help="tokens T of the whole job (default 64 for config2, 4096 for config4)")
-    p.add_argument("--ep-mode", choices=["allgather", "alltoall"], default="allgather")
+    p.add_argument("--ep-mode", choices=["allgather", "alltoall", "p2p"], default="allgather",
+                   help="expert-parallel exchange: NCCL all-gather + reduce-scatter, NCCL all-to-all-v, or "
+                        "NCCL all-gather + the combine pushed to the token owners over peer memory")
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     p.add_argument("--cpu-sample-tokens", type=int, default=2)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -205,7 +207,7 @@ def run_ours(args):
             out.copy_(moe.forward(x, gw, gb))
 
     # the all-to-all-v exchange reads split sizes on the host, so it cannot be captured
-    use_graph = (not args.no_graph) and (world == 1 or args.ep_mode == "allgather")
+    use_graph = (not args.no_graph) and (world == 1 or args.ep_mode in ("allgather", "p2p"))
     graph = None
     for _ in range(max(3, args.warmup)):
         step()
@@ -402,6 +404,8 @@ def run_ours(args):
         del graph
     if world > 1:
         dist.barrier()
+        moe.close()  # every rank is done with the peer buffers
+        dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         emit(line)
@@ -457,7 +461,8 @@ def run_config3(args):
         layers.append(StackLayer(ctx, gw, gb, nw))
     torch.cuda.synchronize(dev)
     torch.cuda.empty_cache()
-    stack = MoEStack(layers, rank=rank, world=world, n_routed_experts=E)
+    stack = MoEStack(layers, rank=rank, world=world, n_routed_experts=E,
+                     mode=args.ep_mode if args.ep_mode != "alltoall" else "allgather")
     h_all = synthetic.make_activations(T, H, seed=11, device=dev)
     h0 = h_all[rank * Tl:(rank + 1) * Tl].contiguous()
     out = torch.empty_like(h0)
@@ -556,7 +561,7 @@ def run_config3(args):
                 "RMS-normalised N(0,1) bf16 hidden; prenorm weights 1 + N(0, 0.02))",
         "config": {"workload": "config3_decode_stack" if L == 58 else f"config3_shape_{L}_layers",
                    "layers": L, "tokens": T, "routed_experts": E, "shared_expert": True, "hidden": H, "inter": I,
-                   "top_k": K, "parallelism": f"ep{world}" + ("_allgather" if world > 1 else ""),
+                   "top_k": K, "parallelism": f"ep{world}" + (f"_{stack.moe[0].mode}" if world > 1 else ""),
                    "cuda_graph": graph is not None, "touched_experts_all_layers": int(bt[1].item()),
                    "l2": f"no flush: {L * (epr + 1) * EXPERT_BYTES / 1e9:.0f} GB of expert weights per GPU "
                          "exceed the 126 MB L2"},
@@ -574,6 +579,9 @@ def run_config3(args):
         graph.reset()
         del graph
     if world > 1:
+        dist.barrier()
+        for m in stack.moe:
+            m.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

@@ -33,7 +33,9 @@ EXPORTED = (
     "cst_expert_forward", "cst_device_error", "cst_ctx_info", "cst_last_error", "cst_abi_version",
     "cst_profile_enable", "cst_profile_read", "cst_shared_combine", "cst_combine_rows", "cst_dequant_fp8",
     "cst_route_noalloc", "cst_moe_routed_range", "cst_set_gemm_mode", "cst_rmsnorm",
+    "cst_ipc_alloc", "cst_ipc_open", "cst_ipc_close", "cst_ipc_free", "cst_moe_routed_push", "cst_reduce_pushed",
 )
+CST_MAX_PEERS = 8
 CST_GEMM_AUTO, CST_GEMM_DECODE, CST_GEMM_PREFILL = 0, 1, 2
 CST_N_STAGES = 7
 STAGE_NAMES = ("router", "route_pack", "pack_x", "grouped_up_gate", "pack_h", "grouped_down", "combine")
@@ -77,6 +79,16 @@ class CstError(RuntimeError):
         self.code = code
 
 
+class CstIpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_uint8 * 64)]
+
+
+class CstPeerSet(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("tl", ctypes.c_int32),
+                ("tl_cap", ctypes.c_int32), ("recv", ctypes.c_void_p * CST_MAX_PEERS),
+                ("flags", ctypes.c_void_p * CST_MAX_PEERS), ("epoch", ctypes.c_void_p), ("done", ctypes.c_void_p)]
+
+
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.is_file():
         raise ImportError(
@@ -109,6 +121,12 @@ def _load() -> ctypes.CDLL:
         "cst_profile_enable": (ctypes.c_int, [P, I32]),
         "cst_profile_read": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_float), I32]),
         "cst_abi_version": (I32, []),
+        "cst_ipc_alloc": (ctypes.c_int, [ctypes.c_int64, ctypes.POINTER(P), ctypes.POINTER(CstIpcHandle)]),
+        "cst_ipc_open": (ctypes.c_int, [ctypes.POINTER(CstIpcHandle), ctypes.POINTER(P)]),
+        "cst_ipc_close": (ctypes.c_int, [P]),
+        "cst_ipc_free": (ctypes.c_int, [P]),
+        "cst_moe_routed_push": (ctypes.c_int, [P, P, I32, P, P, I32, ctypes.POINTER(CstPeerSet), P]),
+        "cst_reduce_pushed": (ctypes.c_int, [P, ctypes.POINTER(CstPeerSet), P, I32, P, I32, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

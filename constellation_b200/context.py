@@ -254,6 +254,28 @@ class ExpertContext:
                                                 _stream(self.device)))
         return out
 
+    def moe_routed_push(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tensor, peers) -> None:
+        """Expert-parallel form with the combine pushed to the token owners
+        (``cst_moe_routed_push``): ``x`` holds all ``world * tl`` gathered tokens; ``peers``
+        is a ``CstPeerSet`` (``constellation_b200.p2p.PeerExchange.peer_set``)."""
+        x = self._check_x(x)
+        with torch.cuda.device(self.device):
+            check(_lib.lib.cst_moe_routed_push(self.handle, x.data_ptr(), dtype_code(x.dtype), topk_idx.data_ptr(),
+                                               topk_weight.data_ptr(), int(topk_idx.shape[1]), ctypes.byref(peers),
+                                               _stream(self.device)))
+
+    def reduce_pushed(self, peers, *, residual: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's ``tl`` tokens: the ranks' pushed partials in rank order (+ residual),
+        cast once (``cst_reduce_pushed``)."""
+        if out is None:
+            out = torch.empty((peers.tl, self.cfg.hidden_size), dtype=out_dtype, device=self.device)
+        with torch.cuda.device(self.device):
+            check(_lib.lib.cst_reduce_pushed(self.handle, ctypes.byref(peers), _ptr(residual),
+                                             dtype_code(residual.dtype) if residual is not None else 0,
+                                             out.data_ptr(), dtype_code(out.dtype), _stream(self.device)))
+        return out
+
     def cast_extra(self, extra: torch.Tensor, *, residual: torch.Tensor | None = None,
                    out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
         """``out = extra (+ residual)`` cast once (``cst_combine_rows`` with no rows)."""

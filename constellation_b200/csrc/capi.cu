@@ -521,7 +521,8 @@ int cst_route(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float
 
 static int moe_routed_impl(cst_ctx* c, const void* x, int x_dtype, int T, const int32_t* topk_idx,
                            const float* topk_w, int K, uint32_t flags, const void* residual, void* out,
-                           int out_dtype, cudaStream_t s, int shared_begin = 0, int shared_end = -1) {
+                           int out_dtype, cudaStream_t s, int shared_begin = 0, int shared_end = -1,
+                           const PeerSet* push = nullptr) {
     const bool shared = (flags & CST_FLAG_ADD_SHARED) != 0;
     if (shared && c->shared_slot < 0) return fail(CST_ERR_NOT_RESIDENT, "no shared expert is resident");
     if (shared_end < 0) shared_end = T;
@@ -541,10 +542,38 @@ static int moe_routed_impl(cst_ctx* c, const void* x, int x_dtype, int T, const 
     pa.row_weight_in = nullptr;
     pa.T = T;
     if (int rc = run_experts(c, pa, x, x_dtype, s)) return rc;
-    CombineArgs ca{c->ws.y, c->cfg.hidden_dim, c->ws.tk_row, K + 1, T, c->cfg.hidden_dim,
-                   residual, x_dtype, out, out_dtype, nullptr};
-    CST_CUDA(launch_combine(ca, s));
+    if (push != nullptr) {
+        PushArgs pu{c->ws.y, c->cfg.hidden_dim, c->ws.tk_row, K + 1, T, c->cfg.hidden_dim, push->tl, *push};
+        CST_CUDA(launch_combine_push(pu, s));
+    } else {
+        CombineArgs ca{c->ws.y, c->cfg.hidden_dim, c->ws.tk_row, K + 1, T, c->cfg.hidden_dim,
+                       residual, x_dtype, out, out_dtype, nullptr};
+        CST_CUDA(launch_combine(ca, s));
+    }
     prof_mark(c, 6, s);
+    return CST_OK;
+}
+
+static int peer_set_from(const cst_peer_set* p, PeerSet* out) {
+    if (p == nullptr) return fail(CST_ERR_INVALID_ARG, "null peer set");
+    if (p->world < 1 || p->world > CST_MAX_PEERS || p->rank < 0 || p->rank >= p->world)
+        return fail(CST_ERR_INVALID_ARG, "peer set: world=%d rank=%d", p->world, p->rank);
+    if (p->tl <= 0 || p->tl > p->tl_cap) return fail(CST_ERR_INVALID_ARG, "peer set: tl=%d tl_cap=%d", p->tl, p->tl_cap);
+    if (!p->epoch || !p->done) return fail(CST_ERR_INVALID_ARG, "peer set: null epoch/counter");
+    PeerSet q{};
+    q.world = p->world;
+    q.rank = p->rank;
+    q.tl = p->tl;
+    q.tl_cap = p->tl_cap;
+    for (int r = 0; r < p->world; ++r) {
+        if (!p->recv[r] || !p->flags[r] || !aligned16(p->recv[r]))
+            return fail(CST_ERR_INVALID_ARG, "peer set: rank %d buffers missing or unaligned", r);
+        q.recv[r] = p->recv[r];
+        q.flags[r] = p->flags[r];
+    }
+    q.epoch = p->epoch;
+    q.done = p->done;
+    *out = q;
     return CST_OK;
 }
 
@@ -749,6 +778,89 @@ int cst_rmsnorm(const void* x, int32_t x_dtype, int32_t T, int32_t H, const floa
     if (!(eps >= 0.0f)) return fail(CST_ERR_INVALID_ARG, "eps must be >= 0");
     if (!aligned16(x) || !aligned16(out)) return fail(CST_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
     CST_CUDA(launch_rmsnorm(x, x_dtype, T, H, weight, eps, out, out_dtype, static_cast<cudaStream_t>(stream)));
+    return CST_OK;
+}
+
+int cst_moe_routed_push(cst_ctx* c, const void* x, int32_t x_dtype, const int32_t* topk_idx,
+                        const float* topk_weight, int32_t top_k, const cst_peer_set* peers, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    PeerSet ps{};
+    if (int rc = peer_set_from(peers, &ps)) return rc;
+    const int T = ps.world * ps.tl;
+    if (!valid_dtype(x_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
+    if (T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, c->cfg.max_tokens);
+    if (top_k <= 0 || top_k > 15) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of range", top_k);
+    if (!x || !topk_idx || !topk_weight) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (!aligned16(x)) return fail(CST_ERR_INVALID_ARG, "x must be 16-byte aligned");
+    if (c->cfg.hidden_dim % 4) return fail(CST_ERR_INVALID_ARG, "hidden_dim must be a multiple of 4");
+    if (int rc = ensure_device(c)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    prof_begin(c, s);
+    prof_fill_skipped(c, 0, s);
+    const int lo = ps.rank * ps.tl;
+    const uint32_t flags = c->shared_slot >= 0 ? CST_FLAG_ADD_SHARED : 0u;
+    return moe_routed_impl(c, x, x_dtype, T, topk_idx, topk_weight, top_k, flags, nullptr, nullptr, CST_DTYPE_FP32,
+                           s, lo, lo + ps.tl, &ps);
+}
+
+int cst_reduce_pushed(cst_ctx* c, const cst_peer_set* peers, const void* residual, int32_t residual_dtype,
+                      void* out, int32_t out_dtype, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    PeerSet ps{};
+    if (int rc = peer_set_from(peers, &ps)) return rc;
+    if (!valid_dtype(out_dtype) || (residual && !valid_dtype(residual_dtype)))
+        return fail(CST_ERR_INVALID_ARG, "bad dtype");
+    if (!out || !aligned16(out) || (residual && !aligned16(residual)))
+        return fail(CST_ERR_INVALID_ARG, "out (and residual) must be non-null and 16-byte aligned");
+    if (int rc = ensure_device(c)) return rc;
+    ReduceArgs ra{ps, ps.tl, c->cfg.hidden_dim, residual, residual_dtype, out, out_dtype, c->ws.err};
+    CST_CUDA(launch_reduce_cast(ra, static_cast<cudaStream_t>(stream)));
+    return CST_OK;
+}
+
+int cst_ipc_alloc(int64_t bytes, void** ptr, cst_ipc_handle* handle) {
+    g_last_error.clear();
+    if (bytes <= 0 || !ptr || !handle) return fail(CST_ERR_INVALID_ARG, "bad arguments");
+    static_assert(sizeof(cudaIpcMemHandle_t) <= sizeof(cst_ipc_handle), "IPC handle does not fit");
+    void* p = nullptr;
+    CST_CUDA(cudaMalloc(&p, size_t(bytes)));
+    cudaError_t e = cudaMemset(p, 0, size_t(bytes));
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(CST_ERR_CUDA, "cst_ipc_alloc: %s", cudaGetErrorString(e));
+    }
+    std::memset(handle, 0, sizeof(*handle));
+    std::memcpy(handle->bytes, &h, sizeof(h));
+    *ptr = p;
+    return CST_OK;
+}
+
+int cst_ipc_open(const cst_ipc_handle* handle, void** ptr) {
+    g_last_error.clear();
+    if (!handle || !ptr) return fail(CST_ERR_INVALID_ARG, "null argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle->bytes, sizeof(h));
+    void* p = nullptr;
+    CST_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    *ptr = p;
+    return CST_OK;
+}
+
+int cst_ipc_close(void* ptr) {
+    g_last_error.clear();
+    if (!ptr) return CST_OK;
+    CST_CUDA(cudaIpcCloseMemHandle(ptr));
+    return CST_OK;
+}
+
+int cst_ipc_free(void* ptr) {
+    g_last_error.clear();
+    if (!ptr) return CST_OK;
+    CST_CUDA(cudaFree(ptr));
     return CST_OK;
 }
 

@@ -129,6 +129,40 @@ cudaError_t launch_grouped_prefill(const FfnArgs& a, bool upgate, int num_sms, c
 cudaError_t launch_rmsnorm(const void* x, int x_dtype, int T, int H, const float* weight, float eps, void* out,
                            int out_dtype, cudaStream_t stream);
 
+// p2p.cu: the combine fused with the cross-rank reduction over peer memory
+constexpr int kMaxPeers = 8;
+struct PeerSet {
+    int world, rank;
+    int tl;       // tokens each rank owns
+    int tl_cap;   // token capacity of one receive slot
+    float* recv[kMaxPeers];      // rank q's receive buffer [world][tl_cap][H] (mapped here)
+    int32_t* flags[kMaxPeers];   // rank q's arrival flags [world]
+    int32_t* epoch;              // this rank's exchange counter
+    int32_t* done;               // this rank's CTA counter (zero between exchanges)
+};
+struct PushArgs {
+    const float* y;         // weighted expert output rows
+    int64_t ldy;
+    const int32_t* tk_row;  // [T, K1]; -1 = absent
+    int K1;
+    int T;                  // gathered tokens = world * tl
+    int H;
+    int tl;
+    PeerSet peers;
+};
+struct ReduceArgs {
+    PeerSet peers;
+    int tl;
+    int H;
+    const void* residual;   // [tl, H] or null
+    int residual_dtype;
+    void* out;              // [tl, H]
+    int out_dtype;
+    int* err;
+};
+cudaError_t launch_combine_push(const PushArgs& a, cudaStream_t stream);
+cudaError_t launch_reduce_cast(const ReduceArgs& a, cudaStream_t stream);
+
 // combine.cu
 struct CombineArgs {
     const float* y;         // [rows, H] fp32 weighted expert outputs

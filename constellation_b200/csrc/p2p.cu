@@ -1,0 +1,186 @@
+// Peer-memory exchange for expert parallelism: the combine of the routed (and shared)
+// expert outputs fused with the cross-rank reduction, over NVLink stores.
+//
+// The reference reduces nothing across GPUs -- its coordinator gathers one expert result
+// per (token, expert) socket request and sums them on the host (server/moe_layer_runtime.py
+// :111-229).  Here every rank holds a quarter / an eighth of the experts and, after the
+// grouped kernels, a weighted output row per (gathered token, local route).  Instead of
+// adding them into an fp32 [T, H] partial and handing that to an NCCL reduce-scatter:
+//
+//   combine_push_kernel  (one CTA per (token, 1024-column chunk)): the token's rows in the
+//     fixed k order, the sum stored straight into the OWNING rank's receive buffer
+//     (slot [this rank][token - owner * tl]) through the peer mapping; the last CTA to
+//     finish raises this exchange's epoch in every rank's arrival flag for this rank.
+//   reduce_cast_kernel   (one CTA per (own token, chunk)): waits -- bounded -- until every
+//     rank's flag shows the epoch, then adds the world partial sums in rank order, the
+//     residual, and casts once.
+//
+// Ordering: each pushing CTA fences (system scope) after its stores and counts itself in on
+// a local atomic; the CTA that counts last fences again and then stores the flags, so a
+// reader that sees a flag sees every partial of that rank.  The epoch is a device counter
+// that every rank advances once per exchange, so CUDA graphs replay it unchanged.  A slot is
+// rewritten only by the next exchange, which in the expert-parallel layer comes after the
+// next all-gather -- a collective every rank enters only after finishing its own reduce of
+// this exchange -- so one buffer per rank suffices.
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "cst_common.cuh"
+#include "kernels.h"
+
+namespace cst {
+
+namespace {
+
+__device__ __forceinline__ int ld_acquire_sys(const int32_t* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int32_t* p, int v) {
+    asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(256) combine_push_kernel(PushArgs a) {
+    const int t = blockIdx.x;
+    const int q = t / a.tl;              // owner rank of token t
+    const int tloc = t - q * a.tl;
+    const int32_t* rows = a.tk_row + int64_t(t) * a.K1;
+    float* dst = a.peers.recv[q] + (int64_t(a.peers.rank) * a.peers.tl_cap + tloc) * a.H;
+    for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < a.H; h += gridDim.y * blockDim.x * 4) {
+        float4 v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int r = (k < a.K1) ? __ldg(rows + k) : -1;
+            v[k] = (r >= 0) ? __ldg(reinterpret_cast<const float4*>(a.y + int64_t(r) * a.ldy + h))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k < a.K1) {
+                acc.x += v[k].x;
+                acc.y += v[k].y;
+                acc.z += v[k].z;
+                acc.w += v[k].w;
+            }
+        }
+        *reinterpret_cast<float4*>(dst + h) = acc;  // a local or a peer store (NVLink)
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();  // this CTA's partials before its count
+        const int total = int(gridDim.x * gridDim.y);
+        if (atomicAdd(a.peers.done, 1) == total - 1) {
+            *a.peers.done = 0;  // every CTA has counted in: ready for the next exchange
+            const int e = *a.peers.epoch + 1;
+            *a.peers.epoch = e;
+            __threadfence_system();  // every CTA's partials before any flag
+            for (int r = 0; r < a.peers.world; ++r) st_release_sys(a.peers.flags[r] + a.peers.rank, e);
+        }
+    }
+}
+
+template <int OUT>
+__device__ __forceinline__ void store_out(void* out, int64_t o, float4 v) {
+    if constexpr (OUT == 3) {
+        *reinterpret_cast<float4*>(static_cast<float*>(out) + o) = v;
+    } else if constexpr (OUT == 2) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t*>(&lo);
+        u.y = *reinterpret_cast<const uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + o) = u;
+    } else {
+        const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t*>(&lo);
+        u.y = *reinterpret_cast<const uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + o) = u;
+    }
+}
+
+__device__ __forceinline__ float4 load4_any(const void* p, int dtype, int64_t idx) {
+    if (dtype == 3) return *reinterpret_cast<const float4*>(static_cast<const float*>(p) + idx);
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + idx);
+    if (dtype == 2)
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                           __uint_as_float(u.y & 0xffff0000u));
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
+template <int OUT>
+__global__ void __launch_bounds__(256) reduce_cast_kernel(ReduceArgs a) {
+    __shared__ int s_ok;
+    const int t = blockIdx.x;  // own token
+    if (threadIdx.x == 0) {
+        const int e = *a.peers.epoch;
+        const int32_t* flags = a.peers.flags[a.peers.rank];
+        bool ok = true;
+        for (int r = 0; r < a.peers.world && ok; ++r) {
+            // bounded: 2^22 polls with a short sleep (~0.5 s), then the device error word
+            uint32_t n = 0;
+            while (ld_acquire_sys(flags + r) < e) {
+                if (++n >= (1u << 22)) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(100);
+            }
+        }
+        if (!ok && a.err) atomicMax(a.err, CST_DEV_ERR_TIMEOUT);
+        s_ok = ok;
+    }
+    __syncthreads();
+    __threadfence();
+    const float* recv = a.peers.recv[a.peers.rank];
+    for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < a.H; h += gridDim.y * blockDim.x * 4) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s_ok) {
+            for (int r = 0; r < a.peers.world; ++r) {  // rank order
+                const float4 v =
+                    *reinterpret_cast<const float4*>(recv + (int64_t(r) * a.peers.tl_cap + t) * a.H + h);
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+        }
+        if (a.residual) {
+            const float4 v = load4_any(a.residual, a.residual_dtype, int64_t(t) * a.H + h);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        store_out<OUT>(a.out, int64_t(t) * a.H + h, acc);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_combine_push(const PushArgs& a, cudaStream_t stream) {
+    if (a.T == 0) return cudaSuccess;
+    const dim3 grid(a.T, (a.H + 1023) / 1024);
+    combine_push_kernel<<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_reduce_cast(const ReduceArgs& a, cudaStream_t stream) {
+    if (a.tl == 0) return cudaSuccess;
+    const dim3 grid(a.tl, (a.H + 1023) / 1024);
+    if (a.out_dtype == 3) {
+        reduce_cast_kernel<3><<<grid, 256, 0, stream>>>(a);
+    } else if (a.out_dtype == 2) {
+        reduce_cast_kernel<2><<<grid, 256, 0, stream>>>(a);
+    } else {
+        reduce_cast_kernel<1><<<grid, 256, 0, stream>>>(a);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace cst

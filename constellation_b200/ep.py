@@ -67,13 +67,14 @@ class ExpertParallelMoE:
                  mode: str = "allgather", local_route_min: int = 128):
         if n_routed_experts % world:
             raise ValueError(f"{n_routed_experts} experts do not shard over {world} ranks")
-        if mode not in ("allgather", "alltoall"):
+        if mode not in ("allgather", "alltoall", "p2p"):
             raise ValueError(f"unknown EP mode {mode!r}")
         self.c = compute
         self.rank, self.world, self.group, self.mode = rank, world, group, mode
         self.E = n_routed_experts
         self.epr = n_routed_experts // world
         self._slot_map = None
+        self._peers = None  # p2p mode: PeerExchange, created on the first forward
         #: all-gather mode: from this many tokens per rank on, each rank routes only its own
         #: tokens and the routes are gathered with the activations (a 2K-int row per token);
         #: below it every rank routes the whole gathered batch and no routes move
@@ -113,6 +114,8 @@ class ExpertParallelMoE:
             return out
         if self.mode == "allgather":
             return self._allgather(x_local, gate_weight, bias, resident, residual, od)
+        if self.mode == "p2p":
+            return self._p2p(x_local, gate_weight, bias, resident, residual, od)
         topk_idx, topk_w = self.c.route(x_local, gate_weight, bias, resident=resident)
         self._mark("route")
         return self._alltoall(x_local, topk_idx, topk_w, residual, od)
@@ -151,6 +154,39 @@ class ExpertParallelMoE:
         out = self.c.cast_extra(mine, residual=residual, out_dtype=od)
         self._mark("cast")
         return out
+
+    def _p2p(self, x_local, gate_weight, bias, resident, residual, od) -> torch.Tensor:
+        """All-gather exchange with the reduce-scatter fused into the combine: every rank
+        stores each gathered token's partial sum into the owning rank's memory over NVLink
+        and the owner adds the ranks' partials (``cst_moe_routed_push`` /
+        ``cst_reduce_pushed``).  The all-gather at the start of each layer call orders one
+        call's reads of the receive slots before the next call's writes."""
+        from .p2p import PeerExchange
+
+        Tl, H = x_local.shape
+        if self._peers is None:
+            self._peers = PeerExchange(x_local.device, world=self.world, rank=self.rank, tl_cap=max(Tl, 1),
+                                       hidden=H, group=self.group)
+        if Tl > self._peers.tl_cap:
+            raise RuntimeError(f"p2p exchange was sized for {self._peers.tl_cap} tokens per rank, got {Tl}")
+        x_all = torch.empty((self.world * Tl, H), dtype=x_local.dtype, device=x_local.device)
+        dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
+        self._mark("all_gather")
+        idx_all, w_all = self.c.route(x_all, gate_weight, bias, resident=resident)
+        self._mark("route")
+        ps = self._peers.peer_set(Tl)
+        self.c.moe_routed_push(x_all, idx_all, w_all, ps)
+        self._mark("experts_push")
+        out = self.c.reduce_pushed(ps, residual=residual, out_dtype=od)
+        self._mark("reduce")
+        return out
+
+    def close(self) -> None:
+        """Release the peer-exchange buffers (every rank, after its last forward)."""
+        if self._peers is not None:
+            torch.cuda.synchronize(self._peers.device)
+            self._peers.close()
+            self._peers = None
 
     def _alltoall(self, x_local, topk_idx, topk_w, residual, od) -> torch.Tensor:
         Tl, K = topk_idx.shape

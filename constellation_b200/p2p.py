@@ -1,0 +1,88 @@
+"""Peer-memory exchange buffers for expert parallelism (one process per GPU on one node).
+
+Each rank allocates one device buffer through ``cst_ipc_alloc`` -- ``world * tl_cap``
+receive slots of ``hidden`` fp32 (slot r holds what rank r pushed for this rank's tokens)
+followed by 64 int32 (arrival flags at [0, world), the exchange epoch at [32], a CTA
+counter at [33]) -- and the ranks swap the CUDA IPC handles with one all-gather, so every
+rank maps every other rank's buffer.  ``cst_moe_routed_push`` then stores each gathered
+token's partial sum straight into its owner's slot over NVLink and ``cst_reduce_pushed``
+adds the slots in rank order on the owner: the reduce-scatter of the all-gather exchange,
+fused into the combine (``constellation_b200.ep``, mode ``"p2p"``).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from ._lib import CST_MAX_PEERS, CstIpcHandle, CstPeerSet, check
+
+_TAIL_INTS = 64  # flags [0, world), epoch at [32], counter at [33]
+
+
+class PeerExchange:
+    def __init__(self, device, *, world: int, rank: int, tl_cap: int, hidden: int, group=None):
+        if not 1 <= world <= CST_MAX_PEERS:
+            raise ValueError(f"peer exchange supports 1..{CST_MAX_PEERS} ranks, got {world}")
+        self.device = torch.device(device)
+        self.world, self.rank, self.tl_cap, self.hidden = int(world), int(rank), int(tl_cap), int(hidden)
+        self.slot_bytes = self.world * self.tl_cap * self.hidden * 4
+        nbytes = self.slot_bytes + _TAIL_INTS * 4
+        own = ctypes.c_void_p()
+        handle = CstIpcHandle()
+        with torch.cuda.device(self.device):
+            check(_lib.lib.cst_ipc_alloc(nbytes, ctypes.byref(own), ctypes.byref(handle)))
+        self._own = own.value
+        self._opened: list[int] = []
+        mine = torch.tensor(list(bytes(handle.bytes)), dtype=torch.uint8, device=self.device)
+        every = torch.empty((self.world, 64), dtype=torch.uint8, device=self.device)
+        if self.world > 1:
+            dist.all_gather_into_tensor(every, mine, group=group)
+        else:
+            every[0].copy_(mine)
+        rows = every.cpu().tolist()
+        bases = []
+        with torch.cuda.device(self.device):
+            for q in range(self.world):
+                if q == self.rank:
+                    bases.append(self._own)
+                    continue
+                h = CstIpcHandle()
+                h.bytes[:] = rows[q]
+                p = ctypes.c_void_p()
+                check(_lib.lib.cst_ipc_open(ctypes.byref(h), ctypes.byref(p)))
+                self._opened.append(p.value)
+                bases.append(p.value)
+        self.bases = bases
+
+    def peer_set(self, tl: int) -> CstPeerSet:
+        """The ABI view of the buffers for an exchange with ``tl`` tokens per rank."""
+        if not 0 < tl <= self.tl_cap:
+            raise ValueError(f"tl={tl} outside (0, {self.tl_cap}]")
+        ps = CstPeerSet()
+        ps.world, ps.rank, ps.tl, ps.tl_cap = self.world, self.rank, int(tl), self.tl_cap
+        for q, b in enumerate(self.bases):
+            ps.recv[q] = b
+            ps.flags[q] = b + self.slot_bytes
+        tail = self._own + self.slot_bytes
+        ps.epoch = tail + 32 * 4
+        ps.done = tail + 33 * 4
+        return ps
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after every rank stopped using them)."""
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _lib.lib.cst_ipc_close(p)
+            self._opened = []
+            if self._own:
+                _lib.lib.cst_ipc_free(self._own)
+                self._own = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

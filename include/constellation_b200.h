@@ -226,6 +226,53 @@ int cst_dequant_fp8(const uint8_t* w, const float* scale_inv, int32_t rows, int3
 int cst_rmsnorm(const void* x, int32_t x_dtype, int32_t T, int32_t H, const float* weight, float eps, void* out,
                 int32_t out_dtype, void* stream);
 
+/* ---- Peer-memory exchange (expert parallelism, one process per GPU, NVLink) -----------
+ * No counterpart in the reference: its coordinator collects one expert result per
+ * (token, expert) socket request and sums them on the host (server/moe_layer_runtime.py
+ * :111-229).  Here the per-rank combine stores every token's partial sum straight into the
+ * owning rank's memory, which then adds the ranks' partials in order -- the NCCL
+ * reduce-scatter of the all-gather exchange, fused into the combine. */
+typedef struct {
+    uint8_t bytes[64];  /* a cudaIpcMemHandle_t */
+} cst_ipc_handle;
+
+/* Zeroed device memory on the current device that other processes can map; *ptr and
+ * *handle receive the local address and its IPC handle.  Free with cst_ipc_free. */
+int cst_ipc_alloc(int64_t bytes, void** ptr, cst_ipc_handle* handle);
+/* Maps another process's cst_ipc_alloc allocation (same node, peer access) at *ptr. */
+int cst_ipc_open(const cst_ipc_handle* handle, void** ptr);
+int cst_ipc_close(void* ptr);
+int cst_ipc_free(void* ptr);
+
+#define CST_MAX_PEERS 8
+/* One rank's view of the exchange buffers.  Each rank allocates one buffer of
+ * world * tl_cap * hidden floats (its receive slots, slot r for rank r) followed by 64
+ * int32 (arrival flags at [0, world), epoch at [32], CTA counter at [33]); recv[q] and
+ * flags[q] are rank q's buffer and flags as mapped in this process (q == rank: local). */
+typedef struct {
+    int32_t world, rank;
+    int32_t tl;      /* tokens each rank owns: the gathered batch is world * tl tokens */
+    int32_t tl_cap;  /* token capacity of one receive slot */
+    float* recv[CST_MAX_PEERS];
+    int32_t* flags[CST_MAX_PEERS];
+    int32_t* epoch;  /* this rank's exchange counter */
+    int32_t* done;   /* this rank's CTA counter */
+} cst_peer_set;
+
+/* The routed experts resident here on all world * tl gathered tokens, the shared expert on
+ * this rank's own tokens, and the combine pushed to the owners: token t's partial sum
+ * (this device's routes in k order, then the shared row) is stored into rank
+ * (t / tl)'s receive slot [this rank], and the exchange's epoch is raised in every rank's
+ * flag for this rank once all partials are out.  Follow with cst_reduce_pushed. */
+int cst_moe_routed_push(cst_ctx* ctx, const void* x, int32_t x_dtype, const int32_t* topk_idx,
+                        const float* topk_weight, int32_t top_k, const cst_peer_set* peers, void* stream);
+/* out[t] = sum over ranks r = 0 .. world-1 of rank r's pushed partial for this rank's token
+ * t (+ residual[t]), one cast.  Waits (bounded, ~0.5 s per rank) until every rank raised
+ * this exchange's epoch; a wait that gives up sets the device error word
+ * (cst_device_error) and leaves only the residual in out. */
+int cst_reduce_pushed(cst_ctx* ctx, const cst_peer_set* peers, const void* residual, int32_t residual_dtype,
+                      void* out, int32_t out_dtype, void* stream);
+
 /* Synchronises the context's device, then returns CST_OK or CST_ERR_DEVICE_TIMEOUT if a
  * kernel's bounded wait gave up since the last call (and clears the flag). */
 int cst_device_error(cst_ctx* ctx);

@@ -40,7 +40,7 @@ def _rank_main(rank, world, port, q):
         from constellation_b200.ep import ExpertParallelMoE
         from oracle import cases
 
-        T = 10
+        T = 5 * world
         cfg = MoEConfig(hidden_size=H, moe_intermediate_size=I, n_routed_experts=E, n_group=G, topk_group=TG,
                         num_experts_per_tok=K)
         epr = E // world
@@ -55,12 +55,18 @@ def _rank_main(rank, world, port, q):
         Tl = T // world
         xl = x[rank * Tl:(rank + 1) * Tl].contiguous()
         res = {}
-        for mode in ("allgather", "allgather_local", "alltoall"):
+        for mode in ("allgather", "allgather_local", "alltoall", "p2p"):
             # allgather_local: own-token routing + gathered routes (the prefill-sized path)
             local = mode == "allgather_local"
             moe = ExpertParallelMoE(ctx, rank=rank, world=world, n_routed_experts=E,
                                     mode="allgather" if local else mode, local_route_min=1 if local else 128)
             res[mode] = moe.forward(xl, gw, gb, out_dtype=torch.float32).cpu().numpy()
+            if mode == "p2p":
+                # a second exchange through the same buffers (epoch 2), then release them
+                res["p2p_again"] = moe.forward(xl, gw, gb, out_dtype=torch.float32).cpu().numpy()
+                torch.cuda.synchronize()
+                dist.barrier()
+                moe.close()
         torch.cuda.synchronize()
         ctx.device_error()
         q.put((rank, res))
@@ -71,7 +77,9 @@ def _rank_main(rank, world, port, q):
 
 
 def test_ep_two_gpus_both_modes():
-    if torch.cuda.device_count() < 2:
+    """Every exchange mode over 2 ranks (or 4 / 8 when the box has them) against the oracle."""
+    n_dev = torch.cuda.device_count()
+    if n_dev < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
 
@@ -79,7 +87,8 @@ def test_ep_two_gpus_both_modes():
     from oracle.expert import DequantExpert
     from oracle.layer import moe_layer
 
-    world, T = 2, 10
+    world = 8 if n_dev >= 8 else (4 if n_dev >= 4 else 2)
+    T = 5 * world
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
@@ -95,11 +104,15 @@ def test_ep_two_gpus_both_modes():
     x = cases.activations(82, T, H)
     ref = moe_layer(x, w, b, {e: DequantExpert(cases.expert(3000 + e, H, I)) for e in range(E)},
                     DequantExpert(cases.expert(3999, H, I)), n_group=G, topk_group=TG, top_k=K)
-    for mode in ("allgather", "allgather_local", "alltoall"):
+    for mode in ("allgather", "allgather_local", "alltoall", "p2p", "p2p_again"):
         out = np.concatenate([got[r][mode] for r in range(world)])
         num = np.abs(out - ref.out_f32).max(axis=1)
         den = np.abs(ref.out_f32).max(axis=1)
         assert float((num / den).max()) < 2e-3, mode
-    # routing locally and gathering the routes gives the same routes, hence the same bits
+    # routing locally and gathering the routes gives the same routes, hence the same bits;
+    # with two ranks the pushed partials add like the reduce-scatter's (one fp32 addition)
     for r in range(world):
         assert np.array_equal(got[r]["allgather"], got[r]["allgather_local"])
+        assert np.array_equal(got[r]["p2p"], got[r]["p2p_again"])
+        if world == 2:
+            assert np.array_equal(got[r]["allgather"], got[r]["p2p"])
