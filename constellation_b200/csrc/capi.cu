@@ -815,7 +815,8 @@ int cst_reduce_pushed(cst_ctx* c, const cst_peer_set* peers, const void* residua
     if (!out || !aligned16(out) || (residual && !aligned16(residual)))
         return fail(CST_ERR_INVALID_ARG, "out (and residual) must be non-null and 16-byte aligned");
     if (int rc = ensure_device(c)) return rc;
-    ReduceArgs ra{ps, ps.tl, c->cfg.hidden_dim, residual, residual_dtype, out, out_dtype, c->ws.err};
+    ReduceArgs ra{ps, ps.tl, c->cfg.hidden_dim, push_chunks(c->cfg.hidden_dim), residual, residual_dtype, out,
+                  out_dtype, c->ws.err};
     CST_CUDA(launch_reduce_cast(ra, static_cast<cudaStream_t>(stream)));
     return CST_OK;
 }

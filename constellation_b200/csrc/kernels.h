@@ -136,9 +136,9 @@ struct PeerSet {
     int tl;       // tokens each rank owns
     int tl_cap;   // token capacity of one receive slot
     float* recv[kMaxPeers];      // rank q's receive buffer [world][tl_cap][H] (mapped here)
-    int32_t* flags[kMaxPeers];   // rank q's arrival flags [world]
+    int32_t* flags[kMaxPeers];   // rank q's arrival counters [world]
     int32_t* epoch;              // this rank's exchange counter
-    int32_t* done;               // this rank's CTA counter (zero between exchanges)
+    int32_t* done;               // reserved
 };
 struct PushArgs {
     const float* y;         // weighted expert output rows
@@ -154,12 +154,15 @@ struct ReduceArgs {
     PeerSet peers;
     int tl;
     int H;
+    int chunks;             // column chunks per pushed token block (push_chunks(H))
     const void* residual;   // [tl, H] or null
     int residual_dtype;
     void* out;              // [tl, H]
     int out_dtype;
     int* err;
 };
+int push_chunks(int H);
+constexpr int kPushTok = 4;  // owner tokens per pushing CTA
 cudaError_t launch_combine_push(const PushArgs& a, cudaStream_t stream);
 cudaError_t launch_reduce_cast(const ReduceArgs& a, cudaStream_t stream);
 

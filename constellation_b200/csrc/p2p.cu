@@ -7,18 +7,18 @@
 // grouped kernels, a weighted output row per (gathered token, local route).  Instead of
 // adding them into an fp32 [T, H] partial and handing that to an NCCL reduce-scatter:
 //
-//   combine_push_kernel  (one CTA per (token, 1024-column chunk)): the token's rows in the
-//     fixed k order, the sum stored straight into the OWNING rank's receive buffer
-//     (slot [this rank][token - owner * tl]) through the peer mapping; the last CTA to
-//     finish raises this exchange's epoch in every rank's arrival flag for this rank.
+//   combine_push_kernel  (one CTA per (owner rank, 4-token block, 1024-column chunk)): each
+//     of those tokens' rows in the fixed k order, the sum stored straight into the OWNING rank's
+//     receive buffer (slot [this rank][token - owner * tl]) through the peer mapping, then
+//     one release-ordered add on the owner's arrival counter for this rank.
 //   reduce_cast_kernel   (one CTA per (own token, chunk)): waits -- bounded -- until every
-//     rank's flag shows the epoch, then adds the world partial sums in rank order, the
-//     residual, and casts once.
+//     rank's counter shows all its pushing CTAs of this exchange, then adds the
+//     world partial sums in rank order, the residual, and casts once.
 //
-// Ordering: each pushing CTA fences (system scope) after its stores and counts itself in on
-// a local atomic; the CTA that counts last fences again and then stores the flags, so a
-// reader that sees a flag sees every partial of that rank.  The epoch is a device counter
-// that every rank advances once per exchange, so CUDA graphs replay it unchanged.  A slot is
+// Ordering: the add is a release at system scope, cumulative over the CTA's stores through
+// the barrier before it, and the reader polls with acquire loads, so a reader that sees the
+// count sees every partial it covers.  The epoch word is a device counter that every rank
+// advances by the same amount per exchange, so CUDA graphs replay it unchanged.  A slot is
 // rewritten only by the next exchange, which in the expert-parallel layer comes after the
 // next all-gather -- a collective every rank enters only after finishing its own reduce of
 // this exchange -- so one buffer per rank suffices.
@@ -39,47 +39,51 @@ __device__ __forceinline__ int ld_acquire_sys(const int32_t* p) {
     return v;
 }
 
-__device__ __forceinline__ void st_release_sys(int32_t* p, int v) {
-    asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_release_sys_add(int32_t* p, int v) {
+    asm volatile("red.release.sys.global.add.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
 
+// grid (world x token blocks, column chunks): CTA (q, b, c) sums the rows of owner q's
+// tokens [b kPushTok, b kPushTok + kPushTok) over its 1024-column chunk and stores them into
+// q's slot [this rank]; then one release-ordered add on q's arrival counter for this rank
+// (cumulative over the CTA's stores through the barrier).  CTA (0, 0) also advances this
+// rank's epoch word by the number of pushing CTAs per owner, which the reduce launch reads.
 __global__ void __launch_bounds__(256) combine_push_kernel(PushArgs a) {
-    const int t = blockIdx.x;
-    const int q = t / a.tl;              // owner rank of token t
-    const int tloc = t - q * a.tl;
-    const int32_t* rows = a.tk_row + int64_t(t) * a.K1;
-    float* dst = a.peers.recv[q] + (int64_t(a.peers.rank) * a.peers.tl_cap + tloc) * a.H;
-    for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < a.H; h += gridDim.y * blockDim.x * 4) {
-        float4 v[16];
+    const int nblk = (a.tl + kPushTok - 1) / kPushTok;
+    const int q = blockIdx.x / nblk;
+    const int i0 = (blockIdx.x - q * nblk) * kPushTok;
+    const int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+    float* dst = a.peers.recv[q] + int64_t(a.peers.rank) * a.peers.tl_cap * a.H;
+    if (h < a.H) {
+        for (int i = i0; i < min(a.tl, i0 + kPushTok); ++i) {
+            const int t = q * a.tl + i;
+            const int32_t* rows = a.tk_row + int64_t(t) * a.K1;
+            float4 v[16];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const int r = (k < a.K1) ? __ldg(rows + k) : -1;
-            v[k] = (r >= 0) ? __ldg(reinterpret_cast<const float4*>(a.y + int64_t(r) * a.ldy + h))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            if (k < a.K1) {
-                acc.x += v[k].x;
-                acc.y += v[k].y;
-                acc.z += v[k].z;
-                acc.w += v[k].w;
+            for (int k = 0; k < 16; ++k) {
+                const int r = (k < a.K1) ? __ldg(rows + k) : -1;
+                v[k] = (r >= 0) ? __ldg(reinterpret_cast<const float4*>(a.y + int64_t(r) * a.ldy + h))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
             }
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                if (k < a.K1) {
+                    acc.x += v[k].x;
+                    acc.y += v[k].y;
+                    acc.z += v[k].z;
+                    acc.w += v[k].w;
+                }
+            }
+            *reinterpret_cast<float4*>(dst + int64_t(i) * a.H + h) = acc;  // local or peer store (NVLink)
         }
-        *reinterpret_cast<float4*>(dst + h) = acc;  // a local or a peer store (NVLink)
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence_system();  // this CTA's partials before its count
-        const int total = int(gridDim.x * gridDim.y);
-        if (atomicAdd(a.peers.done, 1) == total - 1) {
-            *a.peers.done = 0;  // every CTA has counted in: ready for the next exchange
-            const int e = *a.peers.epoch + 1;
-            *a.peers.epoch = e;
-            __threadfence_system();  // every CTA's partials before any flag
-            for (int r = 0; r < a.peers.world; ++r) st_release_sys(a.peers.flags[r] + a.peers.rank, e);
-        }
+        red_release_sys_add(a.peers.flags[q] + a.peers.rank, 1);
+        // the epoch word counts the pushing CTAs every rank sends each rank, summed over
+        // all exchanges so far (every rank runs the same exchanges with the same tl)
+        if (blockIdx.x == 0 && blockIdx.y == 0) *a.peers.epoch += int(gridDim.y) * ((a.tl + kPushTok - 1) / kPushTok);
     }
 }
 
@@ -118,13 +122,14 @@ __global__ void __launch_bounds__(256) reduce_cast_kernel(ReduceArgs a) {
     __shared__ int s_ok;
     const int t = blockIdx.x;  // own token
     if (threadIdx.x == 0) {
-        const int e = *a.peers.epoch;
+        // every rank's pushing CTAs for this rank, over all exchanges up to this one
+        const int target = *a.peers.epoch;
         const int32_t* flags = a.peers.flags[a.peers.rank];
         bool ok = true;
         for (int r = 0; r < a.peers.world && ok; ++r) {
             // bounded: 2^22 polls with a short sleep (~0.5 s), then the device error word
             uint32_t n = 0;
-            while (ld_acquire_sys(flags + r) < e) {
+            while (ld_acquire_sys(flags + r) < target) {
                 if (++n >= (1u << 22)) {
                     ok = false;
                     break;
@@ -163,16 +168,18 @@ __global__ void __launch_bounds__(256) reduce_cast_kernel(ReduceArgs a) {
 
 }  // namespace
 
+int push_chunks(int H) { return (H + 1023) / 1024; }
+
 cudaError_t launch_combine_push(const PushArgs& a, cudaStream_t stream) {
     if (a.T == 0) return cudaSuccess;
-    const dim3 grid(a.T, (a.H + 1023) / 1024);
+    const dim3 grid(a.peers.world * ((a.tl + kPushTok - 1) / kPushTok), push_chunks(a.H));
     combine_push_kernel<<<grid, 256, 0, stream>>>(a);
     return cudaGetLastError();
 }
 
 cudaError_t launch_reduce_cast(const ReduceArgs& a, cudaStream_t stream) {
     if (a.tl == 0) return cudaSuccess;
-    const dim3 grid(a.tl, (a.H + 1023) / 1024);
+    const dim3 grid(a.tl, push_chunks(a.H));
     if (a.out_dtype == 3) {
         reduce_cast_kernel<3><<<grid, 256, 0, stream>>>(a);
     } else if (a.out_dtype == 2) {

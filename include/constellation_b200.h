@@ -247,8 +247,8 @@ int cst_ipc_free(void* ptr);
 #define CST_MAX_PEERS 8
 /* One rank's view of the exchange buffers.  Each rank allocates one buffer of
  * world * tl_cap * hidden floats (its receive slots, slot r for rank r) followed by 64
- * int32 (arrival flags at [0, world), epoch at [32], CTA counter at [33]); recv[q] and
- * flags[q] are rank q's buffer and flags as mapped in this process (q == rank: local). */
+ * int32 (arrival counters at [0, world), epoch at [32], [33] reserved), zeroed; recv[q] and
+ * flags[q] are rank q's buffer and counters as mapped in this process (q == rank: local). */
 typedef struct {
     int32_t world, rank;
     int32_t tl;      /* tokens each rank owns: the gathered batch is world * tl tokens */
@@ -256,20 +256,20 @@ typedef struct {
     float* recv[CST_MAX_PEERS];
     int32_t* flags[CST_MAX_PEERS];
     int32_t* epoch;  /* this rank's exchange counter */
-    int32_t* done;   /* this rank's CTA counter */
+    int32_t* done;   /* reserved (a zeroed int32 of this rank) */
 } cst_peer_set;
 
 /* The routed experts resident here on all world * tl gathered tokens, the shared expert on
  * this rank's own tokens, and the combine pushed to the owners: token t's partial sum
  * (this device's routes in k order, then the shared row) is stored into rank
- * (t / tl)'s receive slot [this rank], and the exchange's epoch is raised in every rank's
- * flag for this rank once all partials are out.  Follow with cst_reduce_pushed. */
+ * (t / tl)'s receive slot [this rank], each column chunk followed by a release-ordered
+ * add on that rank's arrival counter for this rank.  Follow with cst_reduce_pushed. */
 int cst_moe_routed_push(cst_ctx* ctx, const void* x, int32_t x_dtype, const int32_t* topk_idx,
                         const float* topk_weight, int32_t top_k, const cst_peer_set* peers, void* stream);
 /* out[t] = sum over ranks r = 0 .. world-1 of rank r's pushed partial for this rank's token
- * t (+ residual[t]), one cast.  Waits (bounded, ~0.5 s per rank) until every rank raised
- * this exchange's epoch; a wait that gives up sets the device error word
- * (cst_device_error) and leaves only the residual in out. */
+ * t (+ residual[t]), one cast.  Waits (bounded, ~0.5 s per rank) until every rank's
+ * counter shows all chunks of this exchange; a wait that gives up sets the device error
+ * word (cst_device_error) and leaves only the residual in out. */
 int cst_reduce_pushed(cst_ctx* ctx, const cst_peer_set* peers, const void* residual, int32_t residual_dtype,
                       void* out, int32_t out_dtype, void* stream);
 
