@@ -52,7 +52,7 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--tokens", type=int, default=None,
                    help="tokens T of the whole job (default 64 for config2, 4096 for config4)")
-    p.add_argument("--ep-mode", choices=["allgather", "alltoall", "p2p"], default="allgather",
+    p.add_argument("--ep-mode", choices=["allgather", "alltoall", "p2p"], default="p2p",
                    help="expert-parallel exchange: NCCL all-gather + reduce-scatter, NCCL all-to-all-v, or "
                         "NCCL all-gather + the combine pushed to the token owners over peer memory")
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
