@@ -23,6 +23,10 @@ _TAIL_INTS = 64  # flags [0, world), epoch at [32], counter at [33]
 
 
 class PeerExchange:
+    """One rank's exchange buffers and its mappings of every other rank's.  Other ranks may
+    still push into this rank's buffer, so nothing frees it implicitly: ``close()`` -- on
+    every rank, after a barrier -- releases it, or the process exit does."""
+
     def __init__(self, device, *, world: int, rank: int, tl_cap: int, hidden: int, group=None):
         if not 1 <= world <= CST_MAX_PEERS:
             raise ValueError(f"peer exchange supports 1..{CST_MAX_PEERS} ranks, got {world}")
@@ -80,9 +84,3 @@ class PeerExchange:
             if self._own:
                 _lib.lib.cst_ipc_free(self._own)
                 self._own = 0
-
-    def __del__(self):
-        try:
-            self.close()
-        except Exception:
-            pass

@@ -61,3 +61,20 @@ def test_product_has_no_oracle_dependency():
     for p in pkg.rglob("*.py"):
         src = p.read_text()
         assert not re.search(r"^\s*(from|import)\s+oracle\b", src, re.M), p
+
+
+def test_peer_set_layout_matches_the_header():
+    """cst_peer_set (include/constellation_b200.h) as ctypes sees it: four int32, then
+    CST_MAX_PEERS receive pointers, CST_MAX_PEERS counter pointers, epoch, reserved."""
+    import ctypes
+
+    from constellation_b200._lib import CST_MAX_PEERS, CstIpcHandle, CstPeerSet
+
+    P = ctypes.sizeof(ctypes.c_void_p)
+    assert CstPeerSet.recv.offset == 16
+    assert CstPeerSet.flags.offset == 16 + CST_MAX_PEERS * P
+    assert CstPeerSet.epoch.offset == 16 + 2 * CST_MAX_PEERS * P
+    assert ctypes.sizeof(CstPeerSet) == 16 + (2 * CST_MAX_PEERS + 2) * P
+    assert ctypes.sizeof(CstIpcHandle) == 64
+    hdr = (Path(__file__).resolve().parents[1] / "include" / "constellation_b200.h").read_text()
+    assert f"#define CST_MAX_PEERS {CST_MAX_PEERS}" in hdr
