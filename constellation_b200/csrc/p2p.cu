@@ -18,7 +18,10 @@
 // Ordering: the add is a release at system scope, cumulative over the CTA's stores through
 // the barrier before it, and the reader polls with acquire loads, so a reader that sees the
 // count sees every partial it covers.  The epoch word is a device counter that every rank
-// advances by the same amount per exchange, so CUDA graphs replay it unchanged.  A slot is
+// advances by the same amount per exchange, so CUDA graphs replay it unchanged.  Counters
+// and epoch are 32-bit words that wrap (a long-lived server passes 2^31 pushing CTAs within
+// days), so "arrived" is the sign of the wrapped difference, never a plain comparison; a
+// counter trails its target by at most the CTAs of one exchange, far below 2^31.  A slot is
 // rewritten only by the next exchange, which in the expert-parallel layer comes after the
 // next all-gather -- a collective every rank enters only after finishing its own reduce of
 // this exchange -- so one buffer per rank suffices.
@@ -33,15 +36,18 @@ namespace cst {
 
 namespace {
 
-__device__ __forceinline__ int ld_acquire_sys(const int32_t* p) {
-    int v;
-    asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint32_t ld_acquire_sys(const int32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
-__device__ __forceinline__ void red_release_sys_add(int32_t* p, int v) {
-    asm volatile("red.release.sys.global.add.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_release_sys_add(int32_t* p, uint32_t v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
+
+// counter `have` has not reached `want` yet, modulo 2^32
+__device__ __forceinline__ bool before(uint32_t have, uint32_t want) { return int32_t(have - want) < 0; }
 
 // grid (world x token blocks, column chunks): CTA (q, b, c) sums the rows of owner q's
 // tokens [b kPushTok, b kPushTok + kPushTok) over its 1024-column chunk and stores them into
@@ -80,10 +86,13 @@ __global__ void __launch_bounds__(256) combine_push_kernel(PushArgs a) {
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        red_release_sys_add(a.peers.flags[q] + a.peers.rank, 1);
+        red_release_sys_add(a.peers.flags[q] + a.peers.rank, 1u);
         // the epoch word counts the pushing CTAs every rank sends each rank, summed over
         // all exchanges so far (every rank runs the same exchanges with the same tl)
-        if (blockIdx.x == 0 && blockIdx.y == 0) *a.peers.epoch += int(gridDim.y) * ((a.tl + kPushTok - 1) / kPushTok);
+        if (blockIdx.x == 0 && blockIdx.y == 0) {
+            uint32_t* epoch = reinterpret_cast<uint32_t*>(a.peers.epoch);
+            *epoch += gridDim.y * uint32_t((a.tl + kPushTok - 1) / kPushTok);
+        }
     }
 }
 
@@ -123,13 +132,13 @@ __global__ void __launch_bounds__(256) reduce_cast_kernel(ReduceArgs a) {
     const int t = blockIdx.x;  // own token
     if (threadIdx.x == 0) {
         // every rank's pushing CTAs for this rank, over all exchanges up to this one
-        const int target = *a.peers.epoch;
+        const uint32_t target = *reinterpret_cast<const uint32_t*>(a.peers.epoch);
         const int32_t* flags = a.peers.flags[a.peers.rank];
         bool ok = true;
         for (int r = 0; r < a.peers.world && ok; ++r) {
-            // bounded: 2^22 polls with a short sleep (~0.5 s), then the device error word
+            // bounded: 2^22 polls with a short sleep (about 1 s on B200), then the device error word
             uint32_t n = 0;
-            while (ld_acquire_sys(flags + r) < target) {
+            while (before(ld_acquire_sys(flags + r), target)) {
                 if (++n >= (1u << 22)) {
                     ok = false;
                     break;

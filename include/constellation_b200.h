@@ -248,7 +248,8 @@ int cst_ipc_free(void* ptr);
 /* One rank's view of the exchange buffers.  Each rank allocates one buffer of
  * world * tl_cap * hidden floats (its receive slots, slot r for rank r) followed by 64
  * int32 (arrival counters at [0, world), epoch at [32], [33] reserved), zeroed; recv[q] and
- * flags[q] are rank q's buffer and counters as mapped in this process (q == rank: local). */
+ * flags[q] are rank q's buffer and counters as mapped in this process (q == rank: local).
+ * Counters and epoch wrap modulo 2^32; only their differences are compared. */
 typedef struct {
     int32_t world, rank;
     int32_t tl;      /* tokens each rank owns: the gathered batch is world * tl tokens */
@@ -267,7 +268,7 @@ typedef struct {
 int cst_moe_routed_push(cst_ctx* ctx, const void* x, int32_t x_dtype, const int32_t* topk_idx,
                         const float* topk_weight, int32_t top_k, const cst_peer_set* peers, void* stream);
 /* out[t] = sum over ranks r = 0 .. world-1 of rank r's pushed partial for this rank's token
- * t (+ residual[t]), one cast.  Waits (bounded, ~0.5 s per rank) until every rank's
+ * t (+ residual[t]), one cast.  Waits (bounded, about 1 s) until every rank's
  * counter shows all chunks of this exchange; a wait that gives up sets the device error
  * word (cst_device_error) and leaves only the residual in out. */
 int cst_reduce_pushed(cst_ctx* ctx, const cst_peer_set* peers, const void* residual, int32_t residual_dtype,

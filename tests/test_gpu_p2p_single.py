@@ -1,0 +1,133 @@
+"""The peer-exchange kernels (cst_moe_routed_push / cst_reduce_pushed) on one GPU, through a
+one-rank cst_peer_set filled by hand over a torch buffer -- the way a C++ host that owns its
+own mappings fills it.
+
+The arrival counters and the epoch are 32-bit words that wrap in a long-lived process; these
+cases start them just below 2^31 so that exchanges cross the wrap, and check that a target
+the pushes never reach makes the bounded wait give up: the device error word is set, the
+output holds only the residual, and the context stays usable.  The layer itself is checked
+against the oracle (dequantize-then-matmul in fp32, server/moe_layer_runtime.py:581-611) and
+against the single-GPU fused layer.
+"""
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cases
+from oracle.expert import DequantExpert
+from oracle.layer import moe_layer
+
+pytestmark = pytest.mark.gpu
+
+E, H, I, G, TG, K = 16, 256, 128, 4, 2, 4
+T = 24  # one column chunk of 1024 and 6 pushing CTAs of 4 tokens per exchange
+CTAS = 6
+FLAGS, EPOCH = T * H, T * H + 32  # int32 offsets of the counters in the exchange buffer
+
+
+def s32(u: int) -> int:
+    u &= 0xFFFFFFFF
+    return u - (1 << 32) if u >= 1 << 31 else u
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module")
+def layer(dev):
+    from constellation_b200.context import ExpertContext, MoEConfig
+
+    cfg = MoEConfig(hidden_size=H, moe_intermediate_size=I, n_routed_experts=E, n_group=G, topk_group=TG,
+                    num_experts_per_tok=K)
+    x = cases.activations(401, T, H)
+    w, b = cases.router(401, E, H, bias_std=0.05)
+    experts = {e: cases.expert(40100 + e, H, I) for e in range(E)}
+    sh = cases.expert(40199, H, I)
+    res = cases.activations(402, T, H)
+    ctx = ExpertContext(dev, cfg, n_slots=E + 1, max_tokens=T)
+    for e in range(E):
+        ctx.upload_bundle(e, e, experts[e])
+    ctx.upload_bundle(E, -1, sh)
+    ref = moe_layer(x, w, b, {e: DequantExpert(v) for e, v in experts.items()}, DequantExpert(sh), n_group=G,
+                    topk_group=TG, top_k=K)
+    xt = torch.from_numpy(x).to(dev, torch.bfloat16)
+    wt, bt = torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev)
+    rt = torch.from_numpy(res).to(dev)
+    return ctx, xt, wt, bt, rt, ref, res
+
+
+def peer_set(buf: torch.Tensor):
+    from constellation_b200._lib import CstPeerSet
+
+    ps = CstPeerSet()
+    ps.world, ps.rank, ps.tl, ps.tl_cap = 1, 0, T, T
+    base = buf.data_ptr()
+    ps.recv[0] = base
+    ps.flags[0] = base + FLAGS * 4
+    ps.epoch = base + EPOCH * 4
+    ps.done = base + (EPOCH + 1) * 4
+    return ps
+
+
+def exchange(ctx, xt, wt, bt, rt, ps):
+    idx, wts = ctx.route(xt, wt, bt)
+    ctx.moe_routed_push(xt, idx, wts, ps)
+    return ctx.reduce_pushed(ps, residual=rt, out_dtype=torch.float32)
+
+
+def test_push_reduce_matches_layer_across_counter_wrap(layer, dev):
+    ctx, xt, wt, bt, rt, ref, res = layer
+    buf = torch.zeros(T * H + 64, dtype=torch.int32, device=dev)
+    start = (1 << 31) - 2 * CTAS - 3  # the third exchange carries both words past 2^31
+    buf[FLAGS] = s32(start)
+    buf[EPOCH] = s32(start)
+    ps = peer_set(buf)
+    outs = [exchange(ctx, xt, wt, bt, rt, ps) for _ in range(5)]
+    ctx.device_error()  # no wait gave up
+    assert int(buf[FLAGS]) == s32(start + 5 * CTAS) and int(buf[EPOCH]) == s32(start + 5 * CTAS)
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    # the fused single-GPU layer adds the same rows in the same order
+    fused = ctx.moe_layer(xt, wt, bt, out_dtype=torch.float32) + rt
+    torch.testing.assert_close(outs[0], fused, rtol=1e-5, atol=1e-5)
+    ok = ref.route.margin > 1e-5
+    got = outs[0].cpu().numpy() - res
+    rel = np.abs(got - ref.out_f32).max(axis=1) / np.abs(ref.out_f32).max(axis=1)
+    assert float(rel[ok].max()) < 2e-3
+
+
+def test_reduce_wait_gives_up_when_a_target_is_never_reached(layer, dev):
+    """Counter just below 2^31, target just past it: a plain signed comparison reads the
+    wrapped (negative) target as reached and sums whatever the slots hold; the wrapped
+    difference waits, gives up, and reports it."""
+    from constellation_b200._lib import CstError
+
+    ctx, xt, wt, bt, rt, ref, res = layer
+    buf = torch.zeros(T * H + 64, dtype=torch.int32, device=dev)
+    buf[FLAGS] = s32((1 << 31) - 4 * CTAS)
+    buf[EPOCH] = s32((1 << 31) - 2)  # after the push: counter 2^31 - 3 CTAS, target 2^31 + 4
+    ps = peer_set(buf)
+    idx, wts = ctx.route(xt, wt, bt)
+    ctx.moe_routed_push(xt, idx, wts, ps)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    out = ctx.reduce_pushed(ps, residual=rt, out_dtype=torch.float32)
+    torch.cuda.synchronize(dev)
+    waited = time.perf_counter() - t0
+    print(f"bounded wait gave up after {waited:.3f} s")
+    with pytest.raises(CstError):
+        ctx.device_error()
+    assert torch.equal(out, rt)  # only the residual
+    assert waited < 30.0
+    # the error word was cleared and the context still runs a full exchange
+    buf2 = torch.zeros(T * H + 64, dtype=torch.int32, device=dev)
+    good = exchange(ctx, xt, wt, bt, rt, peer_set(buf2))
+    ctx.device_error()
+    fused = ctx.moe_layer(xt, wt, bt, out_dtype=torch.float32) + rt
+    torch.testing.assert_close(good, fused, rtol=1e-5, atol=1e-5)
