@@ -505,10 +505,10 @@ int cst_route(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float
     if (!valid_dtype(x_dtype)) return fail(CST_ERR_INVALID_ARG, "bad x_dtype %d", x_dtype);
     if (T < 0 || T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, c->cfg.max_tokens);
     if (top_k <= 0 || top_k > c->cfg.top_k) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of [1, %d]", top_k, c->cfg.top_k);
+    if (T == 0) return CST_OK;  // empty batch: no work, pointers may be null
     if (!x || !gate_weight || !bias || !topk_idx || !topk_weight) return fail(CST_ERR_INVALID_ARG, "null pointer");
     if (!aligned16(x) || !aligned16(gate_weight))
         return fail(CST_ERR_INVALID_ARG, "x and gate_weight must be 16-byte aligned");
-    if (T == 0) return CST_OK;
     if (int rc = ensure_device(c)) return rc;
     const cst_config& f = c->cfg;
     CST_CUDA(launch_router(x, x_dtype, gate_weight, bias, resident, T, f.n_routed_experts, f.hidden_dim, f.n_group,
@@ -585,9 +585,9 @@ int cst_moe_routed(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const 
     if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
     if (T < 0 || T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d out of range", T);
     if (top_k <= 0 || top_k > 15) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of range", top_k);
+    if (T == 0) return CST_OK;
     if (!x || !out || !topk_idx || !topk_weight) return fail(CST_ERR_INVALID_ARG, "null pointer");
     if (!aligned16(x) || !aligned16(out)) return fail(CST_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
-    if (T == 0) return CST_OK;
     if (int rc = ensure_device(c)) return rc;
     prof_begin(c, static_cast<cudaStream_t>(stream));
     prof_fill_skipped(c, 0, static_cast<cudaStream_t>(stream));
@@ -605,9 +605,9 @@ int cst_moe_routed_range(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, 
     if (top_k <= 0 || top_k > 15) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of range", top_k);
     if (shared_begin < 0 || shared_end < shared_begin || shared_end > T)
         return fail(CST_ERR_INVALID_ARG, "shared token range [%d, %d) outside [0, %d)", shared_begin, shared_end, T);
+    if (T == 0) return CST_OK;
     if (!x || !out || !topk_idx || !topk_weight) return fail(CST_ERR_INVALID_ARG, "null pointer");
     if (!aligned16(x) || !aligned16(out)) return fail(CST_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
-    if (T == 0) return CST_OK;
     if (int rc = ensure_device(c)) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     prof_begin(c, s);
@@ -625,10 +625,10 @@ int cst_moe_layer(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const f
     if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
     if (T < 0 || T > c->cfg.max_tokens) return fail(CST_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, c->cfg.max_tokens);
     if (top_k <= 0 || top_k > c->cfg.top_k) return fail(CST_ERR_INVALID_ARG, "top_k=%d out of range", top_k);
+    if (T == 0) return CST_OK;
     if (!x || !out || !gate_weight || !bias) return fail(CST_ERR_INVALID_ARG, "null pointer");
     if (!aligned16(x) || !aligned16(out) || !aligned16(gate_weight) || (residual && !aligned16(residual)))
         return fail(CST_ERR_INVALID_ARG, "x, out, gate_weight and residual must be 16-byte aligned");
-    if (T == 0) return CST_OK;
     if (int rc = ensure_device(c)) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int32_t* idx = topk_idx ? topk_idx : c->ws.topk_idx;
@@ -648,10 +648,10 @@ int cst_grouped_ffn(cst_ctx* c, const void* x, int32_t x_dtype, int32_t R, const
     if (int rc = check_ctx(c)) return rc;
     if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
     if (R < 0 || R > c->max_rows) return fail(CST_ERR_INVALID_ARG, "R=%d exceeds the workspace (%d rows)", R, c->max_rows);
-    if (!x || !y || !row_slot) return fail(CST_ERR_INVALID_ARG, "null pointer");
     if (R > kMaxRowsModeRows) return fail(CST_ERR_INVALID_ARG, "R=%d exceeds %d rows per call", R, kMaxRowsModeRows);
-    if (!aligned16(x) || !aligned16(y)) return fail(CST_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
     if (R == 0) return CST_OK;
+    if (!x || !y || !row_slot) return fail(CST_ERR_INVALID_ARG, "null pointer");
+    if (!aligned16(x) || !aligned16(y)) return fail(CST_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
     if (int rc = ensure_device(c)) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     PackArgs pa{};
@@ -709,10 +709,10 @@ int cst_shared_combine(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, co
     if (int rc = check_ctx(c)) return rc;
     if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
     if (T < 0 || T > c->max_rows || T > kMaxRowsModeRows) return fail(CST_ERR_INVALID_ARG, "T=%d out of range", T);
+    if (T == 0) return CST_OK;
     if (!x || !out) return fail(CST_ERR_INVALID_ARG, "null pointer");
     if (!aligned16(x) || !aligned16(out) || (extra && !aligned16(extra)) || (residual && !aligned16(residual)))
         return fail(CST_ERR_INVALID_ARG, "x, extra, residual and out must be 16-byte aligned");
-    if (T == 0) return CST_OK;
     if (int rc = ensure_device(c)) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     prof_begin(c, s);
@@ -744,12 +744,12 @@ int cst_combine_rows(cst_ctx* c, const float* rows, int64_t ld_rows, const int32
     if (int rc = check_ctx(c)) return rc;
     if (!valid_dtype(out_dtype) || (residual && !valid_dtype(residual_dtype)))
         return fail(CST_ERR_INVALID_ARG, "bad dtype");
-    if (T < 0 || k1 < 0 || k1 > 16 || (k1 > 0 && (!rows || !tk_row)) || !out)
-        return fail(CST_ERR_INVALID_ARG, "bad arguments (T=%d, k1=%d; k1 must be <= 16)", T, k1);
+    if (T < 0 || k1 < 0 || k1 > 16) return fail(CST_ERR_INVALID_ARG, "bad arguments (T=%d, k1=%d; k1 must be <= 16)", T, k1);
+    if (T == 0) return CST_OK;
+    if ((k1 > 0 && (!rows || !tk_row)) || !out) return fail(CST_ERR_INVALID_ARG, "null pointer");
     if ((rows && (!aligned16(rows) || ld_rows % 4)) || !aligned16(out) || (extra && !aligned16(extra)) ||
         (residual && !aligned16(residual)))
         return fail(CST_ERR_INVALID_ARG, "rows, extra, residual and out must be 16-byte aligned");
-    if (T == 0) return CST_OK;
     if (int rc = ensure_device(c)) return rc;
     CombineArgs ca{rows, ld_rows, tk_row, k1, T, c->cfg.hidden_dim, residual, residual_dtype, out, out_dtype, extra};
     CST_CUDA(launch_combine(ca, static_cast<cudaStream_t>(stream)));
@@ -772,10 +772,11 @@ int cst_dequant_fp8(const uint8_t* w, const float* scale_inv, int32_t rows, int3
 int cst_rmsnorm(const void* x, int32_t x_dtype, int32_t T, int32_t H, const float* weight, float eps, void* out,
                 int32_t out_dtype, void* stream) {
     g_last_error.clear();
-    if (!x || !out) return fail(CST_ERR_INVALID_ARG, "null pointer");
     if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(CST_ERR_INVALID_ARG, "bad dtype");
     if (T < 0 || H <= 0 || H % 8) return fail(CST_ERR_INVALID_ARG, "bad shape (T=%d, H=%d; H must be a multiple of 8)", T, H);
     if (!(eps >= 0.0f)) return fail(CST_ERR_INVALID_ARG, "eps must be >= 0");
+    if (T == 0) return CST_OK;
+    if (!x || !out) return fail(CST_ERR_INVALID_ARG, "null pointer");
     if (!aligned16(x) || !aligned16(out)) return fail(CST_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
     CST_CUDA(launch_rmsnorm(x, x_dtype, T, H, weight, eps, out, out_dtype, static_cast<cudaStream_t>(stream)));
     return CST_OK;

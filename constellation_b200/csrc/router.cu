@@ -662,9 +662,6 @@ extern "C" int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int3
     using namespace cst;
     clear_last_error();
     if (x_dtype < 1 || x_dtype > 3) return set_last_error(3, "bad x_dtype %d", x_dtype);
-    if (!x || !gate_weight || !bias || !topk_idx || !topk_weight) return set_last_error(3, "null pointer");
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate_weight)) & 15u)
-        return set_last_error(3, "x and gate_weight must be 16-byte aligned");
     if (hidden <= 0 || hidden % 128) return set_last_error(3, "hidden=%d must be a positive multiple of 128", hidden);
     if (n_experts <= 0 || n_experts > 1024) return set_last_error(3, "n_experts=%d out of [1, 1024]", n_experts);
     if (n_group <= 0 || n_group > 32 || n_experts % n_group)
@@ -679,7 +676,10 @@ extern "C" int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int3
                               "maximum of %lld (T <= %lld for n_experts = %d); use cst_route",
                               static_cast<long long>(need), static_cast<long long>(kNoAllocScratchFloats),
                               static_cast<long long>(kNoAllocScratchFloats / n_experts), n_experts);
-    if (T == 0) return 0;
+    if (T == 0) return 0;  // empty batch: no work, pointers may be null
+    if (!x || !gate_weight || !bias || !topk_idx || !topk_weight) return set_last_error(3, "null pointer");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate_weight)) & 15u)
+        return set_last_error(3, "x and gate_weight must be 16-byte aligned");
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
         return set_last_error(5, "cudaGetDevice failed or device id out of range");

@@ -164,6 +164,8 @@ class ExpertParallelMoE:
         from .p2p import PeerExchange
 
         Tl, H = x_local.shape
+        if Tl == 0:  # equal on every rank (the all-gather takes equal shares): nothing to exchange
+            return torch.empty((0, H), dtype=od, device=x_local.device)
         if self._peers is None:
             self._peers = PeerExchange(x_local.device, world=self.world, rank=self.rank, tl_cap=max(Tl, 1),
                                        hidden=H, group=self.group)

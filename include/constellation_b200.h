@@ -7,6 +7,11 @@
  * argument (a cudaStream_t passed as void*; NULL = legacy default stream); nothing
  * synchronises the device except cst_device_error and cst_destroy.
  *
+ * Empty batches: a token or row count of 0 is a no-op that returns CST_OK once the scalar
+ * arguments are valid, whatever the data pointers (a zero-size device buffer may be NULL).
+ * The exceptions keep the reference's rules: cst_expert_forward answers batch 0 with
+ * CST_ERR_BACKEND like the worker, and a peer exchange needs tl >= 1.
+ *
  * Threading: one context per device; calls on one context must be serialised by the
  * caller, like the reference node's one worker thread per GPU
  * (expert_node_v2/main.cc:132-149) and its registry lock (worker.cc:120, control.cc:172).

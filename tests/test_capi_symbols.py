@@ -55,6 +55,22 @@ def test_invalid_config_is_rejected_before_touching_a_device():
     assert h.value is None
 
 
+def test_empty_batch_needs_no_device_or_pointers():
+    """T = 0 returns CST_OK once the scalar arguments are valid, with NULL data pointers
+    (a zero-size device tensor has one); invalid scalars are still rejected."""
+    from constellation_b200 import _lib
+
+    L = _lib.lib
+    assert L.cst_rmsnorm(None, 2, 0, 256, None, 1e-6, None, 2, None) == _lib.CST_OK
+    assert L.cst_rmsnorm(None, 2, 0, 12, None, 1e-6, None, 2, None) == _lib.CST_ERR_INVALID_ARG
+    assert L.cst_rmsnorm(None, 2, 1, 256, None, 1e-6, None, 2, None) == _lib.CST_ERR_INVALID_ARG
+    route = (256, None, None, None, 16, 4, 2, 4, 1, 2.5, None, None, None)
+    assert L.cst_route_noalloc(None, 2, 0, *route) == _lib.CST_OK
+    assert L.cst_route_noalloc(None, 2, -1, *route) == _lib.CST_ERR_INVALID_ARG
+    assert L.cst_route_noalloc(None, 2, 1, *route) == _lib.CST_ERR_INVALID_ARG
+    assert "null pointer" in _lib.last_error()
+
+
 def test_product_has_no_oracle_dependency():
     """The shipped package never imports the oracle (it is test infrastructure)."""
     pkg = REPO / "constellation_b200"
