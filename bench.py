@@ -60,10 +60,11 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=58, help="config3: stacked layers")
-    p.add_argument("--workload", choices=["config2", "config1", "config3", "config4"], default="config2",
+    p.add_argument("--workload", choices=["config2", "config1", "config3", "config4", "worker"], default="config2",
                    help="config2: the full decode layer, T=64 (default); config1: grouped FP8 expert matvec "
                         "only, 32 resident experts with n_e ~ U{1..16} rows each, 1 GPU; config4: one layer "
-                        "over a 4096-token prefill chunk with a Zipf-skewed router bias")
+                        "over a 4096-token prefill chunk with a Zipf-skewed router bias; worker: the expert "
+                        "node's InferRequest path, batch --tokens (default 1), 32 resident experts, 1 GPU")
     p.add_argument("--resident-experts", type=int, default=E,
                    help="upload only the first N routed experts of each rank (small profiling case; "
                         "routes to the others contribute nothing)")
@@ -790,6 +791,197 @@ def cpu_config1_rate(seconds: float, sample_rows: int = 4):
 
 
 # ---------------------------------------------------------------------------------------
+W_EXPERTS = 32  # experts the node's requests cycle over: 1.41 GB of weights, more than L2
+
+
+def worker_requests(torch, batch: int, seed: int = 0):
+    """One seeded bf16 -> bf16 InferRequest body per resident expert (global ids 0..31),
+    ``batch`` N(0, 1) rows each, and the rows themselves."""
+    from constellation_b200 import protocol as P
+
+    g = torch.Generator().manual_seed(seed)
+    xs = torch.randn((W_EXPERTS, batch, H), generator=g).to(torch.bfloat16)
+    bodies = [P.encode_infer_request(dict(expert_id=j, batch_size=batch, hidden_dim=H, input_dtype=2,
+                                          output_dtype=2, activation=xs[j].view(torch.int16).numpy().tobytes()))
+              for j in range(W_EXPERTS)]
+    return xs, bodies
+
+
+def worker_metric(batch: int) -> str:
+    return f"expert requests/s (batch-{batch} bf16 InferRequest, one DeepSeek-V3 FP8 expert each)"
+
+
+def run_worker(args):
+    """The expert node's request path (``worker.cc`` HandleInferRequest + RunExpertRequest):
+    a step is one request to each of 32 resident experts in turn.  ``value``: requests/s
+    with the rows already on the device (``cst_expert_forward``); ``e2e``: the same
+    requests as wire bodies through ``cst_serve_infer_request`` (decode, host-to-device
+    copy, expert, device-to-host copy into the response body, encode, stream sync)."""
+    import torch
+
+    from constellation_b200 import protocol as P
+    from constellation_b200 import synthetic
+    from constellation_b200.context import ExpertContext, MoEConfig
+    from constellation_b200.worker import handle_infer_request
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1 or args.gpus != 1:
+        raise SystemExit("--workload worker is a single-GPU configuration")
+    batch = int(args.tokens or 1)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ctx = ExpertContext(dev, MoEConfig(), n_slots=W_EXPERTS, max_tokens=64, max_rows=max(batch, 64 * (K + 1)))
+    for j in range(W_EXPERTS):
+        ex = synthetic.make_expert(H, I, seed=1000 + j, device=dev)
+        ctx.upload_expert(j, j, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
+        del ex
+    xs_h, bodies = worker_requests(torch, batch)
+    xs = xs_h.to(dev)
+    y = torch.empty((batch, H), dtype=torch.bfloat16, device=dev)
+    torch.cuda.synchronize(dev)
+
+    def step():
+        for j in range(W_EXPERTS):
+            ctx.expert_forward(j, xs[j], out=y)
+
+    def timed(fn, k):
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(k):
+            fn()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    graph = None
+    if not args.no_graph:
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(3):
+            graph.replay()
+    run = graph.replay if graph is not None else step
+    with ClockSampler(0) as clk:
+        ms_step = timed(run, args.steps) / args.steps
+    clocks = clk.summary()
+    ms_req = ms_step / W_EXPERTS
+
+    # end to end: wire bodies in, wire bodies out, one synchronous request at a time
+    def e2e_step():
+        resp = None
+        for body in bodies:
+            resp = handle_infer_request([ctx], body)
+        return resp
+
+    for _ in range(3):
+        last = e2e_step()
+    r = P.decode_infer_response(last)
+    if r["status_code"] != 0 or len(r["output"]) != batch * H * 2:
+        raise RuntimeError(f"worker request failed: status {r['status_code']}")
+    ms_e2e = timed(e2e_step, args.steps) / args.steps
+
+    ctx.profile(True)
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    stages = ctx.profile_read()
+    ctx.profile(False)
+    stage_ms = {k: statistics.mean(st[k] for st in stages) for k in stages[0]}
+    req_bytes = EXPERT_BYTES + batch * H * (2 + 2)
+    upg_ms, dn_ms = stage_ms["grouped_up_gate"], stage_ms["grouped_down"]
+    peak, peak_kind = measured_peaks()
+    ach = req_bytes / ((upg_ms + dn_ms) / 1e3) / 1e9
+    line = {
+        "metric": worker_metric(batch),
+        "value": round(1e3 / ms_req, 1),
+        "unit": "requests/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3 weights x e4m3(3-term) activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, 128x128 block E4M3; N(0,1) bf16 rows)",
+        "config": {"workload": f"worker_requests_batch{batch}", "experts": W_EXPERTS, "batch": batch,
+                   "requests_per_step": W_EXPERTS, "hidden": H, "inter": I, "cuda_graph": graph is not None,
+                   "l2": "no flush: the 32 experts' 1.41 GB of weights exceed the 126 MB L2"},
+        "roofline": {"kernel": "grouped_ffn_tc up/gate + down of one request (tcgen05, TMA bulk ring)",
+                     "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(ach / peak, 4), "peak_source": peak_kind, "bytes_per_launch": req_bytes,
+                     "ms_per_launch": round(upg_ms + dn_ms, 4), "traffic": None},
+        "us_per_request": round(ms_req * 1e3, 2),
+        "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+        "e2e": {"value": round(W_EXPERTS * 1e3 / ms_e2e, 1), "unit": "requests/s",
+                "us_per_request": round(ms_e2e * 1e3 / W_EXPERTS, 2),
+                "h2d_bytes_per_step": W_EXPERTS * batch * H * 2, "d2h_bytes_per_step": W_EXPERTS * batch * H * 2,
+                "path": "wire body -> cst_serve_infer_request -> wire body, synchronous per request"},
+        # route_pack, pack x, up/gate, pack h, down, combine per request
+        "gpu_launches": 6 * W_EXPERTS * args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = cpu_worker_rate(args.cpu_seconds, batch)
+        except Exception as exc:
+            line["cpu_baseline"] = {"value": None, "error": f"{type(exc).__name__}: {exc}"}
+    if graph is not None:
+        graph.reset()
+    emit(line)
+
+
+def cpu_worker_rate(seconds: float, batch: int = 1, sample_experts: int = 4):
+    """The reference node's OpenMP FP8 CPU kernels serving the same requests (one batch-1
+    call per row, as RunExpertRequest takes batch 1) on a sample of the experts."""
+    import numpy as np
+    import torch
+
+    from constellation_b200 import synthetic
+    from oracle import refbuild
+
+    threads = os.cpu_count() or 1
+    kind = "reference" if refbuild.ref_available() else "port"
+    xs, _ = worker_requests(torch, batch)
+    experts = []
+    for j in range(sample_experts):
+        ex = synthetic.make_expert(H, I, seed=1000 + j, device="cpu")
+        experts.append(refbuild.ExpertBytes(ex.w_up.numpy(), ex.s_up.numpy(), ex.w_gate.numpy(), ex.s_gate.numpy(),
+                                            ex.w_down.numpy(), ex.s_down.numpy()))
+    xb = xs.view(torch.int16).numpy().view(np.uint16)
+
+    def one(j):
+        if kind == "reference":
+            refbuild.ref_expert_cpu(experts[j], xb[j], 2, 2, threads)
+        else:
+            for row in xb[j]:
+                xf = (row.astype(np.uint32) << 16).view(np.float32)
+                refbuild.oracle_expert_lut(experts[j], xf[None])
+
+    one(0)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        for j in range(sample_experts):
+            one(j)
+        n += sample_experts
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    return {"value": round(n / dt, 3), "unit": "requests/s", "cores": threads, "kind": kind,
+            "sample": f"{n} batch-{batch} requests to experts 0..{sample_experts - 1} ({dt:.1f} s)",
+            "ms_per_request": round(dt / n * 1e3, 2)}
+
+
+# ---------------------------------------------------------------------------------------
 class CpuReferenceLayer:
     """The reference CPU path for a sample of tokens: router (CPU restatement of
     route_token_real), one batch-1 call of the reference node's OpenMP FP8 expert kernels
@@ -885,6 +1077,17 @@ def run_reference(args):
               "cpu_baseline": base,
               "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return
+    if args.workload == "worker":
+        batch = int(args.tokens or 1)
+        base = cpu_worker_rate(args.cpu_seconds, batch)
+        emit({"impl": "reference", "metric": worker_metric(batch), "value": base["value"], "unit": "requests/s",
+              "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+              "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (FP8 LUT decode x block scale)",
+              "data": "synthetic", "config": {"workload": f"worker_requests_batch{batch}", "parallelism": "cpu"},
+              "cpu_baseline": base,
+              "e2e": {"value": base["value"], "unit": "requests/s", "h2d_bytes_per_step": 0,
+                      "d2h_bytes_per_step": 0}})
+        return
     if args.workload == "config3":
         # one token through one layer of the reference CPU path, times the layer count
         base = cpu_reference_rate(args.cpu_sample_tokens, args.cpu_seconds, T=args.tokens or 128)
@@ -961,6 +1164,8 @@ def main():
         run_config1(args)
     elif args.workload == "config3":
         run_config3(args)
+    elif args.workload == "worker":
+        run_worker(args)
     else:
         run_ours(args)
 

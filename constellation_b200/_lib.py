@@ -34,7 +34,11 @@ EXPORTED = (
     "cst_profile_enable", "cst_profile_read", "cst_shared_combine", "cst_combine_rows", "cst_dequant_fp8",
     "cst_route_noalloc", "cst_moe_routed_range", "cst_set_gemm_mode", "cst_rmsnorm",
     "cst_ipc_alloc", "cst_ipc_open", "cst_ipc_close", "cst_ipc_free", "cst_moe_routed_push", "cst_reduce_pushed",
+    "cst_encode_infer_request", "cst_decode_infer_request", "cst_encode_infer_response", "cst_decode_infer_response",
+    "cst_serve_infer_request",
 )
+CST_INFER_REQUEST_FIXED_BYTES = 24
+CST_INFER_RESPONSE_FIXED_BYTES = 20
 CST_MAX_PEERS = 8
 CST_GEMM_AUTO, CST_GEMM_DECODE, CST_GEMM_PREFILL = 0, 1, 2
 CST_N_STAGES = 7
@@ -89,13 +93,24 @@ class CstPeerSet(ctypes.Structure):
                 ("flags", ctypes.c_void_p * CST_MAX_PEERS), ("epoch", ctypes.c_void_p), ("done", ctypes.c_void_p)]
 
 
+class CstInferRequest(ctypes.Structure):
+    _fields_ = [("expert_id", ctypes.c_int32), ("batch_size", ctypes.c_int32), ("hidden_dim", ctypes.c_int32),
+                ("input_dtype", ctypes.c_uint32), ("output_dtype", ctypes.c_uint32),
+                ("activation_bytes", ctypes.c_uint32), ("activation", ctypes.c_void_p)]
+
+
+class CstInferResponse(ctypes.Structure):
+    _fields_ = [("status_code", ctypes.c_int32), ("batch_size", ctypes.c_int32), ("hidden_dim", ctypes.c_int32),
+                ("output_dtype", ctypes.c_uint32), ("output_bytes", ctypes.c_uint32), ("output", ctypes.c_void_p)]
+
+
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.is_file():
         raise ImportError(
             f"{LIB_PATH.name} is not built; run `python -m constellation_b200.build` "
             "(nvcc, sm_100a). The MoE path has no CPU fallback.")
     lib = ctypes.CDLL(str(LIB_PATH))
-    P, I32, U32, F = ctypes.c_void_p, ctypes.c_int32, ctypes.c_uint32, ctypes.c_float
+    P, I32, U32, F, I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_uint32, ctypes.c_float, ctypes.c_int64
     sig = {
         "cst_create": (ctypes.c_int, [I32, ctypes.POINTER(CstConfig), ctypes.POINTER(P)]),
         "cst_destroy": (None, [P]),
@@ -127,6 +142,12 @@ def _load() -> ctypes.CDLL:
         "cst_ipc_free": (ctypes.c_int, [P]),
         "cst_moe_routed_push": (ctypes.c_int, [P, P, I32, P, P, I32, ctypes.POINTER(CstPeerSet), P]),
         "cst_reduce_pushed": (ctypes.c_int, [P, ctypes.POINTER(CstPeerSet), P, I32, P, I32, P]),
+        "cst_encode_infer_request": (ctypes.c_int, [ctypes.POINTER(CstInferRequest), P, I64, ctypes.POINTER(I64)]),
+        "cst_decode_infer_request": (ctypes.c_int, [P, I64, ctypes.POINTER(CstInferRequest)]),
+        "cst_encode_infer_response": (ctypes.c_int, [ctypes.POINTER(CstInferResponse), P, I64, ctypes.POINTER(I64)]),
+        "cst_decode_infer_response": (ctypes.c_int, [P, I64, ctypes.POINTER(CstInferResponse)]),
+        "cst_serve_infer_request": (ctypes.c_int, [ctypes.POINTER(P), I32, I32, P, I64, P, I64, ctypes.POINTER(I64),
+                                                   P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -8,6 +8,7 @@
 //   cst_grouped_ffn / cst_expert_forward = route_pack (rows mode) -> ... -> combine
 // Capacity checks happen on the host from the call's shapes, so no device overflow can
 // occur and nothing has to be read back.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -104,6 +105,10 @@ struct cst_ctx {
     uint8_t* ws_base = nullptr;
     size_t ws_bytes = 0;
     Workspace ws;
+    // cst_serve_infer_request: device copies of one request's activation and output,
+    // allocated at the first request (max rows x hidden x 2 bytes each)
+    uint8_t* serve_io = nullptr;
+    size_t serve_half = 0;
     // stage profiling (cst_profile_enable): one event per stage boundary per call
     bool prof = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -309,6 +314,9 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     dn.row_weight = w.row_weight;
     dn.out_rows = c->max_rows;
     dn.max_split = 1;
+    // one expert's rows (cst_expert_forward, the shared expert alone): the group count is
+    // known here; routed calls leave it to the device
+    dn.groups_hint = pa.single_slot >= 0 ? (pa.T + pa.group_rows - 1) / pa.group_rows : 0;
     CST_CUDA(grouped(dn, false, c->num_sms, s));
     prof_mark(c, 5, s);
     return CST_OK;
@@ -409,6 +417,7 @@ void cst_destroy(cst_ctx* c) {
     cudaFree(c->staging);
     cudaFree(c->d_slot_of_expert);
     cudaFree(c->ws_base);
+    cudaFree(c->serve_io);
     delete c;
 }
 
@@ -700,6 +709,103 @@ int cst_expert_forward(cst_ctx* c, int32_t expert_id, const void* x, int32_t in_
                    nullptr};
     CST_CUDA(launch_combine(ca, s));
     prof_mark(c, 6, s);
+    return CST_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// The device half of one request: activation in, expert run, output back into the host
+// response, stream synchronised (the reference worker copies synchronously too,
+// backend_workspace_cuda_v2.cc:64-105).
+int serve_run(cst_ctx* c, int32_t local_id, const cst_infer_request& m, uint8_t* out_host, void* stream) {
+    if (int rc = ensure_device(c)) return rc;
+    if (c->serve_io == nullptr) {
+        const int64_t rows = std::min<int64_t>(c->max_rows, kMaxRowsModeRows);
+        const size_t half = (size_t(rows) * c->cfg.hidden_dim * 2 + 255) & ~size_t(255);
+        CST_CUDA(cudaMalloc(&c->serve_io, 2 * half));
+        c->serve_half = half;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t nbytes = m.activation_bytes;  // batch * hidden * 2, checked by the caller
+    uint8_t* din = c->serve_io;
+    uint8_t* dout = c->serve_io + c->serve_half;
+    CST_CUDA(cudaMemcpyAsync(din, m.activation, nbytes, cudaMemcpyHostToDevice, s));
+    if (int rc = cst_expert_forward(c, local_id, din, int32_t(m.input_dtype), m.batch_size, dout,
+                                    int32_t(m.output_dtype), stream))
+        return rc;
+    CST_CUDA(cudaMemcpyAsync(out_host, dout, nbytes, cudaMemcpyDeviceToHost, s));
+    CST_CUDA(cudaStreamSynchronize(s));
+    return CST_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cst_serve_infer_request(cst_ctx* const* layers, int32_t n_layers, int32_t experts_per_layer,
+                            const uint8_t* req_body, int64_t req_len, uint8_t* resp_body, int64_t resp_cap,
+                            int64_t* resp_len, void* stream) {
+    g_last_error.clear();
+    if (resp_len == nullptr) return fail(CST_ERR_INVALID_ARG, "null resp_len");
+    *resp_len = 0;
+    if (n_layers < 0 || (n_layers > 0 && layers == nullptr) || experts_per_layer <= 0)
+        return fail(CST_ERR_INVALID_ARG, "bad layer table (n_layers=%d, experts_per_layer=%d)", n_layers,
+                    experts_per_layer);
+    cst_infer_request m{};
+    if (int rc = cst_decode_infer_request(req_body, req_len, &m)) return rc;  // no reply (worker.cc:92-97)
+    // the worker's lookup (worker.cc:112-130): no entry -> 1, not on this device -> 2
+    int32_t status = CST_ERR_BACKEND;
+    cst_ctx* c = nullptr;
+    int32_t local_id = -1;
+    const int32_t layer = m.expert_id >= 0 ? m.expert_id / experts_per_layer : -1;
+    if (layer < 0 || layer >= n_layers || layers[layer] == nullptr) {
+        status = CST_ERR_UNKNOWN_EXPERT;
+    } else {
+        c = layers[layer];
+        if (c->cfg.n_routed_experts != experts_per_layer)
+            return fail(CST_ERR_INVALID_ARG, "experts_per_layer=%d, but the layer-%d context routes %d experts",
+                        experts_per_layer, layer, c->cfg.n_routed_experts);
+        local_id = m.expert_id % experts_per_layer;
+        if (c->slot_of_expert[local_id] < 0) status = CST_ERR_NOT_RESIDENT;
+    }
+    // RunExpertRequest's checks (backend_workspace_cuda_v2.cc:139-181, :33-39), batch >= 1
+    int64_t out_bytes = 0;
+    bool usable = false;
+    if (c != nullptr && status == CST_ERR_BACKEND) {
+        const int64_t H = c->cfg.hidden_dim;
+        const int64_t max_batch = std::min<int64_t>(c->max_rows, kMaxRowsModeRows);
+        const auto wire = [](uint32_t d) { return d == CST_DTYPE_FP16 || d == CST_DTYPE_BF16; };
+        if (m.batch_size < 1 || m.batch_size > max_batch)
+            fail(CST_ERR_BACKEND, "batch %d outside [1, %lld]", m.batch_size, static_cast<long long>(max_batch));
+        else if (m.hidden_dim != H)
+            fail(CST_ERR_BACKEND, "hidden_dim %d, the context has %lld", m.hidden_dim, static_cast<long long>(H));
+        else if (!wire(m.input_dtype) || !wire(m.output_dtype))
+            fail(CST_ERR_BACKEND, "unsupported dtype pair (%u, %u)", m.input_dtype, m.output_dtype);
+        else if (int64_t(m.activation_bytes) != int64_t(m.batch_size) * H * 2)
+            fail(CST_ERR_BACKEND, "activation holds %u bytes, batch x hidden x 2 = %lld", m.activation_bytes,
+                 static_cast<long long>(int64_t(m.batch_size) * H * 2));
+        else {
+            usable = true;
+            out_bytes = int64_t(m.batch_size) * H * 2;
+        }
+    }
+    const int64_t need = kInferResponseFixedBytes + out_bytes;
+    if (resp_body == nullptr || resp_cap < need) {
+        *resp_len = need;
+        return fail(CST_ERR_INVALID_ARG, "the response needs %lld bytes, the buffer holds %lld",
+                    static_cast<long long>(need), static_cast<long long>(resp_body ? resp_cap : 0));
+    }
+    if (usable) {
+        if (serve_run(c, local_id, m, resp_body + kInferResponseFixedBytes, stream) == CST_OK) {
+            status = CST_OK;
+        } else {
+            out_bytes = 0;  // the worker's failed run: status 4, no output (worker.cc:124-128)
+        }
+    }
+    put_infer_response_fixed(resp_body, status, m.batch_size, m.hidden_dim, m.output_dtype, uint32_t(out_bytes));
+    *resp_len = kInferResponseFixedBytes + out_bytes;
     return CST_OK;
 }
 

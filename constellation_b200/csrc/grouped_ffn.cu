@@ -345,12 +345,14 @@ cudaError_t grouped_ffn_init_attributes() {
 }
 
 // up/gate: a.n_mb = I / 128 row blocks.  down: a.n_mb = H / 128 row blocks; pairs of blocks per
-// item when that count is even (32 KB of weights per stage, as up/gate), else one.
+// item when that count is even (32 KB of weights per stage, as up/gate) and the launch has
+// enough groups to give every SM a pair, else one block per item.
 cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream) {
+    const bool few_items = a.groups_hint > 0 && int64_t(a.groups_hint) * (a.n_mb / 2) < num_sms;
     if (upgate) {
         grouped_ffn_tc_kernel<2, kUpGateStages, false>
             <<<num_sms, 192, tc_smem_bytes<2, kUpGateStages>(), stream>>>(a);
-    } else if (a.n_mb % 2 == 0) {
+    } else if (a.n_mb % 2 == 0 && !few_items) {
         FfnArgs p = a;
         p.n_mb = a.n_mb / 2;
         grouped_ffn_tc_kernel<2, kUpGateStages, true>

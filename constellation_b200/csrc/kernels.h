@@ -13,6 +13,13 @@ namespace cst {
 void clear_last_error();
 int set_last_error(int code, const char* fmt, ...);
 
+// infer_codec.cu: the fixed 20 bytes of an InferResponse body (status, batch, hidden,
+// output dtype, output byte count), little-endian
+constexpr int kInferRequestFixedBytes = 24;
+constexpr int kInferResponseFixedBytes = 20;
+void put_infer_response_fixed(uint8_t* body, int32_t status, int32_t batch, int32_t hidden, uint32_t out_dtype,
+                              uint32_t nbytes);
+
 // relayout.cu
 cudaError_t launch_relayout(const uint8_t* wu, const uint8_t* wg, const uint8_t* wd, uint8_t* slot,
                             int inter, int hidden, int num_sms, cudaStream_t stream);
@@ -116,6 +123,11 @@ struct FfnArgs {
     int max_split;            // largest K split this launch may choose (1 = never split)
     const float* row_weight;  // down only
     int* err;
+    // down: an upper bound on the groups of this launch known on the host (one expert's
+    // request: ceil(rows / group rows)), or 0 when the routing decides it on the device.
+    // Below one row-block pair per SM the launch takes single row blocks per item, which
+    // doubles the items a lone expert spreads over.
+    int groups_hint;
 };
 cudaError_t grouped_ffn_init_attributes();
 cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream);

@@ -5,7 +5,8 @@
  * Every device pointer argument is caller-owned, except the expert arena the context
  * allocates and fills through cst_upload_expert.  All work is enqueued on the `stream`
  * argument (a cudaStream_t passed as void*; NULL = legacy default stream); nothing
- * synchronises the device except cst_device_error and cst_destroy.
+ * synchronises the device except cst_device_error, cst_serve_infer_request (it returns the
+ * output bytes) and cst_destroy.
  *
  * Empty batches: a token or row count of 0 is a no-op that returns CST_OK once the scalar
  * arguments are valid, whatever the data pointers (a zero-size device buffer may be NULL).
@@ -278,6 +279,55 @@ int cst_moe_routed_push(cst_ctx* ctx, const void* x, int32_t x_dtype, const int3
  * word (cst_device_error) and leaves only the residual in out. */
 int cst_reduce_pushed(cst_ctx* ctx, const cst_peer_set* peers, const void* residual, int32_t residual_dtype,
                       void* out, int32_t out_dtype, void* stream);
+
+/* ---- Expert-node requests ------------------------------------------------------------
+ * The worker's InferRequest / InferResponse bodies (common/infer_codec.cc:7-76 over the
+ * little-endian helpers of common/protocol.cc:13-80; common/protocol.py:503-577 on the
+ * coordinator side), and the handling of one request (expert_node_v2/worker.cc:83-140 with
+ * backend/cuda/backend_workspace_cuda_v2.cc:19-181), minus the socket and the 16-byte
+ * message header.  The four codec calls are host-only and touch no device. */
+#define CST_INFER_REQUEST_FIXED_BYTES 24  /* i32 expert_id, batch_size, hidden_dim; u32 input_dtype, output_dtype, n */
+#define CST_INFER_RESPONSE_FIXED_BYTES 20 /* i32 status_code, batch_size, hidden_dim; u32 output_dtype, n */
+typedef struct {
+    int32_t expert_id;  /* global id: layer * experts_per_layer + local id (expert_placement.py:4-24) */
+    int32_t batch_size;
+    int32_t hidden_dim;
+    uint32_t input_dtype; /* CST_DTYPE_FP16 / CST_DTYPE_BF16 (0 = unknown) */
+    uint32_t output_dtype;
+    uint32_t activation_bytes;
+    const uint8_t* activation; /* decode: points into the decoded body */
+} cst_infer_request;
+typedef struct {
+    int32_t status_code; /* 0 ok, 1 unknown expert, 2 not on this device, 4 backend failure */
+    int32_t batch_size;
+    int32_t hidden_dim;
+    uint32_t output_dtype;
+    uint32_t output_bytes;
+    const uint8_t* output; /* decode: points into the decoded body */
+} cst_infer_response;
+/* EncodeInferRequestBody / EncodeInferResponseBody: *len = bytes the body takes (set even
+ * when it fails); CST_ERR_INVALID_ARG if body is NULL or cap is short. */
+int cst_encode_infer_request(const cst_infer_request* msg, uint8_t* body, int64_t cap, int64_t* len);
+int cst_encode_infer_response(const cst_infer_response* msg, uint8_t* body, int64_t cap, int64_t* len);
+/* DecodeInferRequestBody / DecodeInferResponseBody: CST_OK, or CST_ERR_INVALID_ARG for a
+ * body that ends inside a field or the payload, or has trailing bytes. */
+int cst_decode_infer_request(const uint8_t* body, int64_t len, cst_infer_request* out);
+int cst_decode_infer_response(const uint8_t* body, int64_t len, cst_infer_response* out);
+/* One request body in, one response body out, with the worker's rules: the response
+ * echoes batch_size, hidden_dim and output_dtype; status 1 if no context holds the
+ * expert's layer (layers[expert_id / experts_per_layer], NULL entries allowed), 2 if the
+ * layer's context does not hold the expert, 4 if the request is unusable (batch outside
+ * [1, the context's max rows] -- the reference takes batch 1 only --, hidden_dim not the
+ * context's, a dtype outside fp16/bf16, activation bytes != batch * hidden * 2) or the
+ * device run failed (cst_last_error() has the cause); 0 with batch * hidden * 2 output
+ * bytes otherwise.  Returns CST_OK when *resp_len bytes of response were written;
+ * CST_ERR_INVALID_ARG when the request does not decode (the worker sends no reply) or
+ * resp_cap is short (*resp_len = the size needed, nothing run).  The activation is copied
+ * to the device on `stream`, the expert runs there, the output is copied back into
+ * resp_body and the stream is synchronised before the call returns. */
+int cst_serve_infer_request(cst_ctx* const* layers, int32_t n_layers, int32_t experts_per_layer,
+                            const uint8_t* req_body, int64_t req_len, uint8_t* resp_body, int64_t resp_cap,
+                            int64_t* resp_len, void* stream);
 
 /* Synchronises the context's device, then returns CST_OK or CST_ERR_DEVICE_TIMEOUT if a
  * kernel's bounded wait gave up since the last call (and clears the flag). */

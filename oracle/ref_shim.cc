@@ -13,13 +13,16 @@
 //     cpu/down_cpu_v2.cc:10-119), the reference's OpenMP CPU backend, which is the
 //     timed CPU baseline (the thread count is passed explicitly instead of the
 //     hard-coded 12 in backend_cpu_v2.cc:245-246);
-//   * the activation codec (activation_codec_v2.h) and the FP8 LUT (fp8_lut_v2.cc).
+//   * the activation codec (activation_codec_v2.h) and the FP8 LUT (fp8_lut_v2.cc);
+//   * the node's InferRequest / InferResponse body codec (common/infer_codec.cc:7-76 over
+//     common/protocol.cc), compiled from its sources too.
 // Views are built over caller-owned memory, so nothing is copied per call.
 #include <cstdint>
 #include <cstring>
 #include <span>
 #include <vector>
 
+#include "common/infer_codec.h"
 #include "expert_node_v2/backend/activation_codec_v2.h"
 #include "expert_node_v2/backend/cpu/down_cpu_v2.h"
 #include "expert_node_v2/backend/cpu/fused_up_gate_cpu_v2.h"
@@ -133,5 +136,69 @@ std::uint16_t ref_encode_bf16(float x) { return EncodeFloatToBf16V2(x); }
 std::uint16_t ref_encode_fp16(float x) { return EncodeFloatToFp16V2(x); }
 float ref_decode_bf16(std::uint16_t b) { return DecodeBf16ToFloatV2(b); }
 float ref_decode_fp16(std::uint16_t b) { return DecodeFp16ToFloatV2(b); }
+
+// EncodeInferRequestBody: the body's length, or -1 if `cap` is short.
+long long ref_encode_infer_request(std::int32_t expert_id, std::int32_t batch, std::int32_t hidden,
+                                   std::uint32_t in_dtype, std::uint32_t out_dtype, const std::uint8_t* act,
+                                   long long n, std::uint8_t* out, long long cap) {
+    common::InferRequestMsg m;
+    m.expert_id = expert_id;
+    m.batch_size = batch;
+    m.hidden_dim = hidden;
+    m.input_dtype = static_cast<common::ActivationDType>(in_dtype);
+    m.output_dtype = static_cast<common::ActivationDType>(out_dtype);
+    m.activation.assign(reinterpret_cast<const char*>(act), static_cast<std::size_t>(n));
+    const std::string body = common::EncodeInferRequestBody(m);
+    if (static_cast<long long>(body.size()) > cap) return -1;
+    std::memcpy(out, body.data(), body.size());
+    return static_cast<long long>(body.size());
+}
+
+// DecodeInferRequestBody: 1 and the fields (expert, batch, hidden, in dtype, out dtype) and
+// payload, or 0 when the reference rejects the body.
+int ref_decode_infer_request(const std::uint8_t* body, long long len, long long* fields,
+                             std::uint8_t* payload, long long cap, long long* n) {
+    common::InferRequestMsg m;
+    if (!common::DecodeInferRequestBody(std::string(reinterpret_cast<const char*>(body), len), &m)) return 0;
+    fields[0] = m.expert_id;
+    fields[1] = m.batch_size;
+    fields[2] = m.hidden_dim;
+    fields[3] = static_cast<long long>(m.input_dtype);
+    fields[4] = static_cast<long long>(m.output_dtype);
+    *n = static_cast<long long>(m.activation.size());
+    if (*n > cap) return 0;
+    std::memcpy(payload, m.activation.data(), m.activation.size());
+    return 1;
+}
+
+long long ref_encode_infer_response(std::int32_t status, std::int32_t batch, std::int32_t hidden,
+                                    std::uint32_t out_dtype, const std::uint8_t* output, long long n,
+                                    std::uint8_t* out, long long cap) {
+    common::InferResponseMsg m;
+    m.status_code = status;
+    m.batch_size = batch;
+    m.hidden_dim = hidden;
+    m.output_dtype = static_cast<common::ActivationDType>(out_dtype);
+    m.output.assign(reinterpret_cast<const char*>(output), static_cast<std::size_t>(n));
+    const std::string body = common::EncodeInferResponseBody(m);
+    if (static_cast<long long>(body.size()) > cap) return -1;
+    std::memcpy(out, body.data(), body.size());
+    return static_cast<long long>(body.size());
+}
+
+// DecodeInferResponseBody: 1 and (status, batch, hidden, out dtype) + payload, or 0.
+int ref_decode_infer_response(const std::uint8_t* body, long long len, long long* fields,
+                              std::uint8_t* payload, long long cap, long long* n) {
+    common::InferResponseMsg m;
+    if (!common::DecodeInferResponseBody(std::string(reinterpret_cast<const char*>(body), len), &m)) return 0;
+    fields[0] = m.status_code;
+    fields[1] = m.batch_size;
+    fields[2] = m.hidden_dim;
+    fields[3] = static_cast<long long>(m.output_dtype);
+    *n = static_cast<long long>(m.output.size());
+    if (*n > cap) return 0;
+    std::memcpy(payload, m.output.data(), m.output.size());
+    return 1;
+}
 
 }  // extern "C"

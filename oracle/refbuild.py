@@ -95,6 +95,16 @@ def ref_lib() -> ctypes.CDLL:
         lib.ref_decode_bf16.argtypes = [ctypes.c_uint16]
         lib.ref_decode_fp16.restype = ctypes.c_float
         lib.ref_decode_fp16.argtypes = [ctypes.c_uint16]
+        LL, LLP, VP = ctypes.c_longlong, ctypes.POINTER(ctypes.c_longlong), ctypes.c_void_p
+        I32, U32 = ctypes.c_int32, ctypes.c_uint32
+        lib.ref_encode_infer_request.restype = LL
+        lib.ref_encode_infer_request.argtypes = [I32, I32, I32, U32, U32, VP, LL, VP, LL]
+        lib.ref_encode_infer_response.restype = LL
+        lib.ref_encode_infer_response.argtypes = [I32, I32, I32, U32, VP, LL, VP, LL]
+        for name in ("ref_decode_infer_request", "ref_decode_infer_response"):
+            fn = getattr(lib, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = [VP, LL, LLP, VP, LL, LLP]
         _ref_lib = lib
     return _ref_lib
 
@@ -207,3 +217,33 @@ def ref_expert_cpu(e: ExpertBytes, x_bits: np.ndarray, in_dtype: int, out_dtype:
         if rc != 0:
             raise RuntimeError(f"RunExpertCpuV2 kernels failed rc={rc}")
     return y
+
+
+def _buf(data: bytes):
+    return (ctypes.c_uint8 * max(1, len(data))).from_buffer_copy(data or b"\0")
+
+
+def ref_encode_infer(kind: str, fields, payload: bytes) -> bytes:
+    """The reference C++ ``Encode{InferRequest,InferResponse}Body`` (common/infer_codec.cc)."""
+    lib = ref_lib()
+    out = (ctypes.c_uint8 * (len(payload) + 64))()
+    src = _buf(payload)
+    fn = lib.ref_encode_infer_request if kind == "request" else lib.ref_encode_infer_response
+    n = fn(*[int(f) for f in fields], ctypes.addressof(src), len(payload), ctypes.addressof(out), len(out))
+    if n < 0:
+        raise RuntimeError("reference encoder: buffer too small")
+    return bytes(out[:n])
+
+
+def ref_decode_infer(kind: str, body: bytes):
+    """The reference C++ ``Decode*Body``: (fields, payload), or None when it rejects the body."""
+    lib = ref_lib()
+    src = _buf(body)
+    fields = (ctypes.c_longlong * 5)()
+    payload = (ctypes.c_uint8 * max(1, len(body)))()
+    n = ctypes.c_longlong(0)
+    fn = lib.ref_decode_infer_request if kind == "request" else lib.ref_decode_infer_response
+    if not fn(ctypes.addressof(src), len(body), fields, ctypes.addressof(payload), len(payload), ctypes.byref(n)):
+        return None
+    k = 5 if kind == "request" else 4
+    return tuple(int(f) for f in fields[:k]), bytes(payload[:n.value])

@@ -6,9 +6,10 @@ Run in a checkout that has the reference tree (``CONSTELLATION_REFERENCE_ROOT``)
 
 It imports the reference's own Python functions (``server.moe_layer_runtime.
 route_token_real``, ``combine_outputs_torch``, ``server.fp8_utils.
-dequant_fp8_weight_blockwise``) and calls the reference's C++ expert code compiled
-from its sources (``oracle/_ref/libref_expert.so``: ``RunExpertReferenceV2``,
-``FillDummyExpertBundleV2``, the activation codec and the FP8 LUT).  Inputs come
+dequant_fp8_weight_blockwise``, ``common.protocol``'s infer codec) and calls the
+reference's C++ code compiled from its sources (``oracle/_ref/libref_expert.so``:
+``RunExpertReferenceV2``, ``FillDummyExpertBundleV2``, the activation codec, the FP8
+LUT, the node's InferRequest / InferResponse codec).  Inputs come
 from seeded, version-independent streams (``oracle.detrand``), so most fixtures
 store the seed and the reference's outputs only.  The fixtures pin the CPU oracle
 (``tests/test_oracle_golden.py``) and, through it, the CUDA path.
@@ -205,6 +206,85 @@ def make_layer(torch, route_token_real, combine_outputs_torch, dequant):
     assert np.all(np.isfinite(decode_bf16(encode_bf16_rne(out))))
 
 
+INFER_REQUESTS = [
+    # expert_id, batch_size, hidden_dim, input_dtype, output_dtype, payload bytes
+    (0, 1, 7168, 2, 2, 14336),                        # one DeepSeek-V3 token, bf16 -> bf16
+    (255, 1, 256, 1, 2, 512),
+    (61 * 256 + 17, 3, 64, 2, 1, 384),                # a global id (layer 61)
+    (-1, 0, 0, 0, 0, 0),                              # empty activation
+    (2 ** 31 - 1, -5, -(2 ** 31), 0xFFFFFFFF, 7, 3),  # field extremes
+]
+INFER_RESPONSES = [
+    # status_code, batch_size, hidden_dim, output_dtype, payload bytes
+    (0, 1, 7168, 2, 14336),
+    (1, 1, 7168, 2, 0),
+    (2, 4, 256, 1, 0),
+    (4, 0, 0, 0, 0),
+    (-3, 2 ** 31 - 1, -1, 0xFFFFFFFF, 5),
+]
+
+
+def _concat(chunks):
+    off = np.zeros(len(chunks) + 1, np.int64)
+    off[1:] = np.cumsum([len(c) for c in chunks])
+    return np.frombuffer(b"".join(chunks), np.uint8).copy(), off
+
+
+def _malformed(body: bytes, fixed: int):
+    """Bodies both reference decoders reject: cut inside each part, a trailing byte, and a
+    payload length that overruns or underruns the body."""
+    bad = [body[:n] for n in (0, 3, 4, fixed - 1, fixed, len(body) - 1)] + [body + b"\x00"]
+    n = int.from_bytes(body[fixed - 4:fixed], "little")
+    for m in (0xFFFFFFFF, n + 1, n - 1):
+        bad.append(body[:fixed - 4] + int(m).to_bytes(4, "little") + body[fixed:])
+    return bad
+
+
+def make_infer_codec():
+    """InferRequest / InferResponse bodies from the reference's C++ codec (compiled into
+    libref_expert.so) and its Python codec (common/protocol.py), which must agree.  Each
+    body's payload is its tail after the fixed fields."""
+    root = refbuild.reference_root()
+    sys.path.insert(0, str(root))
+    from common import protocol as P  # the reference coordinator's codec
+
+    rng = np.random.default_rng(20240611)
+    out = {}
+    for kind, cases_, fixed in (("req", INFER_REQUESTS, 24), ("resp", INFER_RESPONSES, 20)):
+        long_kind = "request" if kind == "req" else "response"
+        enc = P.encode_infer_request if kind == "req" else P.encode_infer_response
+        dec = P.decode_infer_request if kind == "req" else P.decode_infer_response
+        keys = (("expert_id", "batch_size", "hidden_dim", "input_dtype", "output_dtype") if kind == "req" else
+                ("status_code", "batch_size", "hidden_dim", "output_dtype"))
+        pkey = "activation" if kind == "req" else "output"
+        fields, payloads, bodies = [], [], []
+        for c in cases_:
+            f, n = c[:-1], c[-1]
+            payload = rng.integers(0, 256, n, dtype=np.uint8).tobytes()
+            body_cpp = refbuild.ref_encode_infer(long_kind, f, payload)
+            body_py = enc({**dict(zip(keys, f)), pkey: payload})
+            assert body_cpp == body_py, (kind, f)
+            d = dec(body_py)
+            assert tuple(d[k] for k in keys) == tuple(f) and d[pkey] == payload
+            assert refbuild.ref_decode_infer(long_kind, body_cpp) == (tuple(f), payload)
+            fields.append(f)
+            payloads.append(payload)
+            bodies.append(body_cpp)
+        bad = _malformed(next(b for b, q in zip(bodies, payloads) if 0 < len(q) <= 1024), fixed)
+        for b in bad:
+            assert refbuild.ref_decode_infer(long_kind, b) is None
+            try:
+                dec(b)
+            except P.ProtocolError:
+                pass
+            else:
+                raise AssertionError(f"reference Python decoder accepted a malformed {long_kind}")
+        out[f"{kind}_fields"] = np.array(fields, np.int64)
+        out[f"{kind}_body"], out[f"{kind}_body_off"] = _concat(bodies)
+        out[f"bad_{kind}"], out[f"bad_{kind}_off"] = _concat(bad)
+    np.savez_compressed(OUT / "infer_codec_golden.npz", **out)
+
+
 def main():
     refbuild.build()
     torch, route, combine, dequant = _ref_modules()
@@ -214,6 +294,7 @@ def main():
     make_router(torch, route)
     make_expert()
     make_layer(torch, route, combine, dequant)
+    make_infer_codec()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
