@@ -64,7 +64,7 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, compute, *, rank: int, world: int, n_routed_experts: int, group=None,
-                 mode: str = "allgather", local_route_min: int = 128):
+                 mode: str = "allgather", local_route_min: int = 128, p2p_tl_cap: int | None = None):
         if n_routed_experts % world:
             raise ValueError(f"{n_routed_experts} experts do not shard over {world} ranks")
         if mode not in ("allgather", "alltoall", "p2p"):
@@ -75,6 +75,9 @@ class ExpertParallelMoE:
         self.epr = n_routed_experts // world
         self._slot_map = None
         self._peers = None  # p2p mode: PeerExchange, created on the first forward
+        #: p2p mode: tokens per rank the exchange buffers hold (default: the first forward's);
+        #: a later forward with more tokens per rank raises
+        self.p2p_tl_cap = None if p2p_tl_cap is None else int(p2p_tl_cap)
         #: all-gather mode: from this many tokens per rank on, each rank routes only its own
         #: tokens and the routes are gathered with the activations (a 2K-int row per token);
         #: below it every rank routes the whole gathered batch and no routes move
@@ -167,10 +170,11 @@ class ExpertParallelMoE:
         if Tl == 0:  # equal on every rank (the all-gather takes equal shares): nothing to exchange
             return torch.empty((0, H), dtype=od, device=x_local.device)
         if self._peers is None:
-            self._peers = PeerExchange(x_local.device, world=self.world, rank=self.rank, tl_cap=max(Tl, 1),
-                                       hidden=H, group=self.group)
+            self._peers = PeerExchange(x_local.device, world=self.world, rank=self.rank,
+                                       tl_cap=max(Tl, self.p2p_tl_cap or 1), hidden=H, group=self.group)
         if Tl > self._peers.tl_cap:
-            raise RuntimeError(f"p2p exchange was sized for {self._peers.tl_cap} tokens per rank, got {Tl}")
+            raise RuntimeError(f"p2p exchange was sized for {self._peers.tl_cap} tokens per rank, got {Tl}; "
+                               "pass p2p_tl_cap= to size it for the largest batch")
         x_all = torch.empty((self.world * Tl, H), dtype=x_local.dtype, device=x_local.device)
         dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
         self._mark("all_gather")
