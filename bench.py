@@ -581,8 +581,7 @@ def run_config3(args):
         del graph
     if world > 1:
         dist.barrier()
-        for m in stack.moe:
-            m.close()
+        stack.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

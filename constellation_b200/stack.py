@@ -35,14 +35,14 @@ class StackLayer:
 
 class MoEStack:
     def __init__(self, layers: list[StackLayer], *, rank: int = 0, world: int = 1, n_routed_experts: int = 256,
-                 group=None, mode: str = "allgather", eps: float = 1e-6, norm=None):
+                 group=None, mode: str = "allgather", eps: float = 1e-6, norm=None, p2p_tl_cap: int | None = None):
         if not layers:
             raise ValueError("MoEStack needs at least one layer")
         self.layers = layers
         self.eps = float(eps)
         self.norm = norm or rms_norm
         self.moe = [ExpertParallelMoE(l.compute, rank=rank, world=world, n_routed_experts=n_routed_experts,
-                                      group=group, mode=mode) for l in layers]
+                                      group=group, mode=mode, p2p_tl_cap=p2p_tl_cap) for l in layers]
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
         """``h [T_local, H]`` (this rank's tokens) -> the hidden state after every layer, same dtype."""
@@ -50,3 +50,9 @@ class MoEStack:
             xn = self.norm(h, layer.norm_weight, self.eps)
             h = moe.forward(xn, layer.gate_weight, layer.bias, residual=h, out_dtype=h.dtype)
         return h
+
+    def close(self) -> None:
+        """Release every layer's peer-exchange buffers (p2p mode; every rank, after its last
+        forward, behind a barrier)."""
+        for moe in self.moe:
+            moe.close()
