@@ -148,6 +148,56 @@ def test_ep_two_ranks_matches_single_process_oracle(mode):
     np.testing.assert_allclose(out, ref.out_f32, rtol=1e-5, atol=1e-5 * np.abs(ref.out_f32).max())
 
 
+def _uneven_worker(rank, world, port, counts, q):
+    """All-to-all mode with a different token count on each rank (0 allowed): the counts
+    exchange sizes every message, so no rank needs the others' batch size."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import cases
+
+        T = sum(counts)
+        x = torch.from_numpy(cases.activations(62, T, H))
+        gw, gb = (torch.from_numpy(a) for a in cases.router(62, E, H, bias_std=0.05))
+        experts = {e: cases.expert(2100 + e, H, I) for e in range(E)}
+        epr = E // world
+        comp = OracleCompute(rank * epr, (rank + 1) * epr, experts, cases.expert(2199, H, I))
+        moe = ExpertParallelMoE(comp, rank=rank, world=world, n_routed_experts=E, mode="alltoall")
+        lo = sum(counts[:rank])
+        out = moe.forward(x[lo:lo + counts[rank]].to(torch.bfloat16), gw, gb, out_dtype=torch.float32)
+        q.put((rank, out.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("counts", [(5, 0), (1, 4)])
+def test_ep_alltoall_uneven_token_counts(counts):
+    from oracle import cases
+    from oracle.expert import DequantExpert
+    from oracle.layer import moe_layer
+
+    world = len(counts)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_uneven_worker, args=(r, world, port, counts, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert got[r].shape == (counts[r], H)
+    out = np.concatenate([got[r] for r in range(world)])
+    T = sum(counts)
+    x = cases.activations(62, T, H)
+    gw, gb = cases.router(62, E, H, bias_std=0.05)
+    ref = moe_layer(x, gw, gb, {e: DequantExpert(cases.expert(2100 + e, H, I)) for e in range(E)},
+                    DequantExpert(cases.expert(2199, H, I)), n_group=G, topk_group=TG, top_k=K)
+    np.testing.assert_allclose(out, ref.out_f32, rtol=1e-5, atol=1e-5 * np.abs(ref.out_f32).max())
+
+
 def test_plan_dispatch_orders_by_owner_and_inverts():
     idx = torch.tensor([[5, 0, 12], [3, 9, 15], [8, 1, 4]])
     p = plan_dispatch(idx, experts_per_rank=4, world=4)
