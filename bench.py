@@ -95,6 +95,40 @@ def fp8_peak_tflops():
     return 4500.0, "nominal fp8 dense"
 
 
+def step_distribution(torch, run, k: int, dev, world: int = 1):
+    """Per-step device times of ``k`` further steps -- CUDA events between consecutive steps
+    on the launching stream, max over ranks per step -- as mean / p50 / p90 / p99 / max in
+    ms (outside the timed region of the result line).  None if the events failed."""
+    ms = [float("nan")] * k
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    try:
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(k + 1)]
+        torch.cuda.synchronize(dev)
+        ev[0].record()
+        for i in range(k):
+            run()
+            ev[i + 1].record()
+        torch.cuda.synchronize(dev)
+        ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(k)]
+    except Exception:  # the distribution is informative only; every rank still joins the reduction
+        pass
+    t = torch.tensor(ms, device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    vals = sorted(float(v) for v in t.tolist())
+    if not vals or any(v != v for v in vals):
+        return None
+
+    def pct(q):
+        return round(vals[min(len(vals) - 1, int(round(q / 100 * (len(vals) - 1))))], 4)
+
+    return {"n": k, "mean": round(sum(vals) / len(vals), 4), "p50": pct(50), "p90": pct(90), "p99": pct(99),
+            "max": round(vals[-1], 4)}
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
 
@@ -268,6 +302,7 @@ def run_ours(args):
     for _ in range(3):
         e2e_step()
     ms_e2e = timed(e2e_step, args.steps) / args.steps
+    step_ms = step_distribution(torch, run, args.steps, dev, world)
     h2d = x_host.numel() * x_host.element_size() * world
     d2h = out_host.numel() * out_host.element_size() * world
 
@@ -371,6 +406,7 @@ def run_ours(args):
                       "frac": round(layer_bytes / (ms_step / 1e3) / 1e9 / peak, 4)},
         "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
         "ep_phase_ms": ep_phase_ms,
+        "step_ms": step_ms,
         "e2e": {"value": round(T / (ms_e2e / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms_e2e, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
@@ -682,6 +718,7 @@ def run_config1(args):
     for _ in range(3):
         e2e_step()
     ms_e2e = timed(e2e_step, args.steps) / args.steps
+    step_ms = step_distribution(torch, run, args.steps, dev)
 
     ctx.profile(True)
     for _ in range(10):
@@ -723,6 +760,7 @@ def run_config1(args):
                           "frac": round(ach_pair / peak, 4)},
         "frac_of_peak": round(value / peak, 4),
         "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+        "step_ms": step_ms,
         "e2e": {"value": round(nbytes / (ms_e2e / 1e3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 4),
                 "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 4},
         # route_pack, pack x, up/gate, pack h, down, combine
@@ -886,6 +924,7 @@ def run_worker(args):
     if r["status_code"] != 0 or len(r["output"]) != batch * H * 2:
         raise RuntimeError(f"worker request failed: status {r['status_code']}")
     ms_e2e = timed(e2e_step, args.steps) / args.steps
+    step_ms = step_distribution(torch, run, args.steps, dev)
 
     ctx.profile(True)
     for _ in range(2):
@@ -920,6 +959,7 @@ def run_worker(args):
                      "ms_per_launch": round(upg_ms + dn_ms, 4), "traffic": None},
         "us_per_request": round(ms_req * 1e3, 2),
         "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+        "step_ms": step_ms,
         "e2e": {"value": round(W_EXPERTS * 1e3 / ms_e2e, 1), "unit": "requests/s",
                 "us_per_request": round(ms_e2e * 1e3 / W_EXPERTS, 2),
                 "h2d_bytes_per_step": W_EXPERTS * batch * H * 2, "d2h_bytes_per_step": W_EXPERTS * batch * H * 2,
