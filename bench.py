@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 MoE-layer hot path (decode).
+"""Benchmark of the B200 MoE-layer hot path (benchmark config 2, decode).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -419,10 +419,10 @@ def run_ours(args):
         line["dtype"] = "e4m3 weights x e4m3(2-term) activations, fp32 accumulate"
         line["config"]["workload"] = "config4_prefill_T4096_one_layer" if T == 4096 else f"config4_shape_T{T}"
         line["config"]["router_bias"] = "2.0 * log-Zipf(s=1.2) over a seeded permutation of the 256 experts"
-        line["config"]["gemm_kernels"] = "prefill (64-row groups, 2 activation terms)"
+        line["config"]["gemm_kernels"] = "prefill (128-row groups, 2 activation terms, one scale per row)"
         line["config"]["l2"] = ("no flush: 11.3 GB of expert weights (1.4 GB per GPU at N=8) and a "
                                 f"{T * H * 2 / 1e6:.0f} MB activation batch exceed the 126 MB L2")
-        line["roofline"] = {"kernel": "grouped_prefill up/gate (tcgen05 kind::f8f6f4, 64-row groups)",
+        line["roofline"] = {"kernel": "grouped_prefill up/gate (tcgen05 kind::f8f6f4, 128-row groups)",
                             "bound": "tensor", "achieved": round(tflops_upg, 1), "peak": round(fp8_peak, 1),
                             "unit": "TFLOP/s", "frac": round(tflops_upg / fp8_peak, 4), "peak_source": fp8_kind,
                             "flop_per_launch": flop_upg, "ms_per_launch": round(upg_ms, 4), "traffic": None}

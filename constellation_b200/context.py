@@ -30,7 +30,7 @@ def dtype_code(dt: torch.dtype) -> int:
 
 @dataclass
 class MoEConfig:
-    """Layer geometry + router hyper-parameters (DeepSeek-V3 defaults)."""
+    """Layer geometry + router hyper-parameters (DeepSeek-V3 defaults, the benchmark's config 0)."""
 
     hidden_size: int = 7168
     moe_intermediate_size: int = 2048
@@ -186,7 +186,7 @@ class ExpertContext:
 
     def set_gemm_mode(self, mode: str) -> None:
         """Grouped-kernel shape: "auto" (prefill kernels from 32 rows per expert on),
-        "decode" (16-row groups, 3 activation terms) or "prefill" (64-row groups, 2 terms)."""
+        "decode" (16-row groups, 3 activation terms) or "prefill" (128-row groups, 2 terms)."""
         codes = {"auto": _lib.CST_GEMM_AUTO, "decode": _lib.CST_GEMM_DECODE, "prefill": _lib.CST_GEMM_PREFILL}
         if mode not in codes:
             raise ValueError(f"gemm mode must be one of {sorted(codes)}, got {mode!r}")

@@ -220,7 +220,7 @@ int alloc_workspace(cst_ctx* c) {
     return CST_OK;
 }
 
-// Prefill-shaped kernels once a call averages >= 32 rows per expert: groups of 64 rows
+// Prefill-shaped kernels once a call averages >= 32 rows per expert: groups of 128 rows
 // spread each weight tile over more tokens and two activation terms cut the tensor work.
 constexpr int kPrefillMinRowsPerExpert = 32;
 

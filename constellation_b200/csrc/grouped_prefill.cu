@@ -10,7 +10,7 @@
 //     M = 128 x N = 8 NT (up to 128) x K = 32 -- wide enough that the tensor pipe, not the
 //     shared-memory reads of the A tile, sets the pace;
 //   * activations carry TWO E4M3 terms (v = s (q1 + q2), row-wise relative error ~1e-3 on
-//     a full-size expert, inside BASELINE's 1e-2), stacked along K: per k-step two MMAs
+//     a full-size expert, inside the 1e-2 bar), stacked along K: per k-step two MMAs
 //     (term 0, term 1) accumulate into the same TMEM columns;
 //   * one power-of-two activation scale per packed ROW (pack_act.cu, pack_rows_kernel), so
 //     each K block is promoted with the weight scale alone, acc += D * scale_inv[rb, kb],

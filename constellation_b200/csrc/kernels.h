@@ -132,7 +132,7 @@ struct FfnArgs {
 cudaError_t grouped_ffn_init_attributes();
 cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream);
 
-// grouped_prefill.cu: the same contract for groups of up to 64 rows and 2-term activations
+// grouped_prefill.cu: the same contract for groups of up to 128 rows and 2-term activations
 cudaError_t grouped_prefill_init_attributes();
 cudaError_t launch_grouped_prefill(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream);
 

@@ -8,7 +8,7 @@ between the ranks of one node.  Expert ``e`` lives on rank ``e // experts_per_ra
 ranks; the router weights and the shared expert are replicated and every rank applies the
 shared expert to its own tokens.
 
-Two exchange strategies, both deterministic and both behind ``ExpertParallelMoE.forward``:
+Three exchange strategies, all deterministic and all behind ``ExpertParallelMoE.forward``:
 
 ``allgather`` (default for decode)
     all-gather the tokens; every rank routes the whole gathered batch itself (the router is
@@ -19,7 +19,13 @@ Two exchange strategies, both deterministic and both behind ``ExpertParallelMoE.
     fixed, so nothing waits on the host.  At decode batch the bytes match the all-to-all
     (T x H in, T x H x 4 back) because top_k equals the rank count at 8 GPUs.
 
-``alltoall`` (the NCCL all-to-all-v that BASELINE names)
+``p2p``
+    the all-gather exchange with the reduce-scatter fused into the combine: every rank
+    stores each gathered token's partial sum straight into the owning rank's memory over
+    NVLink (CUDA IPC mappings, ``constellation_b200.p2p``) and the owner adds the ranks'
+    partials in rank order (``cst_moe_routed_push`` / ``cst_reduce_pushed``).
+
+``alltoall`` (the NCCL all-to-all-v of the reference's expert-parallel model)
     exchange per-rank row counts (``all_to_all_single`` of ``world`` ints, the count step of
     ``modeling_deepseek_eager.py:656``), send each routed row to the rank that owns its
     expert (``:671-674``), run the grouped FFN on the received rows, send the weighted

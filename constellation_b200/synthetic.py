@@ -1,6 +1,6 @@
 """Seeded synthetic DeepSeek-V3 MoE layers generated on the GPU (benchmark inputs).
 
-BASELINE config 0 defines the data: activations ``N(0, 1)`` RMS-normalised per row and
+The benchmark's config 0 defines the data: activations ``N(0, 1)`` RMS-normalised per row and
 cast to bf16; router weight ``N(0, 0.02)`` ``[E, H]`` fp32 and correction bias
 ``N(0, 0.01)``; expert weights ``N(0, 0.02)`` quantized per 128x128 block with
 ``s = amax / 448``, ``q = e4m3fn(W / s)`` (saturating) and ``s`` kept as ``scale_inv``

@@ -120,7 +120,7 @@ int cst_set_shared_slot(cst_ctx* ctx, int32_t slot);
 /* Kernel shape of the grouped expert products (the reference runs one batch-1 matvec per
  * (token, expert), backend/cuda/backend_cuda_v2.cc:205-255; it has no such choice).
  * CST_GEMM_AUTO (default) takes the prefill kernels once a call averages >= 32 rows per
- * expert: groups of up to 64 rows, activations in two E4M3 terms (row-wise relative error
+ * expert: groups of up to 128 rows, activations in two E4M3 terms (row-wise relative error
  * ~1e-3) instead of three (~2e-5).  The other two values force one shape. */
 #define CST_GEMM_AUTO 0
 #define CST_GEMM_DECODE 1

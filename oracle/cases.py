@@ -1,6 +1,6 @@
 """Seeded synthetic inputs in the shapes of the benchmark configurations (test infrastructure only).
 
-Follows BASELINE config 0: activations ``N(0, 1)``, RMS-normalised per row and cast
+Follows the benchmark's config 0: activations ``N(0, 1)``, RMS-normalised per row and cast
 to bf16; router weight ``N(0, 0.02)`` ``[E, H]`` fp32; correction bias ``N(0, 0.01)``;
 expert weights ``N(0, 0.02)`` quantized per 128x128 block to E4M3 with fp32
 ``scale_inv``.  All streams come from ``oracle.detrand`` so a seed pins the data.

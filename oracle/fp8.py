@@ -10,7 +10,7 @@ References restated here:
   = w.float() * scale_inv[bi, bj]`` over ``block_size`` x ``block_size`` blocks with
   ceil-div block counts (ragged last blocks allowed).  ``weight_fp8.float()`` is
   torch's true e4m3fn decode, where 0x7F / 0xFF are NaN.
-* The synthetic quantizer of the benchmark configurations: per
+* The synthetic quantizer of the benchmark configurations (config 0): per
   128x128 block ``s = amax / 448``, ``q = round_to_e4m3fn(W / s)`` saturating,
   ``s`` stored as ``scale_inv`` -- exactly what ``dequant_fp8_weight_blockwise``
   multiplies by.  The reference itself ships no quantizer (checkpoints arrive

@@ -23,7 +23,10 @@ REF_SO = OUT / "libref_expert.so"
 
 
 def reference_root() -> Path | None:
-    root = Path(os.environ.get("CONSTELLATION_REFERENCE_ROOT", "/root/reference"))
+    """The reference checkout: ``$CONSTELLATION_REFERENCE_ROOT``, else a ``reference``
+    directory beside this repository; None when neither holds the reference sources."""
+    default = HERE.parent.parent / "reference"
+    root = Path(os.environ.get("CONSTELLATION_REFERENCE_ROOT", str(default)))
     marker = root / "expert_node_v2" / "backend" / "expert_reference_v2.cc"
     return root if marker.is_file() else None
 

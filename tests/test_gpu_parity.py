@@ -5,7 +5,7 @@ Tolerances (written here, used below):
   above 1e-5 -- a closer call depends on the last ulp of the fp32 logit and is reported,
   not compared; weights within rtol 2e-6.
 * expert / layer outputs vs the fp32 dequantize-then-matmul oracle: normwise relative
-  error ``max|a - b| / max|ref|`` per token row <= 1e-2 (BASELINE's bf16 bar); the
+  error ``max|a - b| / max|ref|`` per token row <= 1e-2 (the bf16 bar of the benchmark); the
   measured errors are far below (about 3e-3 for bf16 outputs, 1e-4 for fp32).
 * the reference node's own thresholds on its dummy fixture
   (test_benchmark_run_expert_cuda_v2.cc:302-305): max_abs <= 5e-3, mean_abs <= 1e-3,
