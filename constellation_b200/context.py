@@ -44,6 +44,14 @@ class MoEConfig:
     scoring_func: str = "sigmoid"
     topk_method: str = "noaux_tc"
 
+    def __post_init__(self):
+        # the kernels implement this router only (route_token_real's own checks,
+        # server/moe_layer_runtime.py:249-252)
+        if self.scoring_func != "sigmoid":
+            raise RuntimeError(f"unsupported scoring_func={self.scoring_func}")
+        if self.topk_method != "noaux_tc":
+            raise RuntimeError(f"unsupported topk_method={self.topk_method}")
+
     @classmethod
     def from_router_config(cls, rc: dict, inter: int) -> "MoEConfig":
         return cls(hidden_size=int(rc["hidden_size"]), moe_intermediate_size=int(inter),

@@ -91,3 +91,17 @@ def test_dequant_cpu_input_needs_cuda():
 
     with pytest.raises(RuntimeError):
         dequant_fp8_weight_blockwise(torch.zeros(4, 4, dtype=torch.uint8), torch.ones(2, 2))  # bad grid
+
+
+def test_moe_config_from_the_reference_router_config():
+    """``MoEConfig.from_router_config`` reads the dict of ``DeepSeekModelLoader.router_config``
+    (server/deepseek_model_loader.py:66-81) and rejects the routers the kernels do not run."""
+    from constellation_b200.context import MoEConfig
+
+    rc = {"n_group": 8, "topk_group": 4, "top_k": 8, "norm_topk_prob": True, "routed_scaling_factor": 2.5,
+          "scoring_func": "sigmoid", "topk_method": "noaux_tc", "n_routed_experts": 256, "hidden_size": 7168}
+    assert MoEConfig.from_router_config(rc, inter=2048) == MoEConfig()
+    with pytest.raises(RuntimeError, match="scoring_func"):
+        MoEConfig.from_router_config({**rc, "scoring_func": "softmax"}, inter=2048)
+    with pytest.raises(RuntimeError, match="topk_method"):
+        MoEConfig.from_router_config({**rc, "topk_method": "greedy"}, inter=2048)
