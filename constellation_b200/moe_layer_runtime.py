@@ -410,6 +410,23 @@ def run_moe_layer(session, hidden, layer_id: int, *, return_aux: bool = False):
            "topk_idx": idx.long().cpu().numpy()[0 if one else slice(None)],
            "topk_weight": w.cpu().numpy()[0 if one else slice(None)],
            "effective_top_k": top_k}
+    if one:
+        # the rest of the reference's aux for its 1-D call (:559-575): the router's own aux,
+        # the per-route expert outputs (fp16 on the wire, as infer_one_expert returns them)
+        # and their fp32 sum before the cast; "output" stays the fused result
+        router_hidden = x2[0].float()
+        _, raux = route_token_real(router_hidden, gw, bias, n_group=int(rc["n_group"]),
+                                   topk_group=int(rc["topk_group"]), top_k=top_k,
+                                   norm_topk_prob=bool(rc["norm_topk_prob"]),
+                                   routed_scaling_factor=float(rc["routed_scaling_factor"]),
+                                   scoring_func=str(rc.get("scoring_func", "sigmoid")),
+                                   topk_method=str(rc.get("topk_method", "noaux_tc")), n_routed_experts=E,
+                                   hidden_size=H, resident_expert_ids=resident, return_aux=True)
+        combined, weighted, expert_outputs = run_topk_moe_layer(session, router_hidden, global_routes[0],
+                                                                return_aux=True)
+        aux = {"layer_id": layer_id, "router_hidden": aux["router_hidden"], **raux, **aux,
+               "weighted_outputs": weighted, "combined_pre_cast": combined.detach().float().cpu().numpy(),
+               "expert_outputs": expert_outputs}
     return {"output": out.reshape(hidden.shape), "aux": aux}
 
 

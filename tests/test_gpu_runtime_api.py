@@ -97,6 +97,12 @@ def test_run_moe_layer_single_and_batched(dev):
     assert one["output"].shape == (H,)
     assert torch.equal(one["output"], out["output"][2])
     assert one["aux"]["selected_global_expert_ids"] == [3 * E + int(e) for e in ref.route.topk_idx[2]]
+    # the reference's 1-D aux keys (server/moe_layer_runtime.py:559-575 with the router's :389-407)
+    for key in ("logits", "scores", "group_scores", "selected_group_idx", "group_mask", "topk_weight_pre_norm",
+                "weighted_outputs", "combined_pre_cast", "expert_outputs", "resident_local_expert_ids"):
+        assert key in one["aux"], key
+    assert len(one["aux"]["weighted_outputs"]) == K and len(one["aux"]["expert_outputs"]) == K
+    assert rowwise_rel(one["aux"]["combined_pre_cast"], ref.out_f32[2]) < 2e-3
 
 
 def test_run_topk_moe_layer_and_infer_one_expert(dev):
