@@ -31,6 +31,8 @@ __device__ __forceinline__ float4 load_act4(const void* p, int dtype, int64_t id
 // grid (T, ceil(H / 1024)): one float4 column group per thread, all k rows loaded
 // independently, so a token's sum costs one memory latency instead of H / 1024 of them.
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
+    chain_wait();
+    chain_release();
     const int t = blockIdx.x;
     if (t >= a.T) return;
     const int32_t* rows = a.tk_row + int64_t(t) * a.K1;
@@ -91,8 +93,7 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream) {
     if (a.T <= 0) return cudaSuccess;
     const dim3 grid(a.T, (a.H + 1023) / 1024);
-    combine_kernel<<<grid, 256, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_chained(combine_kernel, grid, dim3(256), 0, stream, a);
 }
 
 }  // namespace cst

@@ -34,6 +34,17 @@ constexpr int CST_DEV_ERR_BOUNDS = 2;
 
 constexpr uint32_t kSpinLimit = 1u << 26;
 
+// Programmatic dependent launch.  Kernels of the layer chain are launched with the
+// programmatic-stream-serialization attribute (launch_chained in kernels.h), so a kernel
+// may become resident while its predecessor on the stream still runs.  Each such kernel
+// calls chain_wait() before its first global-memory access -- it returns once every
+// prerequisite grid has completed and its writes are visible -- and then chain_release(),
+// which lets the next kernel of the chain start its own prologue.  Before chain_wait() a
+// kernel touches only shared memory, TMEM and its parameters.  Launched without the
+// attribute, both are no-ops.
+__device__ __forceinline__ void chain_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void chain_release() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -107,6 +107,8 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    chain_wait();
+    chain_release();
     const int base_items = a.meta->n_groups * a.n_mb;
     const int n_rows = a.meta->n_rows;
     const int split = choose_split(base_items, a.KB, a.max_split, n_rows, a.out_rows);
@@ -349,18 +351,17 @@ cudaError_t grouped_ffn_init_attributes() {
 // enough groups to give every SM a pair, else one block per item.
 cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream) {
     const bool few_items = a.groups_hint > 0 && int64_t(a.groups_hint) * (a.n_mb / 2) < num_sms;
-    if (upgate) {
-        grouped_ffn_tc_kernel<2, kUpGateStages, false>
-            <<<num_sms, 192, tc_smem_bytes<2, kUpGateStages>(), stream>>>(a);
-    } else if (a.n_mb % 2 == 0 && !few_items) {
+    if (upgate)
+        return launch_chained(grouped_ffn_tc_kernel<2, kUpGateStages, false>, dim3(num_sms), dim3(192),
+                              tc_smem_bytes<2, kUpGateStages>(), stream, a);
+    if (a.n_mb % 2 == 0 && !few_items) {
         FfnArgs p = a;
         p.n_mb = a.n_mb / 2;
-        grouped_ffn_tc_kernel<2, kUpGateStages, true>
-            <<<num_sms, 192, tc_smem_bytes<2, kUpGateStages>(), stream>>>(p);
-    } else {
-        grouped_ffn_tc_kernel<1, kDownStages, true><<<num_sms, 192, tc_smem_bytes<1, kDownStages>(), stream>>>(a);
+        return launch_chained(grouped_ffn_tc_kernel<2, kUpGateStages, true>, dim3(num_sms), dim3(192),
+                              tc_smem_bytes<2, kUpGateStages>(), stream, p);
     }
-    return cudaGetLastError();
+    return launch_chained(grouped_ffn_tc_kernel<1, kDownStages, true>, dim3(num_sms), dim3(192),
+                          tc_smem_bytes<1, kDownStages>(), stream, a);
 }
 
 }  // namespace cst

@@ -102,6 +102,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) grouped_prefill_kernel(Ffn
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    chain_wait();
+    chain_release();
     const int base_items = a.meta->n_groups * a.n_mb;
     const int n_rows = a.meta->n_rows;
     const int split = pf_split(base_items, a.KB, a.max_split, n_rows, a.out_rows);
@@ -317,16 +319,17 @@ cudaError_t grouped_prefill_init_attributes() {
 }
 
 cudaError_t launch_grouped_prefill(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream) {
-    if (upgate) {
-        grouped_prefill_kernel<2, false><<<num_sms, kPrefillThreads, pf_smem_bytes<2>(), stream>>>(a);
-    } else if (a.n_mb % 2 == 0) {
+    if (upgate)
+        return launch_chained(grouped_prefill_kernel<2, false>, dim3(num_sms), dim3(kPrefillThreads),
+                              pf_smem_bytes<2>(), stream, a);
+    if (a.n_mb % 2 == 0) {
         FfnArgs p = a;
         p.n_mb = a.n_mb / 2;
-        grouped_prefill_kernel<2, true><<<num_sms, kPrefillThreads, pf_smem_bytes<2>(), stream>>>(p);
-    } else {
-        grouped_prefill_kernel<1, true><<<num_sms, kPrefillThreads, pf_smem_bytes<1>(), stream>>>(a);
+        return launch_chained(grouped_prefill_kernel<2, true>, dim3(num_sms), dim3(kPrefillThreads),
+                              pf_smem_bytes<2>(), stream, p);
     }
-    return cudaGetLastError();
+    return launch_chained(grouped_prefill_kernel<1, true>, dim3(num_sms), dim3(kPrefillThreads), pf_smem_bytes<1>(),
+                          stream, a);
 }
 
 }  // namespace cst

@@ -9,6 +9,25 @@
 
 namespace cst {
 
+// Launch of a kernel of the layer chain with programmatic stream serialization: the kernel
+// may start its prologue while the previous kernel on `stream` finishes; it waits for it
+// (chain_wait in cst_common.cuh) before touching global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                           Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // capi.cu: the thread's cst_last_error() message, for entry points in other files
 void clear_last_error();
 int set_last_error(int code, const char* fmt, ...);

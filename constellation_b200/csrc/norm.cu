@@ -66,6 +66,8 @@ __device__ __forceinline__ void store8(void* base, int dtype, int64_t i, const f
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const void* x, int x_dtype, int H, const float* weight,
                                                               float eps, void* out, int out_dtype) {
     __shared__ float s_part[kNormThreads / 32];
+    chain_wait();
+    chain_release();
     const int64_t row = blockIdx.x;
     const int64_t off = row * H;
     float ss = 0.0f;
@@ -97,8 +99,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const void* x, in
 cudaError_t launch_rmsnorm(const void* x, int x_dtype, int T, int H, const float* weight, float eps, void* out,
                            int out_dtype, cudaStream_t stream) {
     if (T == 0) return cudaSuccess;
-    rmsnorm_kernel<<<T, kNormThreads, 0, stream>>>(x, x_dtype, H, weight, eps, out, out_dtype);
-    return cudaGetLastError();
+    return launch_chained(rmsnorm_kernel, dim3(T), dim3(kNormThreads), 0, stream, x, x_dtype, H, weight, eps, out,
+                          out_dtype);
 }
 
 }  // namespace cst

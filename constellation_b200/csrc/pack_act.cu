@@ -76,6 +76,8 @@ __device__ __forceinline__ void load4(const PackActArgs& a, int64_t src_row, int
 constexpr int kPackKbPerTask = 8;  // K blocks one warp packs for one row (at most)
 
 __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
+    chain_wait();
+    chain_release();
     const int KB = a.K / kBlock;
     // split partials read up to 8 loads per element: smaller tasks, more warps in flight
     const int kbpt = a.src_dtype == kSrcUpGatePartials ? 2 : kPackKbPerTask;
@@ -158,6 +160,8 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
 // |v| over all K, pass 2 writes the two terms of every K block with that row's scale.  The
 // second pass re-reads the row from L2.
 __global__ void __launch_bounds__(256) pack_rows_kernel(PackActArgs a) {
+    chain_wait();
+    chain_release();
     const int KB = a.K / kBlock;
     const int n_tiles = a.meta->n_tiles;
     const int split = a.src_dtype == kSrcUpGatePartials ? a.meta->split_k : 1;
@@ -235,6 +239,8 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackActArgs a) {
 // (max |v| over the row -> pow2_scale_for).  Lets the x packer run one pass when a token
 // appears in several packed rows.
 __global__ void __launch_bounds__(256) row_scale_kernel(PackActArgs a, int n_src_rows, float* out) {
+    chain_wait();
+    chain_release();
     const int KB = a.K / kBlock;
     const int lane = threadIdx.x & 31;
     const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -259,19 +265,16 @@ __global__ void __launch_bounds__(256) row_scale_kernel(PackActArgs a, int n_src
 cudaError_t launch_row_scale(const PackActArgs& a, int n_src_rows, float* out, int num_sms, cudaStream_t stream) {
     if (a.src_dtype == kSrcUpGatePartials) return cudaErrorInvalidValue;
     if (n_src_rows == 0) return cudaSuccess;
-    row_scale_kernel<<<num_sms * 4, 256, 0, stream>>>(a, n_src_rows, out);
-    return cudaGetLastError();
+    return launch_chained(row_scale_kernel, dim3(num_sms * 4), dim3(256), 0, stream, a, n_src_rows, out);
 }
 
 cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t stream) {
     if (a.terms != 2) return cudaErrorInvalidValue;
-    pack_rows_kernel<<<num_sms * 8, 256, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_chained(pack_rows_kernel, dim3(num_sms * 8), dim3(256), 0, stream, a);
 }
 
 cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream) {
-    pack_act_kernel<<<num_sms * 8, 256, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_chained(pack_act_kernel, dim3(num_sms * 8), dim3(256), 0, stream, a);
 }
 
 }  // namespace cst

@@ -88,6 +88,8 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a) {
     int* s_wcnt = s_slot + kRankSortMaxKeys;
     int* s_cnt = s_wcnt + kPackWarps * a.n_slots;
     int* s_first = s_cnt + a.n_slots;
+    chain_wait();
+    chain_release();
     __shared__ int s_warp[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
@@ -201,6 +203,8 @@ __global__ void __launch_bounds__(kPackThreads) route_pack_kernel(PackArgs a) {
 
 __global__ void __launch_bounds__(kPackThreads) route_count_kernel(PackArgs a) {
     extern __shared__ int s_hist[];
+    chain_wait();
+    chain_release();
     const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
     const int K1 = mode_rows ? 1 : a.K + 1;
     const int n_routes = mode_rows ? a.T : a.T * K1;
@@ -220,6 +224,8 @@ __global__ void __launch_bounds__(kPackThreads) route_count_kernel(PackArgs a) {
 __global__ void __launch_bounds__(kPackThreads) route_scan_kernel(PackArgs a, int n_chunks) {
     extern __shared__ int s_tot[];  // per slot: routes, then (reused) first row
     __shared__ int s_warp[32];
+    chain_wait();
+    chain_release();
     const int tid = threadIdx.x;
     // per slot: running count over chunks (exclusive, in place) and the slot total
     for (int s = tid; s < a.n_slots; s += kPackThreads) {
@@ -279,6 +285,8 @@ __global__ void __launch_bounds__(kPackThreads) route_scan_kernel(PackArgs a, in
 
 __global__ void __launch_bounds__(kPackThreads) route_scatter_kernel(PackArgs a) {
     __shared__ int s_slot[kPackThreads];
+    chain_wait();
+    chain_release();
     const bool mode_rows = (a.row_slot != nullptr) || (a.single_slot >= 0);
     const int K1 = mode_rows ? 1 : a.K + 1;
     const int n_routes = mode_rows ? a.T : a.T * K1;
@@ -320,14 +328,13 @@ cudaError_t launch_route_pack(const PackArgs& a, cudaStream_t stream) {
         const int chunks = route_pack_chunks(n_routes);
         if (int64_t(chunks) * a.n_slots > a.hist_cap) return cudaErrorInvalidValue;
         const size_t hs = size_t(a.n_slots) * sizeof(int);
-        route_count_kernel<<<chunks, kPackThreads, hs, stream>>>(a);
-        route_scan_kernel<<<1, kPackThreads, hs, stream>>>(a, chunks);
-        route_scatter_kernel<<<chunks, kPackThreads, 0, stream>>>(a);
-        return cudaGetLastError();
+        cudaError_t e = launch_chained(route_count_kernel, dim3(chunks), dim3(kPackThreads), hs, stream, a);
+        if (e == cudaSuccess) e = launch_chained(route_scan_kernel, dim3(1), dim3(kPackThreads), hs, stream, a, chunks);
+        if (e == cudaSuccess) e = launch_chained(route_scatter_kernel, dim3(chunks), dim3(kPackThreads), 0, stream, a);
+        return e;
     }
     const size_t smem = size_t(kRankSortMaxKeys + (kPackWarps + 2) * a.n_slots) * sizeof(int);
-    route_pack_kernel<<<1, kPackThreads, smem, stream>>>(a);
-    return cudaGetLastError();
+    return launch_chained(route_pack_kernel, dim3(1), dim3(kPackThreads), smem, stream, a);
 }
 
 }  // namespace cst

@@ -88,6 +88,8 @@ __global__ void __launch_bounds__(kLWarps * 32) router_logits_kernel(const TX* _
                                                                      float* __restrict__ logits, int T, int E,
                                                                      int H) {
     __shared__ float s_part[kLWarps][kLT * kLE];
+    chain_wait();
+    chain_release();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * kLT;
     const int e0 = blockIdx.y * kLE;
@@ -188,6 +190,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const _
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    chain_wait();
+    chain_release();
     const uint32_t lane_addr = uint32_t(warp * 32) << 16;
     const uint32_t idesc = umma_idesc_bf16(128, N);
     float acc[kRtMaxN];
@@ -343,6 +347,8 @@ template <int EPL>
 __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(RouterArgs a) {
     __shared__ float s_choice[kSelWarps][EPL * 32];
     __shared__ float s_score[kSelWarps][EPL * 32];
+    chain_wait();
+    chain_release();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * kSelWarps + warp;
     if (t >= a.T) return;
@@ -458,6 +464,8 @@ __global__ void __launch_bounds__(1024) router_select_rank_kernel(RouterArgs a) 
     __shared__ float s_gs[32];
     __shared__ int s_keep[32];
     __shared__ int s_sel[16];
+    chain_wait();
+    chain_release();
     const int t = blockIdx.x;
     const int e = threadIdx.x;
     const int E = a.E;
@@ -595,34 +603,36 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
         ks = router_tc_split(T, E, H, cap);
         const int N = router_tc_n(T);
         const dim3 grid((T + N - 1) / N, E / 128, ks);
-        router_logits_tc_kernel<<<grid, kRtThreads, 2 * kRtStage + 1024 + 64, stream>>>(
-            static_cast<const __nv_bfloat16*>(x), w, logits, T, E, H, N, H / kRtKB / ks, err);
+        const cudaError_t e = launch_chained(router_logits_tc_kernel, grid, dim3(kRtThreads),
+                                             size_t(2 * kRtStage + 1024 + 64), stream,
+                                             static_cast<const __nv_bfloat16*>(x), w, logits, T, E, H, N,
+                                             H / kRtKB / ks, err);
+        if (e != cudaSuccess) return e;
     } else {
         const dim3 grid((T + kLT - 1) / kLT, (E + kLE - 1) / kLE);
+        cudaError_t e;
         if (x_dtype == 2) {
-            router_logits_kernel<__nv_bfloat16><<<grid, kLWarps * 32, 0, stream>>>(
-                static_cast<const __nv_bfloat16*>(x), w, logits, T, E, H);
+            e = launch_chained(router_logits_kernel<__nv_bfloat16>, grid, dim3(kLWarps * 32), 0, stream,
+                               static_cast<const __nv_bfloat16*>(x), w, logits, T, E, H);
         } else if (x_dtype == 1) {
-            router_logits_kernel<__half><<<grid, kLWarps * 32, 0, stream>>>(static_cast<const __half*>(x), w, logits,
-                                                                             T, E, H);
+            e = launch_chained(router_logits_kernel<__half>, grid, dim3(kLWarps * 32), 0, stream,
+                               static_cast<const __half*>(x), w, logits, T, E, H);
         } else {
-            router_logits_kernel<float><<<grid, kLWarps * 32, 0, stream>>>(static_cast<const float*>(x), w, logits, T,
-                                                                            E, H);
+            e = launch_chained(router_logits_kernel<float>, grid, dim3(kLWarps * 32), 0, stream,
+                               static_cast<const float*>(x), w, logits, T, E, H);
         }
+        if (e != cudaSuccess) return e;
     }
     RouterArgs a{logits, ks, bias, resident, T, E, n_group, topk_group, top_k, norm, scale,
                  topk_idx, topk_w, group_scores_out};
     if (T <= 2048) {
         // decode-sized batches: one CTA per token, short dependency chains
-        router_select_rank_kernel<<<T, (E + 31) / 32 * 32, 0, stream>>>(a);
+        return launch_chained(router_select_rank_kernel, dim3(T), dim3((E + 31) / 32 * 32), 0, stream, a);
     } else {
         // large batches: one warp per token keeps the grid small
         const int grid_sel = (T + kSelWarps - 1) / kSelWarps;
-        if (E <= 256) {
-            router_select_kernel<8><<<grid_sel, kSelWarps * 32, 0, stream>>>(a);
-        } else {
-            router_select_kernel<32><<<grid_sel, kSelWarps * 32, 0, stream>>>(a);
-        }
+        if (E <= 256) return launch_chained(router_select_kernel<8>, dim3(grid_sel), dim3(kSelWarps * 32), 0, stream, a);
+        return launch_chained(router_select_kernel<32>, dim3(grid_sel), dim3(kSelWarps * 32), 0, stream, a);
     }
     return cudaGetLastError();
 }
