@@ -35,7 +35,7 @@ EXPORTED = (
     "cst_route_noalloc", "cst_moe_routed_range", "cst_set_gemm_mode", "cst_rmsnorm",
     "cst_ipc_alloc", "cst_ipc_open", "cst_ipc_close", "cst_ipc_free", "cst_moe_routed_push", "cst_reduce_pushed",
     "cst_encode_infer_request", "cst_decode_infer_request", "cst_encode_infer_response", "cst_decode_infer_response",
-    "cst_serve_infer_request",
+    "cst_serve_infer_request", "cst_gather_rows",
 )
 CST_INFER_REQUEST_FIXED_BYTES = 24
 CST_INFER_RESPONSE_FIXED_BYTES = 20
@@ -90,7 +90,8 @@ class CstIpcHandle(ctypes.Structure):
 class CstPeerSet(ctypes.Structure):
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("tl", ctypes.c_int32),
                 ("tl_cap", ctypes.c_int32), ("recv", ctypes.c_void_p * CST_MAX_PEERS),
-                ("flags", ctypes.c_void_p * CST_MAX_PEERS), ("epoch", ctypes.c_void_p), ("done", ctypes.c_void_p)]
+                ("flags", ctypes.c_void_p * CST_MAX_PEERS), ("epoch", ctypes.c_void_p), ("done", ctypes.c_void_p),
+                ("x_offset", ctypes.c_int64), ("gather_epoch", ctypes.c_void_p)]
 
 
 class CstInferRequest(ctypes.Structure):
@@ -142,6 +143,7 @@ def _load() -> ctypes.CDLL:
         "cst_ipc_free": (ctypes.c_int, [P]),
         "cst_moe_routed_push": (ctypes.c_int, [P, P, I32, P, P, I32, ctypes.POINTER(CstPeerSet), P]),
         "cst_reduce_pushed": (ctypes.c_int, [P, ctypes.POINTER(CstPeerSet), P, I32, P, I32, P]),
+        "cst_gather_rows": (ctypes.c_int, [P, ctypes.POINTER(CstPeerSet), P, I32, P]),
         "cst_encode_infer_request": (ctypes.c_int, [ctypes.POINTER(CstInferRequest), P, I64, ctypes.POINTER(I64)]),
         "cst_decode_infer_request": (ctypes.c_int, [P, I64, ctypes.POINTER(CstInferRequest)]),
         "cst_encode_infer_response": (ctypes.c_int, [ctypes.POINTER(CstInferResponse), P, I64, ctypes.POINTER(I64)]),

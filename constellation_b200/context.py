@@ -272,6 +272,16 @@ class ExpertContext:
                                                topk_weight.data_ptr(), int(topk_idx.shape[1]), ctypes.byref(peers),
                                                _stream(self.device)))
 
+    def gather_rows(self, x_local: torch.Tensor, peers) -> None:
+        """The all-gather over peer memory (``cst_gather_rows``): this rank's ``[tl, H]``
+        rows into every rank's gathered rows, then a bounded wait for all ranks' rows here."""
+        x_local = self._check_x(x_local)
+        if x_local.shape[0] != peers.tl:
+            raise RuntimeError(f"x_local has {x_local.shape[0]} rows, the exchange {peers.tl}")
+        with torch.cuda.device(self.device):
+            check(_lib.lib.cst_gather_rows(self.handle, ctypes.byref(peers), x_local.data_ptr(),
+                                           dtype_code(x_local.dtype), _stream(self.device)))
+
     def reduce_pushed(self, peers, *, residual: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
                       out: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's ``tl`` tokens: the ranks' pushed partials in rank order (+ residual),

@@ -582,6 +582,11 @@ static int peer_set_from(const cst_peer_set* p, PeerSet* out) {
     }
     q.epoch = p->epoch;
     q.done = p->done;
+    if (p->x_offset < 0 || p->x_offset % 16 || (p->x_offset > 0 && !p->gather_epoch))
+        return fail(CST_ERR_INVALID_ARG, "peer set: bad gathered-row region (offset %lld)",
+                    static_cast<long long>(p->x_offset));
+    q.x_off = p->x_offset;
+    q.gather_epoch = p->gather_epoch;
     *out = q;
     return CST_OK;
 }
@@ -909,6 +914,21 @@ int cst_moe_routed_push(cst_ctx* c, const void* x, int32_t x_dtype, const int32_
     const uint32_t flags = c->shared_slot >= 0 ? CST_FLAG_ADD_SHARED : 0u;
     return moe_routed_impl(c, x, x_dtype, T, topk_idx, topk_weight, top_k, flags, nullptr, nullptr, CST_DTYPE_FP32,
                            s, lo, lo + ps.tl, &ps);
+}
+
+int cst_gather_rows(cst_ctx* c, const cst_peer_set* peers, const void* x, int32_t x_dtype, void* stream) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    PeerSet ps{};
+    if (int rc = peer_set_from(peers, &ps)) return rc;
+    if (ps.x_off == 0) return fail(CST_ERR_INVALID_ARG, "the peer set has no gathered-row slots");
+    if (x_dtype != CST_DTYPE_FP16 && x_dtype != CST_DTYPE_BF16)
+        return fail(CST_ERR_INVALID_ARG, "gathered rows must be fp16 or bf16, got dtype %d", x_dtype);
+    if (!x || !aligned16(x)) return fail(CST_ERR_INVALID_ARG, "x must be non-null and 16-byte aligned");
+    if (int rc = ensure_device(c)) return rc;
+    GatherArgs ga{ps, x, ps.tl, c->cfg.hidden_dim, c->ws.err};
+    CST_CUDA(launch_gather_rows(ga, static_cast<cudaStream_t>(stream)));
+    return CST_OK;
 }
 
 int cst_reduce_pushed(cst_ctx* c, const cst_peer_set* peers, const void* residual, int32_t residual_dtype,

@@ -170,7 +170,20 @@ struct PeerSet {
     int32_t* flags[kMaxPeers];   // rank q's arrival counters [world]
     int32_t* epoch;              // this rank's exchange counter
     int32_t* done;               // reserved
+    int64_t x_off;               // byte offset of the gathered-row slots from recv[q] (0: none)
+    int32_t* gather_epoch;       // this rank's gather counter
 };
+// Gathered-row exchange: arrival counters at flags[q] + kGatherFlags
+constexpr int kGatherFlags = 8;
+constexpr int kGatherRows = 4;  // rows per pushing CTA
+struct GatherArgs {
+    PeerSet peers;
+    const void* x;   // this rank's [tl, H] rows, 2-byte elements
+    int tl;
+    int H;
+    int* err;
+};
+cudaError_t launch_gather_rows(const GatherArgs& a, cudaStream_t stream);
 struct PushArgs {
     const float* y;         // weighted expert output rows
     int64_t ldy;

@@ -1,5 +1,13 @@
-// Peer-memory exchange for expert parallelism: the combine of the routed (and shared)
-// expert outputs fused with the cross-rank reduction, over NVLink stores.
+// Peer-memory exchange for expert parallelism: the all-gather of the tokens' rows and the
+// combine of the routed (and shared) expert outputs fused with the cross-rank reduction,
+// both over NVLink stores.
+//
+//   gather_push_kernel + gather_wait_kernel: every rank stores its own rows into every
+//     rank's gathered-row slots and counts them there; the owner waits (bounded) for all
+//     ranks' rows before the router reads them.  A rank's slots are rewritten by the next
+//     exchange only after every rank has pushed the combine of this one, which each rank
+//     does after its last read of the gathered rows (the activation packer), so one slot
+//     set per rank suffices here too.
 //
 // The reference reduces nothing across GPUs -- its coordinator gathers one expert result
 // per (token, expert) socket request and sums them on the host (server/moe_layer_runtime.py
@@ -21,10 +29,10 @@
 // advances by the same amount per exchange, so CUDA graphs replay it unchanged.  Counters
 // and epoch are 32-bit words that wrap (a long-lived server passes 2^31 pushing CTAs within
 // days), so "arrived" is the sign of the wrapped difference, never a plain comparison; a
-// counter trails its target by at most the CTAs of one exchange, far below 2^31.  A slot is
-// rewritten only by the next exchange, which in the expert-parallel layer comes after the
-// next all-gather -- a collective every rank enters only after finishing its own reduce of
-// this exchange -- so one buffer per rank suffices.
+// counter trails its target by at most the CTAs of one exchange, far below 2^31.  A receive
+// slot is rewritten only by the next exchange's push, which a rank issues after that
+// exchange's gather -- and every rank starts its gather only after finishing its own reduce
+// of this exchange -- so one buffer per rank suffices.
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -93,6 +101,48 @@ __global__ void __launch_bounds__(256) combine_push_kernel(PushArgs a) {
             uint32_t* epoch = reinterpret_cast<uint32_t*>(a.peers.epoch);
             *epoch += gridDim.y * uint32_t((a.tl + kPushTok - 1) / kPushTok);
         }
+    }
+}
+
+// The all-gather half.  grid (world x row blocks): CTA (q, b) copies this rank's rows
+// [b kGatherRows, b kGatherRows + kGatherRows) into rank q's gathered-row slots (row
+// rank * tl + i) with 16-byte stores, then one release-ordered add on q's gather counter
+// for this rank.  CTA (0, 0) advances this rank's gather epoch by the blocks per owner.
+__global__ void __launch_bounds__(256) gather_push_kernel(GatherArgs a) {
+    const int nblk = (a.tl + kGatherRows - 1) / kGatherRows;
+    const int q = blockIdx.x / nblk;
+    const int r0 = (blockIdx.x - q * nblk) * kGatherRows;
+    const int rows = min(a.tl, r0 + kGatherRows) - r0;
+    const int64_t row16 = int64_t(a.H) * 2 / 16;  // 16-byte units per row
+    const uint4* src = reinterpret_cast<const uint4*>(a.x) + int64_t(r0) * row16;
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.peers.recv[q]) + a.peers.x_off) +
+                 (int64_t(a.peers.rank) * a.tl + r0) * row16;
+    for (int64_t i = threadIdx.x; i < rows * row16; i += blockDim.x) dst[i] = __ldg(src + i);  // local or peer store
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        red_release_sys_add(a.peers.flags[q] + kGatherFlags + a.peers.rank, 1u);
+        if (blockIdx.x == 0) {
+            uint32_t* epoch = reinterpret_cast<uint32_t*>(a.peers.gather_epoch);
+            *epoch += uint32_t(nblk);
+        }
+    }
+}
+
+// One warp: lane r waits (bounded, like reduce_cast_kernel) until rank r's gather counter
+// here covers every block of this exchange; a wait that gives up sets the error word.  The
+// kernels after it on the stream read the gathered rows.
+__global__ void __launch_bounds__(32) gather_wait_kernel(GatherArgs a) {
+    const int r = threadIdx.x;
+    if (r >= a.peers.world) return;
+    const uint32_t target = *reinterpret_cast<const uint32_t*>(a.peers.gather_epoch);
+    const int32_t* flag = a.peers.flags[a.peers.rank] + kGatherFlags + r;
+    uint32_t n = 0;
+    while (before(ld_acquire_sys(flag), target)) {
+        if (++n >= (1u << 22)) {
+            if (a.err) atomicMax(a.err, CST_DEV_ERR_TIMEOUT);
+            return;
+        }
+        __nanosleep(100);
     }
 }
 
@@ -183,6 +233,14 @@ cudaError_t launch_combine_push(const PushArgs& a, cudaStream_t stream) {
     if (a.T == 0) return cudaSuccess;
     const dim3 grid(a.peers.world * ((a.tl + kPushTok - 1) / kPushTok), push_chunks(a.H));
     combine_push_kernel<<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const GatherArgs& a, cudaStream_t stream) {
+    if (a.tl == 0) return cudaSuccess;
+    const int nblk = (a.tl + kGatherRows - 1) / kGatherRows;
+    gather_push_kernel<<<a.peers.world * nblk, 256, 0, stream>>>(a);
+    gather_wait_kernel<<<1, 32, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

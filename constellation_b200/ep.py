@@ -165,11 +165,12 @@ class ExpertParallelMoE:
         return out
 
     def _p2p(self, x_local, gate_weight, bias, resident, residual, od) -> torch.Tensor:
-        """All-gather exchange with the reduce-scatter fused into the combine: every rank
-        stores each gathered token's partial sum into the owning rank's memory over NVLink
-        and the owner adds the ranks' partials (``cst_moe_routed_push`` /
-        ``cst_reduce_pushed``).  The all-gather at the start of each layer call orders one
-        call's reads of the receive slots before the next call's writes."""
+        """All-gather exchange over peer memory: every rank stores its rows into every rank's
+        gathered rows (``cst_gather_rows``; NCCL all-gather for fp32 rows), and each gathered
+        token's partial sum into the owning rank's memory, where the owner adds the ranks'
+        partials (``cst_moe_routed_push`` / ``cst_reduce_pushed``).  A rank pushes the next
+        call's rows only after its reduce of this call, which waited for every rank's push
+        of this call's partials, so no slot is rewritten while its owner still reads it."""
         from .p2p import PeerExchange
 
         Tl, H = x_local.shape
@@ -181,12 +182,18 @@ class ExpertParallelMoE:
         if Tl > self._peers.tl_cap:
             raise RuntimeError(f"p2p exchange was sized for {self._peers.tl_cap} tokens per rank, got {Tl}; "
                                "pass p2p_tl_cap= to size it for the largest batch")
-        x_all = torch.empty((self.world * Tl, H), dtype=x_local.dtype, device=x_local.device)
-        dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
+        ps = self._peers.peer_set(Tl)
+        if x_local.dtype in (torch.bfloat16, torch.float16):
+            # the all-gather over peer memory: each rank stores its rows into every rank's
+            # gathered rows and waits for the others' (cst_gather_rows)
+            self.c.gather_rows(x_local.contiguous(), ps)
+            x_all = self._peers.gathered(Tl, x_local.dtype)
+        else:
+            x_all = torch.empty((self.world * Tl, H), dtype=x_local.dtype, device=x_local.device)
+            dist.all_gather_into_tensor(x_all, x_local.contiguous(), group=self.group)
         self._mark("all_gather")
         idx_all, w_all = self.c.route(x_all, gate_weight, bias, resident=resident)
         self._mark("route")
-        ps = self._peers.peer_set(Tl)
         self.c.moe_routed_push(x_all, idx_all, w_all, ps)
         self._mark("experts_push")
         out = self.c.reduce_pushed(ps, residual=residual, out_dtype=od)

@@ -1,13 +1,20 @@
 """Peer-memory exchange buffers for expert parallelism (one process per GPU on one node).
 
-Each rank allocates one device buffer through ``cst_ipc_alloc`` -- ``world * tl_cap``
-receive slots of ``hidden`` fp32 (slot r holds what rank r pushed for this rank's tokens)
-followed by 64 int32 (arrival flags at [0, world), the exchange epoch at [32], a CTA
-counter at [33]) -- and the ranks swap the CUDA IPC handles with one all-gather, so every
-rank maps every other rank's buffer.  ``cst_moe_routed_push`` then stores each gathered
-token's partial sum straight into its owner's slot over NVLink and ``cst_reduce_pushed``
-adds the slots in rank order on the owner: the reduce-scatter of the all-gather exchange,
-fused into the combine (``constellation_b200.ep``, mode ``"p2p"``).
+Each rank allocates one device buffer through ``cst_ipc_alloc``:
+
+* ``world * tl_cap`` receive slots of ``hidden`` fp32 (slot r holds what rank r pushed for
+  this rank's tokens);
+* ``world * tl_cap`` gathered rows of ``hidden`` 2-byte elements (the all-gather of the
+  tokens, rank-major);
+* 64 int32: combine arrival counters at [0, world), gather arrival counters at [8, 8 +
+  world), the combine epoch at [32], a reserved word at [33], the gather epoch at [34].
+
+The ranks swap the CUDA IPC handles with one all-gather, so every rank maps every other
+rank's buffer.  ``cst_gather_rows`` stores each rank's rows into every rank's gathered
+rows; ``cst_moe_routed_push`` stores each gathered token's partial sum straight into its
+owner's slot over NVLink and ``cst_reduce_pushed`` adds the slots in rank order on the
+owner.  Both halves of the all-gather exchange thus run over peer memory
+(``constellation_b200.ep``, mode ``"p2p"``).
 """
 from __future__ import annotations
 
@@ -16,10 +23,10 @@ import ctypes
 import torch
 import torch.distributed as dist
 
-from . import _lib
+from . import _dlpack, _lib
 from ._lib import CST_MAX_PEERS, CstIpcHandle, CstPeerSet, check
 
-_TAIL_INTS = 64  # flags [0, world), epoch at [32], counter at [33]
+_TAIL_INTS = 64  # combine flags [0, world), gather flags [8, 8 + world), epochs at [32] and [34]
 
 
 class PeerExchange:
@@ -33,7 +40,10 @@ class PeerExchange:
         self.device = torch.device(device)
         self.world, self.rank, self.tl_cap, self.hidden = int(world), int(rank), int(tl_cap), int(hidden)
         self.slot_bytes = self.world * self.tl_cap * self.hidden * 4
-        nbytes = self.slot_bytes + _TAIL_INTS * 4
+        self.x_off = self.slot_bytes
+        self.x_bytes = self.world * self.tl_cap * self.hidden * 2
+        self.tail_off = self.x_off + self.x_bytes
+        nbytes = self.tail_off + _TAIL_INTS * 4
         own = ctypes.c_void_p()
         handle = CstIpcHandle()
         with torch.cuda.device(self.device):
@@ -69,11 +79,20 @@ class PeerExchange:
         ps.world, ps.rank, ps.tl, ps.tl_cap = self.world, self.rank, int(tl), self.tl_cap
         for q, b in enumerate(self.bases):
             ps.recv[q] = b
-            ps.flags[q] = b + self.slot_bytes
-        tail = self._own + self.slot_bytes
+            ps.flags[q] = b + self.tail_off
+        tail = self._own + self.tail_off
         ps.epoch = tail + 32 * 4
         ps.done = tail + 33 * 4
+        ps.x_offset = self.x_off
+        ps.gather_epoch = tail + 34 * 4
         return ps
+
+    def gathered(self, tl: int, dtype: torch.dtype) -> torch.Tensor:
+        """This rank's gathered rows ``[world * tl, hidden]`` (a view of the exchange buffer,
+        valid until ``close()``), filled by ``ExpertContext.gather_rows``."""
+        if dtype not in (torch.bfloat16, torch.float16):
+            raise TypeError(f"gathered rows are 2-byte, got {dtype}")
+        return _dlpack.view(self._own + self.x_off, (self.world * int(tl), self.hidden), dtype, self.device)
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (after every rank stopped using them)."""

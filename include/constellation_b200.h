@@ -264,7 +264,19 @@ typedef struct {
     int32_t* flags[CST_MAX_PEERS];
     int32_t* epoch;  /* this rank's exchange counter */
     int32_t* done;   /* reserved (a zeroed int32 of this rank) */
+    int64_t x_offset;       /* byte offset from recv[q] of rank q's gathered-row slots
+                             * [world * tl_cap, hidden] 2-byte rows; 0: none (cst_gather_rows) */
+    int32_t* gather_epoch;  /* this rank's gather counter (zeroed int32); gather arrival counters
+                             * are flags[q][8 + r] */
 } cst_peer_set;
+
+/* The all-gather of the expert-parallel exchange over peer memory: this rank's tl rows of x
+ * ([tl, hidden], fp16 or bf16) are stored into every rank's gathered-row slots (rows
+ * rank * tl ..), each block of rows followed by a release-ordered add on that rank's gather
+ * counter for this rank; then the stream waits (bounded, about 1 s; the device error word on
+ * timeout) until every rank's rows of this exchange have arrived here.  Afterwards this
+ * rank's slots hold all world * tl rows, rank-major: the x of cst_moe_routed_push. */
+int cst_gather_rows(cst_ctx* ctx, const cst_peer_set* peers, const void* x, int32_t x_dtype, void* stream);
 
 /* The routed experts resident here on all world * tl gathered tokens, the shared expert on
  * this rank's own tokens, and the combine pushed to the owners: token t's partial sum

@@ -24,7 +24,9 @@ pytestmark = pytest.mark.gpu
 E, H, I, G, TG, K = 16, 256, 128, 4, 2, 4
 T = 24  # one column chunk of 1024 and 6 pushing CTAs of 4 tokens per exchange
 CTAS = 6
-FLAGS, EPOCH = T * H, T * H + 32  # int32 offsets of the counters in the exchange buffer
+X_INTS = T * H // 2  # the gathered rows: T x H 2-byte elements
+TAIL = T * H + X_INTS  # int32 offset of the counters in the exchange buffer
+FLAGS, EPOCH, GFLAGS, GEPOCH = TAIL, TAIL + 32, TAIL + 8, TAIL + 34
 
 
 def s32(u: int) -> int:
@@ -72,6 +74,8 @@ def peer_set(buf: torch.Tensor):
     ps.flags[0] = base + FLAGS * 4
     ps.epoch = base + EPOCH * 4
     ps.done = base + (EPOCH + 1) * 4
+    ps.x_offset = T * H * 4
+    ps.gather_epoch = base + GEPOCH * 4
     return ps
 
 
@@ -83,7 +87,7 @@ def exchange(ctx, xt, wt, bt, rt, ps):
 
 def test_push_reduce_matches_layer_across_counter_wrap(layer, dev):
     ctx, xt, wt, bt, rt, ref, res = layer
-    buf = torch.zeros(T * H + 64, dtype=torch.int32, device=dev)
+    buf = torch.zeros(TAIL + 64, dtype=torch.int32, device=dev)
     start = (1 << 31) - 2 * CTAS - 3  # the third exchange carries both words past 2^31
     buf[FLAGS] = s32(start)
     buf[EPOCH] = s32(start)
@@ -109,7 +113,7 @@ def test_reduce_wait_gives_up_when_a_target_is_never_reached(layer, dev):
     from constellation_b200._lib import CstError
 
     ctx, xt, wt, bt, rt, ref, res = layer
-    buf = torch.zeros(T * H + 64, dtype=torch.int32, device=dev)
+    buf = torch.zeros(TAIL + 64, dtype=torch.int32, device=dev)
     buf[FLAGS] = s32((1 << 31) - 4 * CTAS)
     buf[EPOCH] = s32((1 << 31) - 2)  # after the push: counter 2^31 - 3 CTAS, target 2^31 + 4
     ps = peer_set(buf)
@@ -126,8 +130,37 @@ def test_reduce_wait_gives_up_when_a_target_is_never_reached(layer, dev):
     assert torch.equal(out, rt)  # only the residual
     assert waited < 30.0
     # the error word was cleared and the context still runs a full exchange
-    buf2 = torch.zeros(T * H + 64, dtype=torch.int32, device=dev)
+    buf2 = torch.zeros(TAIL + 64, dtype=torch.int32, device=dev)
     good = exchange(ctx, xt, wt, bt, rt, peer_set(buf2))
     ctx.device_error()
     fused = ctx.moe_layer(xt, wt, bt, out_dtype=torch.float32) + rt
     torch.testing.assert_close(good, fused, rtol=1e-5, atol=1e-5)
+
+
+def test_gather_rows_across_counter_wrap_and_timeout(layer, dev):
+    """cst_gather_rows on one rank: the rows land in the gathered slots (the layer over them
+    equals the layer over x), across the 32-bit wrap of its counters; a gather target that is
+    never reached gives up, sets the error word and leaves the context usable."""
+    from constellation_b200._lib import CstError
+
+    ctx, xt, wt, bt, rt, ref, res = layer
+    buf = torch.zeros(TAIL + 64, dtype=torch.int32, device=dev)
+    start = (1 << 31) - 9  # 6 row blocks per exchange: the second one wraps
+    buf[GFLAGS] = s32(start)
+    buf[GEPOCH] = s32(start)
+    ps = peer_set(buf)
+    gathered = buf[T * H:TAIL].view(torch.bfloat16).view(T, H)
+    for i in range(3):
+        ctx.gather_rows(xt, ps)
+        ctx.device_error()
+        assert torch.equal(gathered, xt), i
+    assert int(buf[GFLAGS]) == s32(start + 3 * 6) and int(buf[GEPOCH]) == s32(start + 3 * 6)
+    out = exchange(ctx, gathered, wt, bt, rt, ps)
+    fused = ctx.moe_layer(xt, wt, bt, out_dtype=torch.float32) + rt
+    torch.testing.assert_close(out, fused, rtol=1e-5, atol=1e-5)
+    # a target ahead of what arrives: the wait gives up
+    buf[GEPOCH] = s32(int(buf[GEPOCH]) + 100)
+    ctx.gather_rows(xt, ps)
+    with pytest.raises(CstError):
+        ctx.device_error()
+    ctx.device_error()  # cleared
