@@ -38,6 +38,15 @@ from pathlib import Path
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
+# Host thread pools, fixed before numpy or torch load: numpy's BLAS and torch's intra-op pool
+# run one thread each, and only the reference's OpenMP expert kernels take the host cores
+# (their thread count is an argument, ``host_cores()``).  Idle pools left spinning beside
+# those kernels slowed them several times over; torchrun sets OMP_NUM_THREADS=1 for N > 1,
+# so this also makes the CPU numbers the same at every N.
+HOST_POOL_THREADS = 1
+for _v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+    os.environ[_v] = str(HOST_POOL_THREADS)
+
 H, I, E, G, TG, K = 7168, 2048, 256, 8, 4, 8
 EXPERT_BYTES = 3 * I * H + 3 * (I // 128) * (H // 128) * 4  # 44,050,944
 ROUTER_BYTES = E * H * 4 + E * 4
@@ -59,6 +68,9 @@ def parse():
     p.add_argument("--cpu-sample-tokens", type=int, default=2)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed layer's output")
+    p.add_argument("--parity-tokens", type=int, default=4,
+                   help="tokens whose layer output the CPU oracle recomputes (routes: every token)")
     p.add_argument("--layers", type=int, default=58, help="config3: stacked layers")
     p.add_argument("--workload", choices=["config2", "config1", "config3", "config4", "worker"], default="config2",
                    help="config2: the full decode layer, T=64 (default); config1: grouped FP8 expert matvec "
@@ -69,6 +81,18 @@ def parse():
                    help="upload only the first N routed experts of each rank (small profiling case; "
                         "routes to the others contribute nothing)")
     return p.parse_args()
+
+
+def host_cores() -> int:
+    """Host cores this process may run on (the affinity mask, not the machine's count)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def host_threads_note(cores: int) -> dict:
+    return {"reference_kernels": cores, "omp_default": HOST_POOL_THREADS, "blas": HOST_POOL_THREADS}
 
 
 def measured_peaks():
@@ -129,8 +153,16 @@ def step_distribution(torch, run, k: int, dev, world: int = 1):
             "max": round(vals[-1], 4)}
 
 
+def smi_gpu_id(torch, dev) -> str:
+    """The device's PCI bus id in nvidia-smi's form.  nvidia-smi numbers GPUs in PCI order
+    and ignores CUDA_VISIBLE_DEVICES, so a CUDA ordinal can name another GPU there."""
+    p = torch.cuda.get_device_properties(dev)
+    return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+
+
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons of one GPU (``gpu``: PCI bus id), sampled every
+    200 ms while running."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -173,7 +205,67 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "samples": len(rows), "reasons": reasons}
+                "samples": len(rows), "reasons": reasons, "gpu": self.gpu}
+
+
+def rowwise_rel(a, ref) -> float:
+    import numpy as np
+
+    a = np.atleast_2d(a).astype(np.float64)
+    ref = np.atleast_2d(ref).astype(np.float64)
+    return float((np.abs(a - ref).max(axis=1) / np.maximum(np.abs(ref).max(axis=1), 1e-30)).max())
+
+
+def layer_parity(torch, moe, rank, world, dev, x_all, gw, gb, out_local, n_tokens: int):
+    """Correctness of the timed layer, checked outside the timed region at every N.
+
+    The output rows of all ranks are gathered to rank 0 (NCCL, after timing).  Rank 0
+    recomputes every token's routes with the router calls the layer made
+    (``ExpertParallelMoE.routes``) and compares them with the CPU oracle of
+    ``route_token_real`` on EVERY token; then the oracle recomputes the layer output
+    (dequantize, then fp32 matmul, fp32 combine + shared) for ``n_tokens`` tokens spread over
+    the batch -- so over the ranks -- regenerating only the experts those tokens reach from
+    their seeds.  Returns the summary for the result line (rank 0) or None."""
+    import torch.distributed as dist
+
+    T = x_all.shape[0]
+    if world > 1:
+        out_all = torch.empty((T, H), dtype=out_local.dtype, device=dev)
+        dist.all_gather_into_tensor(out_all, out_local.contiguous())
+    else:
+        out_all = out_local
+    res = None
+    if rank == 0:
+        import numpy as np
+
+        from constellation_b200 import synthetic
+        from oracle import router as orouter
+        from oracle.layer import moe_layer_tokens
+
+        t0 = time.perf_counter()
+        idx, w, logits = moe.routes(x_all, gw, gb, return_logits=True)
+        torch.cuda.synchronize(dev)
+        xh, gwh, gbh = x_all.float().cpu().numpy(), gw.cpu().numpy(), gb.cpu().numpy()
+        kw = dict(n_group=G, topk_group=TG, top_k=K, norm_topk_prob=True, routed_scaling_factor=2.5)
+        cmp = orouter.compare_routes(idx.cpu().numpy(), w.cpu().numpy(), xh, gwh, gbh,
+                                     dev_logits=logits.cpu().numpy(), **kw)
+        tokens = np.unique(np.linspace(0, T - 1, max(1, n_tokens)).round().astype(np.int64))
+
+        def bundle(e):
+            return synthetic.make_expert(H, I, seed=synthetic.expert_seed(e), device=dev).host()
+
+        _, ref = moe_layer_tokens(xh, gwh, gbh, bundle, bundle(-1), tokens, workers=min(16, host_cores()), **kw)
+        err = rowwise_rel(out_all.float().cpu().numpy()[tokens], ref)
+        res = {"routes_checked_tokens": cmp["tokens"], "index_mismatch": cmp["mismatched"],
+               "index_mismatch_unexplained": cmp["unexplained"], "near_ties": cmp["near_ties"],
+               "weight_max_rel": cmp["weight_max_rel"], "output_checked_tokens": [int(t) for t in tokens],
+               "output_max_rowwise_rel": err, "tol": 1e-2,
+               "ok": bool(cmp["unexplained"] == 0 and err <= 1e-2),
+               "oracle": "CPU restatement of route_token_real + dequantize-then-fp32-matmul experts + fp32 combine",
+               "seconds": round(time.perf_counter() - t0, 1)}
+    if world > 1:
+        dist.barrier()
+    return res
 
 
 # ---------------------------------------------------------------------------------------
@@ -186,16 +278,16 @@ def setup_layer(torch, rank, world, T_total, dev, resident=E, zipf=False):
     ctx = ExpertContext(dev, cfg, n_slots=epr + 1, max_tokens=T_total)
     for j in range(min(epr, resident)):
         e = rank * epr + j
-        ex = synthetic.make_expert(H, I, seed=1000 + e, device=dev)
+        ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(e), device=dev)
         ctx.upload_expert(j, e, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
         del ex
-    sh = synthetic.make_expert(H, I, seed=999, device=dev)
+    sh = synthetic.make_expert(H, I, seed=synthetic.expert_seed(-1), device=dev)
     ctx.upload_expert(epr, -1, sh.w_up, sh.s_up, sh.w_gate, sh.s_gate, sh.w_down, sh.s_down)
     del sh
-    gw, gb = synthetic.make_router(H, E, seed=7, device=dev)
+    gw, gb = synthetic.make_router(H, E, seed=synthetic.router_seed(), device=dev)
     if zipf:  # config 4: router bias = 2.0 * log-Zipf(1.2) over a seeded permutation
-        gb = synthetic.zipf_bias(E, seed=7, device=dev)
-    x_all = synthetic.make_activations(T_total, H, seed=11, device=dev)
+        gb = synthetic.zipf_bias(E, seed=synthetic.router_seed(), device=dev)
+    x_all = synthetic.make_activations(T_total, H, seed=synthetic.ACTIVATION_SEED, device=dev)
     Tl = T_total // world
     x = x_all[rank * Tl:(rank + 1) * Tl].contiguous()
     torch.cuda.synchronize(dev)
@@ -284,7 +376,7 @@ def run_ours(args):
         return ms
 
     run = graph.replay if graph is not None else step
-    with ClockSampler(local) as clk:
+    with ClockSampler(smi_gpu_id(torch, dev)) as clk:
         ms_total = timed(run, args.steps)
     clocks = clk.summary()
     ms_step = ms_total / args.steps
@@ -305,6 +397,12 @@ def run_ours(args):
     step_ms = step_distribution(torch, run, args.steps, dev, world)
     h2d = x_host.numel() * x_host.element_size() * world
     d2h = out_host.numel() * out_host.element_size() * world
+    parity = None
+    if not args.no_parity and args.resident_experts == E:
+        run()
+        torch.cuda.synchronize(dev)
+        parity = layer_parity(torch, moe, rank, world, dev, x_all, gw, gb, out,
+                              args.parity_tokens * (2 if prefill else 1))
 
     # per-stage device times (separate profiled pass) for the roofline
     ctx.profile(True)
@@ -411,6 +509,7 @@ def run_ours(args):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
+        "parity": parity,
     }
     if prefill:
         tflops_upg = flop_upg / (upg_ms / 1e3) / 1e12
@@ -485,22 +584,22 @@ def run_config3(args):
         ctx = ExpertContext(dev, MoEConfig(), n_slots=epr + 1, max_tokens=T)
         for j in range(epr):
             e = rank * epr + j
-            ex = synthetic.make_expert(H, I, seed=1000 * (l + 1) + e, device=dev)
+            ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(e, l), device=dev)
             ctx.upload_expert(j, e, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
             del ex
-        sh = synthetic.make_expert(H, I, seed=1000 * (l + 1) + 999, device=dev)
+        sh = synthetic.make_expert(H, I, seed=synthetic.expert_seed(-1, l), device=dev)
         ctx.upload_expert(epr, -1, sh.w_up, sh.s_up, sh.w_gate, sh.s_gate, sh.w_down, sh.s_down)
         del sh
-        gw, gb = synthetic.make_router(H, E, seed=7 + 13 * l, device=dev)
+        gw, gb = synthetic.make_router(H, E, seed=synthetic.router_seed(l), device=dev)
         g = torch.Generator(device=dev)
-        g.manual_seed(100 + l)
+        g.manual_seed(synthetic.norm_seed(l))
         nw = (1.0 + 0.02 * torch.randn((H,), generator=g, device=dev)).contiguous()
         layers.append(StackLayer(ctx, gw, gb, nw))
     torch.cuda.synchronize(dev)
     torch.cuda.empty_cache()
     stack = MoEStack(layers, rank=rank, world=world, n_routed_experts=E,
                      mode=args.ep_mode if args.ep_mode != "alltoall" else "allgather")
-    h_all = synthetic.make_activations(T, H, seed=11, device=dev)
+    h_all = synthetic.make_activations(T, H, seed=synthetic.ACTIVATION_SEED, device=dev)
     h0 = h_all[rank * Tl:(rank + 1) * Tl].contiguous()
     out = torch.empty_like(h0)
 
@@ -545,7 +644,7 @@ def run_config3(args):
             ms = float(t.item())
         return ms
 
-    with ClockSampler(local) as clk:
+    with ClockSampler(smi_gpu_id(torch, dev)) as clk:
         ms_step = timed(run, args.steps) / args.steps
     clocks = clk.summary()
     h_host = h0.cpu().pin_memory()
@@ -659,7 +758,7 @@ def run_config1(args):
     R = x_h.shape[0]
     ctx = ExpertContext(dev, MoEConfig(), n_slots=C1_EXPERTS, max_tokens=64, max_rows=max(R, 64 * (K + 1)))
     for j in range(C1_EXPERTS):
-        ex = synthetic.make_expert(H, I, seed=1000 + j, device=dev)
+        ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(j), device=dev)
         ctx.upload_expert(j, j, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
         del ex
     x = x_h.to(dev)
@@ -701,7 +800,7 @@ def run_config1(args):
         torch.cuda.synchronize(dev)
         return a.elapsed_time(b)
 
-    with ClockSampler(0) as clk:
+    with ClockSampler(smi_gpu_id(torch, dev)) as clk:
         ms_step = timed(run, args.steps) / args.steps
     clocks = clk.summary()
     nbytes = config1_bytes(R)
@@ -786,7 +885,7 @@ def cpu_config1_rate(seconds: float, sample_rows: int = 4):
     from constellation_b200 import synthetic
     from oracle import refbuild
 
-    threads = os.cpu_count() or 1
+    threads = host_cores()
     kind = "reference" if refbuild.ref_available() else "port"
     n_e, row_slot, x, _ = config1_rows(torch)
     R = x.shape[0]
@@ -797,7 +896,7 @@ def cpu_config1_rate(seconds: float, sample_rows: int = 4):
     for r in sample:
         j = int(row_slot[r])
         if j not in experts:
-            ex = synthetic.make_expert(H, I, seed=1000 + j, device="cpu")
+            ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(j), device="cpu")
             experts[j] = refbuild.ExpertBytes(ex.w_up.numpy(), ex.s_up.numpy(), ex.w_gate.numpy(),
                                               ex.s_gate.numpy(), ex.w_down.numpy(), ex.s_down.numpy())
 
@@ -822,7 +921,7 @@ def cpu_config1_rate(seconds: float, sample_rows: int = 4):
     ms_row = dt / n * 1e3
     ms_call = ms_row * R
     return {"value": round(config1_bytes(R) / (ms_call / 1e3) / 1e9, 4), "unit": "GB/s", "cores": threads,
-            "kind": kind, "sample": f"{n} batch-1 expert calls over one row each of experts 0..{len(sample) - 1} ({dt:.1f} s); "
+            "threads": host_threads_note(threads), "kind": kind, "sample": f"{n} batch-1 expert calls over one row each of experts 0..{len(sample) - 1} ({dt:.1f} s); "
                                    f"one config-1 step = {R} such calls = {ms_call:.0f} ms (extrapolated)",
             "ms_per_row": round(ms_row, 2)}
 
@@ -868,7 +967,7 @@ def run_worker(args):
     torch.cuda.set_device(dev)
     ctx = ExpertContext(dev, MoEConfig(), n_slots=W_EXPERTS, max_tokens=64, max_rows=max(batch, 64 * (K + 1)))
     for j in range(W_EXPERTS):
-        ex = synthetic.make_expert(H, I, seed=1000 + j, device=dev)
+        ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(j), device=dev)
         ctx.upload_expert(j, j, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
         del ex
     xs_h, bodies = worker_requests(torch, batch)
@@ -906,7 +1005,7 @@ def run_worker(args):
         for _ in range(3):
             graph.replay()
     run = graph.replay if graph is not None else step
-    with ClockSampler(0) as clk:
+    with ClockSampler(smi_gpu_id(torch, dev)) as clk:
         ms_step = timed(run, args.steps) / args.steps
     clocks = clk.summary()
     ms_req = ms_step / W_EXPERTS
@@ -987,12 +1086,12 @@ def cpu_worker_rate(seconds: float, batch: int = 1, sample_experts: int = 4):
     from constellation_b200 import synthetic
     from oracle import refbuild
 
-    threads = os.cpu_count() or 1
+    threads = host_cores()
     kind = "reference" if refbuild.ref_available() else "port"
     xs, _ = worker_requests(torch, batch)
     experts = []
     for j in range(sample_experts):
-        ex = synthetic.make_expert(H, I, seed=1000 + j, device="cpu")
+        ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(j), device="cpu")
         experts.append(refbuild.ExpertBytes(ex.w_up.numpy(), ex.s_up.numpy(), ex.w_gate.numpy(), ex.s_gate.numpy(),
                                             ex.w_down.numpy(), ex.s_down.numpy()))
     xb = xs.view(torch.int16).numpy().view(np.uint16)
@@ -1016,6 +1115,7 @@ def cpu_worker_rate(seconds: float, batch: int = 1, sample_experts: int = 4):
         if dt >= seconds:
             break
     return {"value": round(n / dt, 3), "unit": "requests/s", "cores": threads, "kind": kind,
+            "threads": host_threads_note(threads),
             "sample": f"{n} batch-{batch} requests to experts 0..{sample_experts - 1} ({dt:.1f} s)",
             "ms_per_request": round(dt / n * 1e3, 2)}
 
@@ -1038,11 +1138,11 @@ class CpuReferenceLayer:
         self.kind = "reference" if refbuild.ref_available() else "port"
         self.refbuild = refbuild
         torch.manual_seed(0)
-        gw, gb = synthetic.make_router(H, E, seed=7, device="cpu")
+        gw, gb = synthetic.make_router(H, E, seed=synthetic.router_seed(), device="cpu")
         if zipf:
-            gb = synthetic.zipf_bias(E, seed=7, device="cpu")
+            gb = synthetic.zipf_bias(E, seed=synthetic.router_seed(), device="cpu")
         self.gw, self.gb = gw.numpy(), gb.numpy()
-        x = synthetic.make_activations(sample_tokens, H, seed=11, device="cpu")
+        x = synthetic.make_activations(sample_tokens, H, seed=synthetic.ACTIVATION_SEED, device="cpu")
         self.x_bits = x.view(torch.int16).numpy().view(np.uint16)
         self.x = x.float().numpy()
         from oracle import router as orouter
@@ -1052,7 +1152,7 @@ class CpuReferenceLayer:
         need = sorted(set(int(e) for e in r.topk_idx.reshape(-1)))
         self.experts = {}
         for e in need + [-1]:
-            ex = synthetic.make_expert(H, I, seed=1000 + e if e >= 0 else 999, device="cpu")
+            ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(e), device="cpu")
             self.experts[e] = refbuild.ExpertBytes(ex.w_up.numpy(), ex.s_up.numpy(), ex.w_gate.numpy(),
                                                    ex.s_gate.numpy(), ex.w_down.numpy(), ex.s_down.numpy())
         self.sample_tokens = sample_tokens
@@ -1083,7 +1183,7 @@ class CpuReferenceLayer:
 
 
 def cpu_reference_rate(sample_tokens: int, seconds: float, T: int = 64, zipf: bool = False):
-    threads = os.cpu_count() or 1
+    threads = host_cores()
     layer = CpuReferenceLayer(sample_tokens, threads, zipf=zipf)
     layer.run()  # warm-up (page in the weights)
     n = 0
@@ -1096,6 +1196,7 @@ def cpu_reference_rate(sample_tokens: int, seconds: float, T: int = 64, zipf: bo
             break
     tok_s = n * sample_tokens / dt
     return {"value": round(tok_s, 3), "unit": "tokens/s", "cores": threads, "kind": layer.kind,
+            "threads": host_threads_note(threads),
             "sample": f"{sample_tokens} tokens of the T={T} batch through router + 8 routed + shared experts at "
                       f"batch 1 per (token, expert), {n} repetitions, {dt:.1f} s",
             "ms_per_token": round(dt / (n * sample_tokens) * 1e3, 2)}
@@ -1142,7 +1243,7 @@ def run_reference(args):
                                    sample=base["sample"] + f"; per step x {L} layers (extrapolated)"),
               "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return
-    threads = os.cpu_count() or 1
+    threads = host_cores()
     prefill = args.workload == "config4"
     T = args.tokens or (4096 if prefill else 64)
     layer = CpuReferenceLayer(args.cpu_sample_tokens, threads, zipf=prefill)
@@ -1174,6 +1275,7 @@ def run_reference(args):
                    "shared_expert": True, "hidden": H, "inter": I, "top_k": K, "parallelism": "cpu",
                    "sample_tokens_per_step": args.cpu_sample_tokens},
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": layer.kind,
+                         "threads": host_threads_note(threads),
                          "sample": f"{args.cpu_sample_tokens} tokens of the T={T} batch per step, batch 1 "
                                    "per (token, expert) through the reference node's OpenMP FP8 CPU kernels"},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -49,13 +49,15 @@ cudaError_t launch_dequant_fp8(const uint8_t* w, const float* s, float* out, int
 
 // router.cu
 // `logits` holds `cap` floats: scratch for the partial logits of a K split, or the caller's
-// [T, E] logits when cap == T * E (no split).  err: device error word or null.
+// [T, E] logits when cap == T * E (no split).  err: device error word (the tensor-core
+// logits kernel's bounded waits report there); with allow_tc false the logits always run
+// on the CUDA cores, whose kernel has no waits, and err may be null.
 int router_tc_split(int T, int E, int H, int64_t cap);
 int64_t router_scratch_floats(int x_dtype, int T, int E, int H);  // scratch a call of T tokens may use
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
                           int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
                           float* logits, int64_t cap, int32_t* topk_idx, float* topk_w, float* group_scores_out,
-                          int* err, cudaStream_t stream);
+                          int* err, cudaStream_t stream, bool allow_tc = true);
 
 // route_pack.cu
 struct PackArgs {

@@ -22,6 +22,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <algorithm>
+#include <cudaTypedefs.h>
 #include <mutex>
 
 #include "cst_common.cuh"
@@ -583,9 +584,9 @@ int64_t router_scratch_floats(int x_dtype, int T, int E, int H) {
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
                           int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
                           float* logits, int64_t cap, int32_t* topk_idx, float* topk_w, float* group_scores_out,
-                          int* err, cudaStream_t stream) {
+                          int* err, cudaStream_t stream, bool allow_tc) {
     int ks = 1;
-    if (router_tc_ok(x_dtype, T, E, H)) {
+    if (allow_tc && err != nullptr && router_tc_ok(x_dtype, T, E, H)) {
         static std::mutex mu;
         static bool attr_set[64] = {};
         int dev = 0;
@@ -649,18 +650,53 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
 // This variant keeps that scratch in the file-scope array below instead.  The array is
 // part of the library image: every GPU that loads the library holds it (2 MiB) until the
 // process exits.  Host code cannot use the array's name as a device address, so the first
-// call on each device looks the address up with cudaGetSymbolAddress (with that device
-// current) and caches it; that first call should therefore come before any stream
-// capture.  Every call overwrites every scratch element it later reads, so nothing needs
-// clearing between calls -- but all calls share the one array: calls that overlap on the
-// GPU (other streams, other threads, concurrent graph replays) race on it.
+// call in each CUDA context looks the address up with cudaGetSymbolAddress (with that
+// context current) and caches it under the context's unique id -- a runtime that creates
+// its own driver contexts, or calls after cudaDeviceReset, gets the address of its own
+// context's copy.  That first call should therefore come before any stream capture.  Every
+// call overwrites every scratch element it later reads, so nothing needs clearing between
+// calls -- but all calls share the one array: calls that overlap on the GPU (other
+// streams, other threads, concurrent graph replays) race on it.  The logits always run on
+// the CUDA cores here: that kernel has no device-side waits, so no call can time out with
+// nowhere to report it (cst_route reports the tensor-core kernel's bounded waits through
+// its context's error word, which this entry point does not have).
 constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 19;  // 2 MiB
 static __device__ __align__(256) float g_router_noalloc_scratch[kNoAllocScratchFloats];
 
 namespace {
-constexpr int kMaxDevices = 64;
-float* g_noalloc_ptr[kMaxDevices] = {};
+constexpr int kMaxContexts = 64;
+struct NoAllocEntry {
+    unsigned long long ctx_id;
+    float* ptr;
+};
+NoAllocEntry g_noalloc_cache[kMaxContexts];
+int g_noalloc_n = 0;
 std::mutex g_noalloc_mu;
+
+// Unique id of the calling thread's current CUDA context (cuCtxGetCurrent + cuCtxGetId,
+// reached through the runtime's driver entry points, so the library links no libcuda);
+// false when no context is current yet or the driver lacks the calls.
+bool current_context_id(unsigned long long* id) {
+    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    static PFN_cuCtxGetId_v12000 get_id = nullptr;
+    static bool resolved = false;
+    if (!resolved) {  // under g_noalloc_mu
+        cudaDriverEntryPointQueryResult q1{}, q2{};
+        void* f1 = nullptr;
+        void* f2 = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f1, 4000, cudaEnableDefault, &q1) == cudaSuccess &&
+            q1 == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f1);
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f2, 12000, cudaEnableDefault, &q2) == cudaSuccess &&
+            q2 == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(f2);
+        resolved = true;
+    }
+    if (!get_current || !get_id) return false;
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+    return get_id(ctx, id) == CUDA_SUCCESS;
+}
 }  // namespace
 
 }  // namespace cst
@@ -690,25 +726,31 @@ extern "C" int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int3
     if (!x || !gate_weight || !bias || !topk_idx || !topk_weight) return set_last_error(3, "null pointer");
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate_weight)) & 15u)
         return set_last_error(3, "x and gate_weight must be 16-byte aligned");
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-        return set_last_error(5, "cudaGetDevice failed or device id out of range");
     float* scratch = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
-        if (g_noalloc_ptr[dev] == nullptr) {
+        unsigned long long cid = 0;
+        bool have_id = current_context_id(&cid);
+        if (have_id) {
+            for (int i = 0; i < g_noalloc_n; ++i)
+                if (g_noalloc_cache[i].ctx_id == cid) scratch = g_noalloc_cache[i].ptr;
+        }
+        if (scratch == nullptr) {
+            // first call in this context (the lookup also binds the device's primary context
+            // when the thread has none current yet)
             void* p = nullptr;
             const cudaError_t e = cudaGetSymbolAddress(&p, g_router_noalloc_scratch);
             if (e != cudaSuccess || p == nullptr)
                 return set_last_error(5, "cudaGetSymbolAddress(router scratch) failed: %s", cudaGetErrorString(e));
-            g_noalloc_ptr[dev] = static_cast<float*>(p);
+            scratch = static_cast<float*>(p);
+            if (!have_id) have_id = current_context_id(&cid);
+            if (have_id && g_noalloc_n < kMaxContexts) g_noalloc_cache[g_noalloc_n++] = {cid, scratch};
         }
-        scratch = g_noalloc_ptr[dev];
     }
     const cudaError_t e = launch_router(x, x_dtype, gate_weight, bias, resident, T, n_experts, hidden, n_group,
                                         topk_group, top_k, norm_topk_prob, routed_scaling_factor, scratch,
                                         kNoAllocScratchFloats, topk_idx, topk_weight, nullptr, nullptr,
-                                        static_cast<cudaStream_t>(stream));
+                                        static_cast<cudaStream_t>(stream), /*allow_tc=*/false);
     if (e != cudaSuccess) return set_last_error(5, "router launch failed: %s", cudaGetErrorString(e));
     return 0;
 }

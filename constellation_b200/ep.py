@@ -129,6 +129,22 @@ class ExpertParallelMoE:
         self._mark("route")
         return self._alltoall(x_local, topk_idx, topk_w, residual, od)
 
+    def routes(self, x_all: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor, *,
+               resident: torch.Tensor | None = None, return_logits: bool = False):
+        """The routes ``forward`` computes for the gathered batch ``x_all`` (``[world * Tl, H]``,
+        rank order): the same router calls over the same row sets -- the whole batch where
+        every rank routes it, each rank's own rows where ranks route their own tokens -- so
+        a checker can compare them with a reference without running the exchange."""
+        Tl = x_all.shape[0] // self.world
+        whole = self.world == 1 or self.mode == "p2p" or (self.mode == "allgather" and Tl < self.local_route_min)
+        chunks = [x_all] if whole else [x_all[r * Tl:(r + 1) * Tl] for r in range(self.world)]
+        parts = [self.c.route(ch, gate_weight, bias, resident=resident, return_aux=return_logits) for ch in chunks]
+        idx = torch.cat([p[0] for p in parts])
+        w = torch.cat([p[1] for p in parts])
+        if return_logits:
+            return idx, w, torch.cat([p[2] for p in parts])
+        return idx, w
+
     # ------------------------------------------------------------------------------
     def _allgather(self, x_local, gate_weight, bias, resident, residual, od) -> torch.Tensor:
         Tl, H = x_local.shape

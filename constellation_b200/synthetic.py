@@ -15,6 +15,26 @@ from __future__ import annotations
 
 import torch
 
+# Seeds of the synthetic tensors.  Layer ``l`` of a stack (``l = 0`` for the one-layer
+# workloads): routed expert ``e`` is seeded ``1000 (l + 1) + e``, the shared expert
+# ``1000 (l + 1) + 999``, the router weight and bias ``7 + 13 l``, the prenorm weight
+# ``100 + l``; the activations ``11``.  Each tensor set has its own generator, so one
+# expert can be regenerated alone (the parity checks rebuild only the experts they need).
+ACTIVATION_SEED = 11
+
+
+def expert_seed(expert: int, layer: int = 0) -> int:
+    """Seed of routed expert ``expert`` of stacked layer ``layer`` (``expert < 0``: the shared one)."""
+    return 1000 * (layer + 1) + (999 if expert < 0 else int(expert))
+
+
+def router_seed(layer: int = 0) -> int:
+    return 7 + 13 * layer
+
+
+def norm_seed(layer: int) -> int:
+    return 100 + layer
+
 
 def quantize_blockwise(w: torch.Tensor, block: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
     """fp32 ``[r, c]`` (multiples of ``block``) -> (uint8 E4M3FN codes, fp32 scale_inv grid)."""
@@ -36,6 +56,12 @@ class SyntheticExpert:
         self.w_gate, self.s_gate = w_gate, s_gate
         self.w_down, self.s_down = w_down, s_down
         self.block = block
+
+
+    def host(self) -> "SyntheticExpert":
+        """numpy copies of the six tensors (what a CPU checker reads)."""
+        t = [v.cpu().numpy() for v in (self.w_up, self.s_up, self.w_gate, self.s_gate, self.w_down, self.s_down)]
+        return SyntheticExpert(*t, block=self.block)
 
 
 def make_expert(hidden: int, inter: int, *, seed: int, device, std: float = 0.02) -> SyntheticExpert:

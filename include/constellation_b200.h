@@ -150,10 +150,14 @@ int cst_route(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, const flo
  * which every GPU that loads the library holds until the process exits.  Limit:
  * T * n_experts <= 524288 floats -- T <= 2048 at 256 experts; larger calls return
  * CST_ERR_INVALID_ARG with a message naming the limit.
- * The first call on a device looks the array's device address up (cudaGetSymbolAddress
- * with that device current) and caches it, so make that first call before any stream
- * capture.  All calls share the one array: calls that overlap on the GPU (other streams,
- * threads or graph replays) race on it.  Results equal cst_route's. */
+ * The first call in each CUDA context (the device's primary context, or a driver context
+ * the caller made current) looks the array's device address up (cudaGetSymbolAddress with
+ * that context current) and caches it under the context's unique id, so make that first
+ * call before any stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (other streams, threads or graph replays) race on it.  The logits always run on
+ * the CUDA cores (a kernel with no device-side waits, so no call can time out unreported);
+ * results equal cst_route's wherever cst_route does the same (up to 2048 bf16 tokens, or
+ * fp16 / fp32 input) and differ elsewhere only in the last ulp of a logit. */
 int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int32_t hidden, const float* gate_weight,
                       const float* bias, const uint8_t* resident, int32_t n_experts, int32_t n_group,
                       int32_t topk_group, int32_t top_k, int32_t norm_topk_prob, float routed_scaling_factor,

@@ -104,6 +104,12 @@ def dequant_fp8_weight_blockwise(w_u8: np.ndarray, scale_inv: np.ndarray, block_
             f"shape mismatch: weight={tuple(w_u8.shape)} scale_inv={tuple(scale_inv.shape)} "
             f"expected_scale_inv={block_grid(rows, cols, block_size)} block_size={block_size}")
     w = decode_e4m3fn(w_u8, ref_quirk=ref_quirk)
+    if rows % block_size == 0 and cols % block_size == 0:
+        # whole blocks: the same fp32 products, broadcast over a block view (no [r, c] scale copy)
+        br, bc = rows // block_size, cols // block_size
+        wb = w.reshape(br, block_size, bc, block_size)
+        wb *= scale_inv[:, None, :, None]
+        return w
     return (w * expand_block_scale(scale_inv, rows, cols, block_size)).astype(np.float32)
 
 

@@ -60,6 +60,50 @@ def moe_layer(x: np.ndarray, gate_weight: np.ndarray, bias: np.ndarray, experts,
                        shared_f32=shared_y, route=r)
 
 
+def moe_layer_tokens(x: np.ndarray, gate_weight: np.ndarray, bias: np.ndarray, get_bundle, shared_bundle, tokens, *,
+                     n_group: int, topk_group: int, top_k: int, norm_topk_prob: bool = True,
+                     routed_scaling_factor: float = 2.5, workers: int = 8):
+    """The layer of ``moe_layer`` for full-size weights, computed for a subset of tokens.
+
+    Routing runs for every token (it is cheap); expert outputs only for ``tokens``, with
+    each touched expert dequantized once, used for its rows and dropped, so host memory
+    stays at ``workers`` dequantized experts.  ``get_bundle(eid)`` returns the expert's six
+    upload tensors as numpy (``w_up``, ``s_up``, ``w_gate``, ``s_gate``, ``w_down``,
+    ``s_down``, ``block``); ``shared_bundle`` likewise or None.  Same arithmetic and
+    accumulation order as ``moe_layer``.  Returns ``(RouteResult, out_f32 [len(tokens), H])``.
+    """
+    from concurrent.futures import ThreadPoolExecutor
+
+    x = np.atleast_2d(np.asarray(x, dtype=np.float32))
+    tokens = np.asarray(tokens, dtype=np.int64)
+    r = route_batched(x, gate_weight, bias, n_group=n_group, topk_group=topk_group, top_k=top_k,
+                      norm_topk_prob=norm_topk_prob, routed_scaling_factor=routed_scaling_factor)
+    sub_idx = r.topk_idx[tokens]
+    k = sub_idx.shape[1]
+    xs = x[tokens]
+    y_tk = np.zeros((tokens.size, k, x.shape[1]), dtype=np.float32)
+
+    def one(e):
+        tt, kk = np.nonzero(sub_idx == e)
+        y = DequantExpert(get_bundle(int(e))).forward(xs[tt])
+        return tt, kk, y
+
+    jobs = [int(e) for e in np.unique(sub_idx)]
+    shared_y = None
+    with ThreadPoolExecutor(max_workers=max(1, workers)) as pool:
+        sh = pool.submit(lambda: DequantExpert(shared_bundle).forward(xs)) if shared_bundle is not None else None
+        for tt, kk, y in pool.map(one, jobs):
+            y_tk[tt, kk] = y
+        if sh is not None:
+            shared_y = sh.result()
+    routed = np.zeros((tokens.size, x.shape[1]), dtype=np.float32)
+    w = r.topk_weight[tokens]
+    for j in range(k):
+        routed = (routed + w[:, j:j + 1] * y_tk[:, j]).astype(np.float32)
+    out = routed if shared_y is None else (routed + shared_y).astype(np.float32)
+    return r, out
+
+
 def bf16_round(x: np.ndarray) -> np.ndarray:
     """fp32 -> nearest bf16 value, as fp32."""
     return decode_bf16(encode_bf16_rne(x))
@@ -90,4 +134,4 @@ def moe_stack(h: np.ndarray, layers, *, n_group: int, topk_group: int, top_k: in
     return h
 
 
-__all__ = ["LayerResult", "moe_layer", "moe_stack", "bf16_round", "rms_norm", "DequantExpert"]
+__all__ = ["LayerResult", "moe_layer", "moe_layer_tokens", "moe_stack", "bf16_round", "rms_norm", "DequantExpert"]

@@ -145,3 +145,48 @@ def canonicalize(routes, scores_for_choice: np.ndarray | None = None):
         return sorted(routes, key=lambda r: r[0])
     sfc = np.asarray(scores_for_choice, dtype=np.float64)
     return sorted(routes, key=lambda r: (-sfc[r[0]], r[0]))
+
+
+def compare_routes(dev_idx, dev_w, hidden, gate_weight, bias, *, dev_logits=None, near_tie: float = 1e-5,
+                   **route_kw) -> dict:
+    """Device routes against this oracle on EVERY token.
+
+    ``dev_idx`` / ``dev_w``: ``[T, k]`` as the device returned them (order: choice desc,
+    index asc, like the oracle).  ``dev_logits``: the device's own ``[T, E]`` fp32 logits,
+    used only to explain a disagreement.
+
+    Returns a dict:
+
+    * ``tokens``; ``near_ties``: tokens whose oracle selection margin is ``<= near_tie``;
+    * ``mismatched``: tokens whose index row differs from the oracle's;
+    * ``explained``: mismatched tokens that are near-ties AND whose device selection this
+      oracle reproduces exactly when it is given the device's fp32 logits instead of its own
+      (correctly rounded, fp64-accumulated) ones -- the two then differ only in the last
+      ulp of a logit, not in the selection logic;
+    * ``unexplained`` = mismatched - explained (what a test asserts to be 0);
+    * ``weight_max_rel``: max relative weight difference over the matching tokens;
+    * ``max_logit_abs_diff`` (with ``dev_logits``): device vs correctly rounded logits.
+    """
+    dev_idx = np.asarray(dev_idx).astype(np.int64)
+    dev_w = np.asarray(dev_w, dtype=np.float32)
+    r = route_batched(hidden, gate_weight, bias, **route_kw)
+    same = np.all(dev_idx == r.topk_idx, axis=1)
+    mism = np.nonzero(~same)[0]
+    near = r.margin <= near_tie
+    explained = 0
+    if mism.size and dev_logits is not None:
+        dl = np.asarray(dev_logits, dtype=np.float32)
+        r2 = route_batched(np.asarray(hidden)[mism], gate_weight, bias, logits=dl[mism], **route_kw)
+        ok = np.all(r2.topk_idx == dev_idx[mism], axis=1) & near[mism]
+        explained = int(ok.sum())
+    wrel = 0.0
+    if same.any():
+        a = dev_w[same].astype(np.float64)
+        b = r.topk_weight[same].astype(np.float64)
+        wrel = float(np.max(np.abs(a - b) / np.maximum(np.abs(b), 1e-30)))
+    out = {"tokens": int(dev_idx.shape[0]), "near_ties": int(near.sum()), "mismatched": int(mism.size),
+           "explained": explained, "unexplained": int(mism.size) - explained, "weight_max_rel": wrel,
+           "mismatched_tokens": [int(t) for t in mism[:16]]}
+    if dev_logits is not None:
+        out["max_logit_abs_diff"] = float(np.max(np.abs(np.asarray(dev_logits, np.float64) - r.logits)))
+    return out

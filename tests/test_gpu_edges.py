@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle import cases
+from oracle import cases, router
 from oracle.expert import DequantExpert
 from oracle.layer import moe_layer
 
@@ -68,9 +68,11 @@ def check_layer(ctx, x, w, b, de, sh, dev, top_k=K):
     args = (torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev))
     out, idx, _ = ctx.moe_layer(*args, top_k=top_k, return_routes=True, out_dtype=torch.float32)
     ref = moe_layer(x, w, b, de, sh, n_group=G, topk_group=TG, top_k=top_k)
-    ok = ref.route.margin > 1e-5
-    assert ok.mean() > 0.9
-    np.testing.assert_array_equal(idx.cpu().numpy()[ok], ref.route.topk_idx[ok])
+    _, _, logits, _ = ctx.route(*args, top_k=top_k, return_aux=True)
+    c = router.compare_routes(idx.cpu().numpy(), ref.route.topk_weight, x, w, b, dev_logits=logits.cpu().numpy(),
+                              n_group=G, topk_group=TG, top_k=top_k)
+    assert c["unexplained"] == 0, c
+    ok = np.all(idx.cpu().numpy() == ref.route.topk_idx, axis=1)
     got = out.cpu().numpy()[ok]
     rel = np.abs(got - ref.out_f32[ok]).max(axis=1) / np.abs(ref.out_f32[ok]).max(axis=1)
     assert float(rel.max()) < 2e-3

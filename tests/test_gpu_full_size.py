@@ -1,0 +1,220 @@
+"""The whole MoE layer at the benchmark's full shapes vs the CPU oracle (needs a B200).
+
+Configs 0 (T = 4), 2 (T = 64) and 4 (T = 4096, Zipf-skewed router bias) of the benchmark on
+one GPU: H = 7168, I = 2048, 256 routed experts + 1 shared (FP8 E4M3 with 128x128 fp32 block
+scales), sigmoid routing with n_group 8 / topk_group 4 / top-8, normalised, x2.5, on the
+benchmark's own seeded synthetic data (``constellation_b200.synthetic``: expert e of layer 0
+seeded 1000 + e, the shared expert 1999, the router 7, the activations 11).
+
+The reference path restated by the oracle: ``route_token_real``
+(server/moe_layer_runtime.py:232-408), dequantize-then-matmul per (token, expert)
+(``run_one_expert_reference``, :581-611), the fp32 combine (``combine_outputs_torch``,
+:148-167) and the shared expert on every token (server/deepseek_full_model_executor.py:264-316),
+``oracle.layer.moe_layer_tokens``.  The oracle dequantizes only the experts the checked tokens
+reach, one at a time per worker thread.
+
+Tolerances:
+* routing: ``topk_idx`` equal on EVERY token.  A token that differs must be a near-tie
+  (oracle margin <= 1e-5) whose device choice the oracle reproduces from the device's own
+  fp32 logits -- the two then differ in the last ulp of a logit, not in the selection; the
+  counts are printed.  Weights within rtol 2e-6 on every matching token.
+* layer output: max row-wise relative error ``max|a - b| / max|ref|`` <= 1e-2 for the bf16
+  output (the benchmark's bar, against an fp32 accumulation) and <= 2e-3 for the fp32 output.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import router
+from oracle.layer import moe_layer_tokens
+
+pytestmark = pytest.mark.gpu
+
+H, I, E, G, TG, K = 7168, 2048, 256, 8, 4, 8
+REL_TOL = 1e-2
+ROUTE_KW = dict(n_group=G, topk_group=TG, top_k=K, norm_topk_prob=True, routed_scaling_factor=2.5)
+WORKERS = min(16, os.cpu_count() or 1)
+
+
+def rowwise_rel(a: np.ndarray, ref: np.ndarray) -> float:
+    a = np.atleast_2d(a).astype(np.float64)
+    ref = np.atleast_2d(ref).astype(np.float64)
+    num = np.abs(a - ref).max(axis=1)
+    den = np.maximum(np.abs(ref).max(axis=1), 1e-30)
+    return float((num / den).max())
+
+
+@pytest.fixture(scope="module")
+def layer():
+    """One full-size layer resident on cuda:0: all 256 routed experts + the shared one."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from constellation_b200 import synthetic
+    from constellation_b200.context import ExpertContext, MoEConfig
+
+    dev = torch.device("cuda", 0)
+    ctx = ExpertContext(dev, MoEConfig(), n_slots=E + 1, max_tokens=4096)
+    for e in range(E):
+        ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(e), device=dev)
+        ctx.upload_expert(e, e, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
+        del ex
+    sh = synthetic.make_expert(H, I, seed=synthetic.expert_seed(-1), device=dev)
+    ctx.upload_expert(E, -1, sh.w_up, sh.s_up, sh.w_gate, sh.s_gate, sh.w_down, sh.s_down)
+    del sh
+    gw, gb = synthetic.make_router(H, E, seed=synthetic.router_seed(), device=dev)
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+
+    def bundle(e):
+        return synthetic.make_expert(H, I, seed=synthetic.expert_seed(e), device=dev).host()
+
+    yield dev, ctx, gw, gb, bundle
+    ctx.close()
+
+
+def _check_layer(dev, ctx, gw, gb, bundle, x, tokens, label):
+    """Device layer (bf16 and fp32 outputs, routes) vs the oracle on ``tokens``."""
+    out, idx, wt = ctx.moe_layer(x, gw, gb, return_routes=True)
+    out32 = ctx.moe_layer(x, gw, gb, out_dtype=torch.float32)
+    _, _, logits, _ = ctx.route(x, gw, gb, return_aux=True)
+    torch.cuda.synchronize(dev)
+    ctx.device_error()
+    xh = x.float().cpu().numpy()
+    gwh, gbh = gw.cpu().numpy(), gb.cpu().numpy()
+    cmp = router.compare_routes(idx.cpu().numpy(), wt.cpu().numpy(), xh, gwh, gbh,
+                                dev_logits=logits.cpu().numpy(), **ROUTE_KW)
+    r, ref = moe_layer_tokens(xh, gwh, gbh, bundle, bundle(-1), tokens, workers=WORKERS, **ROUTE_KW)
+    touched = int(np.unique(r.topk_idx).size)
+    err16 = rowwise_rel(out.float().cpu().numpy()[tokens], ref)
+    err32 = rowwise_rel(out32.cpu().numpy()[tokens], ref)
+    print(f"\n{label}: T={x.shape[0]} touched={touched} checked_tokens={len(tokens)} routes={cmp} "
+          f"bf16_rel={err16:.3e} fp32_rel={err32:.3e}")
+    assert cmp["unexplained"] == 0, cmp
+    assert cmp["weight_max_rel"] <= 2e-6, cmp
+    assert err16 <= REL_TOL, err16
+    assert err32 <= 2e-3, err32
+    return cmp
+
+
+@pytest.mark.parametrize("T", [4, 64])
+def test_full_layer_decode_vs_oracle(layer, T):
+    """Configs 0 and 2: every token's routes and outputs (the decode kernels, K split on the
+    device over ~30 / ~215 touched experts, the paired down items, combine + shared)."""
+    from constellation_b200 import synthetic
+
+    dev, ctx, gw, gb, bundle = layer
+    ctx.set_gemm_mode("auto")
+    x = synthetic.make_activations(T, H, seed=synthetic.ACTIVATION_SEED, device=dev)
+    _check_layer(dev, ctx, gw, gb, bundle, x, np.arange(T), f"config {0 if T == 4 else 2}")
+
+
+def test_full_layer_prefill_zipf_vs_oracle(layer):
+    """Config 4: 4096 tokens with the Zipf-skewed bias -- the tensor-core router logits, the
+    multi-CTA packer and the 128-row prefill kernels.  Routes on every token; outputs on 24
+    tokens spread over the batch (the oracle's cost grows with the experts they reach)."""
+    from constellation_b200 import synthetic
+
+    dev, ctx, gw, _, bundle = layer
+    T = 4096
+    gb = synthetic.zipf_bias(E, seed=synthetic.router_seed(), device=dev)
+    x = synthetic.make_activations(T, H, seed=synthetic.ACTIVATION_SEED, device=dev)
+    tokens = np.linspace(0, T - 1, 24).astype(np.int64)
+    ctx.set_gemm_mode("auto")
+    _check_layer(dev, ctx, gw, gb, bundle, x, tokens, "config 4")
+
+
+def _tie_router(dev):
+    """Gate weight with exact duplicates: row 37 = row 5, and group 3 (rows 96-127) = group 2
+    (rows 64-95), biases duplicated too, so those logits and choice values tie bit for bit."""
+    from constellation_b200 import synthetic
+
+    gw, gb = synthetic.make_router(H, E, seed=synthetic.router_seed(), device=dev)
+    gw[37] = gw[5]
+    gw[96:128] = gw[64:96]
+    gb.zero_()
+    return gw.contiguous(), gb
+
+
+@pytest.mark.parametrize("T", [8, 2100])
+def test_router_exact_ties_go_to_the_lower_index(layer, T):
+    """Exact ties at both selection boundaries, on the SIMT (T = 8) and tensor-core (T = 2100)
+    logit paths.
+    * expert boundary: 7 experts biased +3 in groups 0 and 1, then experts 5 and 37 at +2 with
+      identical rows: the 8th slot must be expert 5, never 37.
+    * group boundary: groups 0, 1 and 4 lead; groups 2 and 3 are identical and lead the rest,
+      so the 4th group slot ties: group 2 must win, and its two +2 experts (64, 65) are chosen
+      rather than group 3's copies (96, 97)."""
+    from constellation_b200 import synthetic
+
+    dev, ctx, *_ = layer
+    gw, gb = _tie_router(dev)
+    x = synthetic.make_activations(T, H, seed=synthetic.ACTIVATION_SEED + 1, device=dev)
+
+    b1 = gb.clone()
+    b1[[0, 1, 2, 3, 33, 34, 35]] = 3.0
+    b1[[5, 37]] = 2.0
+    idx, _, logits, _ = ctx.route(x, gw, b1, return_aux=True)
+    torch.cuda.synchronize(dev)
+    lg = logits.cpu().numpy()
+    assert np.array_equal(lg[:, 5].view(np.uint32), lg[:, 37].view(np.uint32))  # the tie is exact
+    got = np.sort(idx.cpu().numpy(), axis=1)
+    want = np.sort(np.array([0, 1, 2, 3, 33, 34, 35, 5]))
+    assert (got == want).all(), got[np.any(got != want, axis=1)][:4]
+    assert (idx.cpu().numpy()[:, 7] == 5).all()  # the 8th choice: 5 (the tie, lower index)
+
+    b2 = gb.clone()
+    b2[[0, 1, 32, 33, 128, 129]] = 3.0
+    b2[[64, 65, 96, 97]] = 2.0
+    idx2, _, _, gs = ctx.route(x, gw, b2, return_aux=True)
+    torch.cuda.synchronize(dev)
+    g = gs.cpu().numpy()
+    assert np.array_equal(g[:, 2].view(np.uint32), g[:, 3].view(np.uint32))  # groups 2 and 3 tie exactly
+    got2 = np.sort(idx2.cpu().numpy(), axis=1)
+    want2 = np.sort(np.array([0, 1, 32, 33, 128, 129, 64, 65]))
+    assert (got2 == want2).all(), got2[np.any(got2 != want2, axis=1)][:4]
+    # and the oracle, on the same inputs, agrees token for token
+    for b, got_idx in ((b1, idx), (b2, idx2)):
+        r = router.route_batched(x[:8].float().cpu().numpy(), gw.cpu().numpy(), b.cpu().numpy(), **ROUTE_KW)
+        assert np.array_equal(r.topk_idx, got_idx[:8].cpu().numpy().astype(np.int64))
+
+
+def test_activation_outlier_floor(layer):
+    """One element 1e4 times the rest inside a 128-column block of a full-size expert's input.
+
+    The decode packer scales each (row, 128-block) by one power of two fitted to the block's
+    max, so the 127 small elements of that block are represented with an absolute floor of
+    about 2e-6 of the outlier.  To see that floor alone, the expert's up and gate columns at
+    the outlier's position are zeroed: the exact output then does not depend on the outlier at
+    all, and any difference between the device and the oracle is the small elements'
+    representation error.  Bound: row-wise 1e-2 of the output (the benchmark's bar)."""
+    from constellation_b200 import synthetic
+    from constellation_b200.context import ExpertContext, MoEConfig
+    from oracle.expert import DequantExpert
+
+    dev = layer[0]
+    ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(3), device=dev)
+    col = 128 * 17 + 45
+    ex.w_up[:, col] = 0
+    ex.w_gate[:, col] = 0
+    ctx = ExpertContext(dev, MoEConfig(), n_slots=1, max_tokens=4)
+    try:
+        ctx.upload_expert(0, 3, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
+        x = synthetic.make_activations(4, H, seed=synthetic.ACTIVATION_SEED + 2, device=dev).float()
+        base = x.clone()
+        x[:, col] = 1e4 * x.abs().max()
+        xb, baseb = x.to(torch.bfloat16), base.to(torch.bfloat16)
+        y = ctx.expert_forward(3, xb, out_dtype=torch.float32)
+        y0 = ctx.expert_forward(3, baseb, out_dtype=torch.float32)
+        torch.cuda.synchronize(dev)
+        de = DequantExpert(ex.host())
+        ref = de.forward(xb.float().cpu().numpy())
+        ref0 = de.forward(baseb.float().cpu().numpy())
+        assert rowwise_rel(ref, ref0) < 1e-6  # the outlier's column is inert in the exact product
+        err = rowwise_rel(y.cpu().numpy(), ref)
+        err0 = rowwise_rel(y0.cpu().numpy(), ref0)
+        print(f"\noutlier 1e4 x in one block: rel err {err:.3e} (same rows without it: {err0:.3e})")
+        assert err <= REL_TOL, err
+    finally:
+        ctx.close()

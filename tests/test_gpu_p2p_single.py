@@ -15,7 +15,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle import cases
+from oracle import cases, router
 from oracle.expert import DequantExpert
 from oracle.layer import moe_layer
 
@@ -100,7 +100,11 @@ def test_push_reduce_matches_layer_across_counter_wrap(layer, dev):
     # the fused single-GPU layer adds the same rows in the same order
     fused = ctx.moe_layer(xt, wt, bt, out_dtype=torch.float32) + rt
     torch.testing.assert_close(outs[0], fused, rtol=1e-5, atol=1e-5)
-    ok = ref.route.margin > 1e-5
+    idx, _, logits, _ = ctx.route(xt, wt, bt, return_aux=True)
+    c = router.compare_routes(idx.cpu().numpy(), ref.route.topk_weight, xt.float().cpu().numpy(), wt.cpu().numpy(),
+                              bt.cpu().numpy(), dev_logits=logits.cpu().numpy(), n_group=G, topk_group=TG, top_k=K)
+    assert c["unexplained"] == 0, c
+    ok = np.all(idx.cpu().numpy() == ref.route.topk_idx, axis=1)
     got = outs[0].cpu().numpy() - res
     rel = np.abs(got - ref.out_f32).max(axis=1) / np.abs(ref.out_f32).max(axis=1)
     assert float(rel[ok].max()) < 2e-3

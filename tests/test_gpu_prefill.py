@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle import cases
+from oracle import cases, router
 from oracle.expert import DequantExpert
 from oracle.layer import moe_layer
 
@@ -100,8 +100,11 @@ def test_moe_layer_modes_vs_oracle(dev, mode, T):
     out, idx, _ = ctx.moe_layer(*args, return_routes=True, out_dtype=torch.float32)
     de = {e: DequantExpert(v) for e, v in experts.items()}
     ref = moe_layer(x, w, b, de, DequantExpert(sh), n_group=G, topk_group=TG, top_k=K)
-    ok = ref.route.margin > 1e-5
-    np.testing.assert_array_equal(idx.cpu().numpy()[ok], ref.route.topk_idx[ok])
+    _, _, logits, _ = ctx.route(*args, return_aux=True)
+    c = router.compare_routes(idx.cpu().numpy(), ref.route.topk_weight, x, w, b, dev_logits=logits.cpu().numpy(),
+                              n_group=G, topk_group=TG, top_k=K)
+    assert c["unexplained"] == 0, c
+    ok = np.all(idx.cpu().numpy() == ref.route.topk_idx, axis=1)
     tol = 2e-3 if mode == "decode" else PF_TOL
     assert rowwise_rel(out.cpu().numpy()[ok], ref.out_f32[ok]) < tol
     # bit-identical on repeat
