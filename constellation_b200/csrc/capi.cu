@@ -75,10 +75,11 @@ struct Workspace {
     int32_t* tk_row = nullptr;        // [max(max_tokens * 16, max_rows)]
     PackMeta* meta = nullptr;
     uint8_t* xfrag = nullptr;         // [max_rows, H/128, 3072]
-    float* xscale = nullptr;          // [max_rows, H/128, 8]
+    float* xscale = nullptr;          // [max_rows, H/128, 24] (3 terms x 8 tokens per n-tile)
     float* h = nullptr;               // up/gate partial sums [part_rows, 2, I]
     uint8_t* hfrag = nullptr;
     float* hscale = nullptr;
+    int* fix_cnt = nullptr;           // [max_rows, I/128] finished up/gate K splits (self-resetting)
     float* y = nullptr;               // [max_rows, H]
     int* err = nullptr;
     float* tok_scale = nullptr;       // prefill: per x row scale [max(max_tokens, max_rows)]
@@ -198,10 +199,11 @@ int alloc_workspace(cst_ctx* c) {
         {reinterpret_cast<void**>(&w.tk_row), tk * 4},
         {reinterpret_cast<void**>(&w.meta), sizeof(PackMeta)},
         {reinterpret_cast<void**>(&w.xfrag), size_t(R) * (H / kBlock) * kBTileBytes},
-        {reinterpret_cast<void**>(&w.xscale), size_t(R) * (H / kBlock) * kTileCols * 4},
+        {reinterpret_cast<void**>(&w.xscale), size_t(R) * (H / kBlock) * kScalesPerTile * 4},
         {reinterpret_cast<void**>(&w.h), size_t(c->part_rows) * 2 * I * 4},
         {reinterpret_cast<void**>(&w.hfrag), size_t(R) * (I / kBlock) * kBTileBytes},
-        {reinterpret_cast<void**>(&w.hscale), size_t(R) * (I / kBlock) * kTileCols * 4},
+        {reinterpret_cast<void**>(&w.hscale), size_t(R) * (I / kBlock) * kScalesPerTile * 4},
+        {reinterpret_cast<void**>(&w.fix_cnt), size_t(R) * (I / kBlock) * 4},
         {reinterpret_cast<void**>(&w.y), size_t(R) * H * 4},
         {reinterpret_cast<void**>(&w.err), 256},
         {reinterpret_cast<void**>(&w.hist), size_t(w.hist_cap) * 4},
@@ -293,11 +295,18 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     up.max_split = kMaxUpGateSplit;
     up.row_weight = nullptr;
     up.err = w.err;
+    // decode: the up/gate kernel applies SiLU * mul and packs h for the down kernel itself
+    up.h_frag = pf ? nullptr : w.hfrag;
+    up.h_scale = pf ? nullptr : w.hscale;
+    up.fix_cnt = pf ? nullptr : w.fix_cnt;
     CST_CUDA(grouped(up, true, c->num_sms, s));
     prof_mark(c, 3, s);
 
-    PackActArgs ph{w.h, kSrcUpGatePartials, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale, terms};
-    CST_CUDA(pf ? launch_pack_rows(ph, c->num_sms, s) : launch_pack_act(ph, c->num_sms, s));
+    if (pf) {
+        PackActArgs ph{w.h, kSrcUpGatePartials, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale,
+                       terms};
+        CST_CUDA(launch_pack_rows(ph, c->num_sms, s));
+    }
     prof_mark(c, 4, s);
 
     FfnArgs dn = up;
@@ -521,10 +530,9 @@ int cst_route(cst_ctx* c, const void* x, int32_t x_dtype, int32_t T, const float
     if (int rc = ensure_device(c)) return rc;
     const cst_config& f = c->cfg;
     CST_CUDA(launch_router(x, x_dtype, gate_weight, bias, resident, T, f.n_routed_experts, f.hidden_dim, f.n_group,
-                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor,
-                           logits ? logits : c->ws.router_logits,
-                           logits ? int64_t(T) * f.n_routed_experts : c->ws.router_cap, topk_idx, topk_weight,
-                           group_scores, c->ws.err, static_cast<cudaStream_t>(stream)));
+                           f.topk_group, top_k, f.norm_topk_prob, f.routed_scaling_factor, c->ws.router_logits,
+                           c->ws.router_cap, topk_idx, topk_weight, group_scores, c->ws.err,
+                           static_cast<cudaStream_t>(stream), true, logits));
     return CST_OK;
 }
 
@@ -1001,6 +1009,8 @@ int cst_device_error(cst_ctx* c) {
     CST_CUDA(cudaMemcpy(&v, c->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
     if (v != CST_DEV_OK) {
         CST_CUDA(cudaMemset(c->ws.err, 0, sizeof(int)));
+        // a launch that gave up may have left K-split counters part-way: start them afresh
+        CST_CUDA(cudaMemset(c->ws.fix_cnt, 0, size_t(c->max_rows) * (c->cfg.inter_dim / kBlock) * 4));
         return fail(CST_ERR_DEVICE_TIMEOUT, "a device-side wait gave up (code %d)", v);
     }
     return CST_OK;

@@ -26,6 +26,8 @@ constexpr int kPrefillMaxTiles = 16;  // prefill groups carry at most 128 rows
 constexpr int kPrefillGroupRows = kPrefillMaxTiles * kTileCols;
 // B bytes of one n-tile for one 128-wide K block: 3 terms x 8 rows x 128 bytes
 constexpr int kBTileBytes = kSplits * kTileCols * kBlock;  // 3072
+// Activation scales of one n-tile for one K block: a power of two per (term, token)
+constexpr int kScalesPerTile = kSplits * kTileCols;  // 24
 
 // Device error word values (written with atomicMax so the first/most severe sticks).
 constexpr int CST_DEV_OK = 0;
@@ -239,6 +241,29 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
+}
+
+// Max over the warp of 16 values per lane at once (a transposed butterfly: 16 shuffles
+// instead of 80).  Lane l returns the warp-wide max of value t = l >> 1.
+template <int N>
+__device__ __forceinline__ void max_half(float* a, int o, int lane) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+        const float keep = upper ? a[i + N / 2] : a[i];
+        const float send = upper ? a[i] : a[i + N / 2];
+        a[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, o));
+    }
+}
+__device__ __forceinline__ float warp_max16(const float (&v)[16], int lane) {
+    float a[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a[i] = v[i];
+    max_half<16>(a, 16, lane);
+    max_half<8>(a, 8, lane);
+    max_half<4>(a, 4, lane);
+    max_half<2>(a, 2, lane);
+    return fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], 1));
 }
 
 }  // namespace cst

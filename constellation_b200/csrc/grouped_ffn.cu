@@ -47,8 +47,9 @@ struct TcShape {
     static constexpr int kABytes = MATS * 16384;                       // weight tile(s) per kb
     static constexpr int kBBytes = kMaxTilesPerGroup * kBTileBytes;     // 6 KB
     static constexpr int kStage = kABytes + kBBytes;                    // multiple of 1024
-    // per-stage scales: 16 B of each weight-scale row (kb rounded down to 4) + act scales
-    static constexpr int kScBytes = 128;
+    // per-stage scales: 16 B of each weight-scale row (kb rounded down to 4) + the act
+    // scales of the group (3 terms x 8 NT tokens, <= 192 B)
+    static constexpr int kScBytes = 256;
     static constexpr int kScAct = 32;                                   // act scales at +32
     static constexpr int kColsPerBuf = MATS * 48;
     // four accumulator buffers let the MMA issuer run up to four K blocks ahead of the
@@ -71,6 +72,9 @@ __device__ __forceinline__ int choose_split(int base_items, int KB, int max_spli
     return S;
 }
 
+// The four epilogue warps (warps 2-5) synchronise among themselves on named barrier 1.
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+
 // MATS accumulators per item: up/gate (DOWN false) -> mat 0 = w_up, mat 1 = w_gate of one
 // 128-row block; down (DOWN true) -> MATS consecutive 128-row blocks of w_down (so the down
 // projection streams 32 KB per K block too when its row-block count is even).
@@ -85,6 +89,11 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + S::kTmemBufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + S::kTmemBufs);
+    // up/gate epilogue exchange (double-buffered by item): each warp's wait status, the
+    // last-split flag, and the per-token block maxima of each term's residual per warp
+    __shared__ int s_ok[2][4];
+    __shared__ int s_last[2];
+    __shared__ __align__(16) float s_red[2][kSplits][kGroupRows][4];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
@@ -137,9 +146,9 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 const float* W0 = reinterpret_cast<const float*>(slot + a.s0_off);
                 const float* W1 = reinterpret_cast<const float*>(slot + a.s1_off);
                 const int64_t wrow = int64_t(DOWN ? rb * MATS : rb) * a.scale_ld;
-                const float* X = a.bscale + int64_t(gr.tile_base) * a.KB * kTileCols;
+                const float* X = a.bscale + int64_t(gr.tile_base) * a.KB * kScalesPerTile;
                 const uint32_t bbytes = uint32_t(NT) * kBTileBytes;
-                const uint32_t xsb = uint32_t(NT) * kTileCols * 4;
+                const uint32_t xsb = uint32_t(NT) * kScalesPerTile * 4;
                 for (int kb = ks * KBs; kb < (ks + 1) * KBs; ++kb) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
@@ -164,7 +173,7 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                         const int64_t wi = (wrow + (DOWN ? m * a.scale_ld : 0) + kb) & ~int64_t(3);
                         tma_bulk_g2s(sc + 16 * m, (DOWN || m == 0 ? W0 : W1) + wi, 16, &full[s]);
                     }
-                    tma_bulk_g2s(sc + S::kScAct, X + int64_t(kb) * NT * kTileCols, xsb, &full[s]);
+                    tma_bulk_g2s(sc + S::kScAct, X + int64_t(kb) * NT * kScalesPerTile, xsb, &full[s]);
                     ++it;
                 }
             }
@@ -220,21 +229,23 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
         const int row = quarter * 32 + lane;          // weight row inside the 128-row block
         const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
         uint32_t it = 0;
+        uint32_t ep_it = 0;  // items this CTA's epilogue finished (parity selects the exchange buffers)
         bool ok = true;
-        for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++ep_it) {
             const int ks = item % split;
             const int gm = item / split;
             const int gi = gm / a.n_mb;
             const int rb = gm - gi * a.n_mb;
             const GroupRec gr = a.groups[gi];
             const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
+            const int TP = NT * kTileCols;
             float acc[MATS][kGroupRows];
 #pragma unroll
             for (int m = 0; m < MATS; ++m)
 #pragma unroll
                 for (int t = 0; t < kGroupRows; ++t) acc[m][t] = 0.0f;
 
-            for (int kb = ks * KBs; kb < (ks + 1) * KBs; ++kb) {
+            for (int kb = ks * KBs; ok && kb < (ks + 1) * KBs; ++kb) {
                 const int s = it % STAGES;
                 const uint32_t ph = (it / STAGES) & 1u;
                 const int b = it % S::kTmemBufs;
@@ -253,65 +264,141 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                     tmem_ld16(base + m * 48 + 16, &d[m][16]);
                     tmem_ld16(base + m * 48 + 32, &d[m][32]);
                 }
-                // scales of this K block, from the stage
+                tmem_wait_ld();
+#pragma unroll
+                for (int m = 0; m < MATS; ++m) tmem_reg_fence(d[m]);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);
+                // scales of this K block, from the stage: weight scale_inv per matrix, and the
+                // power of two of every (term, token) of the group at xsc[term * TP + token]
                 const float* sc = reinterpret_cast<const float*>(sc_base + s * S::kScBytes);
+                const float* xsc = sc + S::kScAct / 4;
                 float wsc[MATS];
 #pragma unroll
                 for (int m = 0; m < MATS; ++m) {
                     const int64_t wr = int64_t(DOWN ? rb * MATS + m : rb) * a.scale_ld;
                     wsc[m] = sc[4 * m + int((wr + kb) & 3)];
                 }
-                float xs[kGroupRows];
-#pragma unroll
-                for (int t = 0; t < kGroupRows; ++t) xs[t] = (t < NT * kTileCols) ? sc[S::kScAct / 4 + t] : 0.0f;
-                tmem_wait_ld();
-#pragma unroll
-                for (int m = 0; m < MATS; ++m) tmem_reg_fence(d[m]);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&tempty[b]);
-                    mbar_arrive(&empty[s]);
-                }
+                // acc[t] += (D[term0] s0[t] + D[term1] s1[t] + D[term2] s2[t]) * scale_inv[rb, kb]
                 if (NT == 1) {
 #pragma unroll
                     for (int t = 0; t < kTileCols; ++t) {
+                        const float x0 = xsc[t], x1 = xsc[kTileCols + t], x2 = xsc[2 * kTileCols + t];
 #pragma unroll
                         for (int m = 0; m < MATS; ++m) {
-                            const float v = __uint_as_float(d[m][t]) + __uint_as_float(d[m][8 + t]) +
-                                            __uint_as_float(d[m][16 + t]);
-                            acc[m][t] = fmaf(v, wsc[m] * xs[t], acc[m][t]);
+                            const float v = fmaf(__uint_as_float(d[m][16 + t]), x2,
+                                                 fmaf(__uint_as_float(d[m][8 + t]), x1, __uint_as_float(d[m][t]) * x0));
+                            acc[m][t] = fmaf(v, wsc[m], acc[m][t]);
                         }
                     }
                 } else {
 #pragma unroll
                     for (int t = 0; t < kGroupRows; ++t) {
+                        const float x0 = xsc[t], x1 = xsc[kGroupRows + t], x2 = xsc[2 * kGroupRows + t];
 #pragma unroll
                         for (int m = 0; m < MATS; ++m) {
-                            const float v = __uint_as_float(d[m][t]) + __uint_as_float(d[m][16 + t]) +
-                                            __uint_as_float(d[m][32 + t]);
-                            acc[m][t] = fmaf(v, wsc[m] * xs[t], acc[m][t]);
+                            const float v = fmaf(__uint_as_float(d[m][32 + t]), x2,
+                                                 fmaf(__uint_as_float(d[m][16 + t]), x1, __uint_as_float(d[m][t]) * x0));
+                            acc[m][t] = fmaf(v, wsc[m], acc[m][t]);
                         }
                     }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);  // the stage's scales are read
                 ++it;
             }
-            if (!ok) break;
-            // epilogue: one weight row, every token of the group (coalesced along the rows)
+            if constexpr (DOWN) {
+                if (!ok) break;
+                // y * routing weight, one weight row for every token of the group
 #pragma unroll
-            for (int t = 0; t < kGroupRows; ++t) {
-                if (t < gr.n_rows) {
-                    const int prow = gr.row_start + t;
-                    if constexpr (!DOWN) {
-                        // raw split accumulators; the h packer adds the splits and applies SiLU
-                        float* o = a.out + (int64_t(ks) * n_rows + prow) * 2 * a.ld_out + rb * kBlock + row;
-                        o[0] = acc[0][t];
-                        o[a.ld_out] = acc[1][t];
-                    } else {
+                for (int t = 0; t < kGroupRows; ++t) {
+                    if (t < gr.n_rows) {
+                        const int prow = gr.row_start + t;
                         const float rw = a.row_weight[prow];
 #pragma unroll
                         for (int m = 0; m < MATS; ++m)
                             a.out[int64_t(prow) * a.ld_out + (rb * MATS + m) * kBlock + row] = acc[m][t] * rw;
+                    }
+                }
+            } else {
+                // up/gate: h = silu(gate) * up for I-rows [rb 128, rb 128 + 128) of the group's
+                // tokens -- exactly the down projection's K block kb = rb -- quantized here into
+                // the down kernel's B tile (three E4M3 terms, a power of two per term and
+                // token, as pack_act.cu packs x).  With a K split, each split writes its raw
+                // partial sums and the split that finishes last adds them in split order.
+                const int eb = ep_it & 1;
+                if (lane == 0) s_ok[eb][quarter] = ok ? 1 : 0;
+                if (ok && split > 1) {
+#pragma unroll
+                    for (int t = 0; t < kGroupRows; ++t) {
+                        if (t < gr.n_rows) {
+                            float* o = a.out + (int64_t(ks) * n_rows + gr.row_start + t) * 2 * a.ld_out + rb * kBlock + row;
+                            o[0] = acc[0][t];
+                            o[a.ld_out] = acc[1][t];
+                        }
+                    }
+                    __threadfence();
+                }
+                epilogue_sync();
+                const bool all_ok = s_ok[eb][0] && s_ok[eb][1] && s_ok[eb][2] && s_ok[eb][3];
+                if (!all_ok) break;  // the same decision in all four warps: no barrier is left waiting
+                if (split > 1) {
+                    if (threadIdx.x == 64) {
+                        const int old = atomicAdd(a.fix_cnt + gm, 1);
+                        const bool last = old == split - 1;
+                        if (last) {
+                            a.fix_cnt[gm] = 0;  // ready for the next launch
+                            __threadfence();
+                        }
+                        s_last[eb] = last ? 1 : 0;
+                    }
+                    epilogue_sync();
+                    if (!s_last[eb]) continue;
+#pragma unroll
+                    for (int t = 0; t < kGroupRows; ++t) {
+                        if (t < gr.n_rows) {
+                            const float* p = a.out + (int64_t(gr.row_start) + t) * 2 * a.ld_out + rb * kBlock + row;
+                            const int64_t ss = int64_t(n_rows) * 2 * a.ld_out;
+                            float u = ks == 0 ? acc[0][t] : __ldcg(p);
+                            float g = ks == 0 ? acc[1][t] : __ldcg(p + a.ld_out);
+                            for (int z = 1; z < split; ++z) {
+                                u += z == ks ? acc[0][t] : __ldcg(p + z * ss);
+                                g += z == ks ? acc[1][t] : __ldcg(p + z * ss + a.ld_out);
+                            }
+                            acc[0][t] = u;
+                            acc[1][t] = g;
+                        }
+                    }
+                }
+                float r[kGroupRows];
+#pragma unroll
+                for (int t = 0; t < kGroupRows; ++t) {
+                    const float g = acc[1][t];
+                    r[t] = t < gr.n_rows ? (g / (1.0f + expf(-g))) * acc[0][t] : 0.0f;
+                }
+                uint8_t* tile = a.h_frag + (int64_t(gr.tile_base) * a.n_mb + int64_t(rb) * NT) * kBTileBytes;
+                float* tsc = a.h_scale + (int64_t(gr.tile_base) * a.n_mb + int64_t(rb) * NT) * kScalesPerTile;
+#pragma unroll
+                for (int sp = 0; sp < kSplits; ++sp) {
+                    // block max of the residual of every token over the 128 rows (4 warps)
+                    float m[kGroupRows];
+#pragma unroll
+                    for (int t = 0; t < kGroupRows; ++t) m[t] = fabsf(r[t]);
+                    const float wm = warp_max16(m, lane);
+                    if ((lane & 1) == 0) s_red[eb][sp][lane >> 1][quarter] = wm;
+                    epilogue_sync();
+#pragma unroll
+                    for (int t = 0; t < kGroupRows; ++t) {
+                        if (t < gr.n_rows) {
+                            const float4 q4 = *reinterpret_cast<const float4*>(&s_red[eb][sp][t][0]);
+                            const float scl = pow2_scale_for(fmaxf(fmaxf(q4.x, q4.y), fmaxf(q4.z, q4.w)));
+                            const uint8_t bq = e4m3_rn(r[t] * (1.0f / scl));
+                            r[t] -= e4m3_to_f32(bq) * scl;  // exact, as in the x packer
+                            const int n = sp * TP + t;
+                            tile[n * kBlock + ((((row >> 4) ^ (n & 7)) << 4) | (row & 15))] = bq;
+                            if (row == t) tsc[sp * TP + t] = scl;
+                        }
                     }
                 }
             }

@@ -51,13 +51,15 @@ cudaError_t launch_dequant_fp8(const uint8_t* w, const float* s, float* out, int
 // `logits` holds `cap` floats: scratch for the partial logits of a K split, or the caller's
 // [T, E] logits when cap == T * E (no split).  err: device error word (the tensor-core
 // logits kernel's bounded waits report there); with allow_tc false the logits always run
-// on the CUDA cores, whose kernel has no waits, and err may be null.
+// on the CUDA cores, whose kernel has no waits, and err may be null.  logits_out: [T, E]
+// copy of the summed logits the selection used (or null), so a caller that asks for them
+// gets exactly the routing of a call that does not.
 int router_tc_split(int T, int E, int H, int64_t cap);
 int64_t router_scratch_floats(int x_dtype, int T, int E, int H);  // scratch a call of T tokens may use
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
                           int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
                           float* logits, int64_t cap, int32_t* topk_idx, float* topk_w, float* group_scores_out,
-                          int* err, cudaStream_t stream, bool allow_tc = true);
+                          int* err, cudaStream_t stream, bool allow_tc = true, float* logits_out = nullptr);
 
 // route_pack.cu
 struct PackArgs {
@@ -135,8 +137,9 @@ struct FfnArgs {
     PackMeta* meta;           // read: n_groups; written (block 0): the K split chosen
     const uint8_t* bfrag;
     const float* bscale;
-    // up/gate: raw fp32 accumulators out[((split * n_rows + row) * 2 + mat) * ld_out + col],
-    //          n_rows = meta->n_rows
+    // up/gate, K split > 1: raw fp32 partial sums out[((split * n_rows + row) * 2 + mat) * ld_out
+    //          + col], n_rows = meta->n_rows (the decode kernel adds them itself; the prefill
+    //          kernel leaves them to the h packer)
     // down:    out[row * ld_out + col] = accumulator * row_weight[row]
     float* out;
     int64_t ld_out;
@@ -149,6 +152,13 @@ struct FfnArgs {
     // Below one row-block pair per SM the launch takes single row blocks per item, which
     // doubles the items a lone expert spreads over.
     int groups_hint;
+    // decode up/gate only: h = silu(gate) * up is packed by the kernel itself into the down
+    // projection's B tiles (h_frag, h_scale: the layout pack_act.cu writes for x), and
+    // fix_cnt [groups * n_mb] counts the finished K splits of each (group, row block) (zero
+    // between launches: the last split resets its counter)
+    uint8_t* h_frag;
+    float* h_scale;
+    int* fix_cnt;
 };
 cudaError_t grouped_ffn_init_attributes();
 cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream);

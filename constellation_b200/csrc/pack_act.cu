@@ -8,13 +8,16 @@
 // (row, 128-wide K block) is written as
 //     v = s * (q1 + q2 + q3),  q1 = e4m3(v/s), q2 = e4m3(v/s - q1), q3 = e4m3(v/s - q1 - q2)
 // (decode kernels; the prefill kernels take the first two terms only)
-// with s the smallest power of two that maps the block's max |v| to <= 448.  The three
-// terms reproduce v/s to ~2^-12 relative (absolute floor 2^-10 in the scaled domain, i.e.
-// about 2e-6 of the block max), far inside the bf16 resolution of the inputs, and the
-// residuals are exact in fp32.  The grouped kernel applies s per (row, K block) and the
-// weight scale_inv per 128x128 weight block while accumulating in fp32 -- the same
-// algebra as dequantize-then-matmul (server/fp8_utils.py:4-39,
-// server/moe_layer_runtime.py:604-609).
+// with s the smallest power of two that maps the block's max |v| to <= 448.  The decode
+// packer gives every term its own power of two, fitted to the block's largest residual
+// (v = s1 q1 + s2 q2 + s3 q3), so one large element in a block costs the small ones
+// nothing beyond the first term: the three terms reproduce every element to ~2^-12
+// relative of the block's residuals, far inside the bf16 resolution of the inputs, and the
+// residuals are exact in fp32.  (The prefill packer keeps one scale per row for both of
+// its terms; its absolute floor is ~2e-6 of the row max.)  The grouped kernel applies the
+// term scales per (row, K block) and the weight scale_inv per 128x128 weight block while
+// accumulating in fp32 -- the same algebra as dequantize-then-matmul
+// (server/fp8_utils.py:4-39, server/moe_layer_runtime.py:604-609).
 //
 // One warp per (packed row, 8 consecutive K blocks): the row's metadata is read once and
 // the 8 source loads are issued together; per K block 128 elements, 4 per lane, one 32-bit
@@ -122,22 +125,26 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
         for (int i = 0; i < kPackKbPerTask; ++i) {
             const int kb = kb0 + i;
             if (i >= kbpt || kb >= KB) break;
-            float amax = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
-            amax = warp_max(amax);
-            const float s = pow2_scale_for(amax);
-            const float inv = 1.0f / s;  // exact: s is a power of two
+            // term sp carries the residual of the terms before it, scaled by its own power of
+            // two fitted to the block's largest residual: a large element then limits the
+            // resolution of the small ones in its block only through the first term
             uint32_t q[kSplits] = {0u, 0u, 0u};
+            float sc[kSplits] = {1.0f, 1.0f, 1.0f};
+            float* r = v[i];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                float rsd = v[i][e] * inv;
+            for (int sp = 0; sp < kSplits; ++sp) {
+                if (sp >= a.terms) break;
+                float amax = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
+                amax = warp_max(amax);
+                const float s = pow2_scale_for(amax);
+                const float inv = 1.0f / s;  // exact: s is a power of two
 #pragma unroll
-                for (int sp = 0; sp < kSplits; ++sp) {
-                    if (sp < a.terms) {
-                        const uint8_t b = e4m3_rn(rsd);
-                        q[sp] |= uint32_t(b) << (8 * e);
-                        rsd -= e4m3_to_f32(b);
-                    }
+                for (int e = 0; e < 4; ++e) {
+                    const uint8_t b = e4m3_rn(r[e] * inv);
+                    q[sp] |= uint32_t(b) << (8 * e);
+                    r[e] -= e4m3_to_f32(b) * s;  // exact: the scaled residual is representable
                 }
+                sc[sp] = s;
             }
             // K-major, 128-byte swizzled placement: B row n = term * TP + token (TP = 8 NT),
             // 128 bytes of K per row, 16-byte chunk c of row n stored at chunk c ^ (n & 7);
@@ -151,7 +158,11 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
                 const int pc = c ^ (n & 7);
                 *reinterpret_cast<uint32_t*>(base + n * kBlock + pc * 16 + 4 * (lane & 3)) = q[sp];
             }
-            if (lane == 0) a.bscale[gk * kTileCols + tok] = s;
+            if (lane == 0) {
+#pragma unroll
+                for (int sp = 0; sp < kSplits; ++sp)
+                    if (sp < a.terms) a.bscale[gk * kScalesPerTile + sp * TP + tok] = sc[sp];
+            }
         }
     }
 }

@@ -311,6 +311,7 @@ struct RouterArgs {
     int32_t* topk_idx;      // [T, top_k]
     float* topk_w;          // [T, top_k]
     float* group_scores_out;  // [T, n_group] or null
+    float* logits_out;        // [T, E] summed logits or null (the caller's aux copy)
 };
 
 // Warp arg-max with (value desc, index asc); inactive candidates carry idx = INT_MAX.
@@ -367,6 +368,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(RouterArg
         if (e < E) {
             float l = lg[e];
             for (int z = 1; z < a.ks; ++z) l += lg[z * zs + e];  // K ranges in order
+            if (a.logits_out) a.logits_out[int64_t(t) * E + e] = l;
             const float sg = 1.0f / (1.0f + expf(-l));
             const bool res = (a.resident == nullptr) || (a.resident[e] != 0);
             ch[i] = res ? (sg + a.bias[e]) : -INFINITY;
@@ -485,6 +487,7 @@ __global__ void __launch_bounds__(1024) router_select_rank_kernel(RouterArgs a) 
             for (int i = 0; i < 16; ++i)
                 if (z0 + i < a.ks) l += v[i];
         }
+        if (a.logits_out) a.logits_out[int64_t(t) * E + e] = l;
         const float sg = 1.0f / (1.0f + expf(-l));
         const bool res = (a.resident == nullptr) || (a.resident[e] != 0);
         ch = res ? (sg + a.bias[e]) : -INFINITY;
@@ -584,7 +587,7 @@ int64_t router_scratch_floats(int x_dtype, int T, int E, int H) {
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
                           int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
                           float* logits, int64_t cap, int32_t* topk_idx, float* topk_w, float* group_scores_out,
-                          int* err, cudaStream_t stream, bool allow_tc) {
+                          int* err, cudaStream_t stream, bool allow_tc, float* logits_out) {
     int ks = 1;
     if (allow_tc && err != nullptr && router_tc_ok(x_dtype, T, E, H)) {
         static std::mutex mu;
@@ -625,7 +628,7 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
         if (e != cudaSuccess) return e;
     }
     RouterArgs a{logits, ks, bias, resident, T, E, n_group, topk_group, top_k, norm, scale,
-                 topk_idx, topk_w, group_scores_out};
+                 topk_idx, topk_w, group_scores_out, logits_out};
     if (T <= 2048) {
         // decode-sized batches: one CTA per token, short dependency chains
         return launch_chained(router_select_rank_kernel, dim3(T), dim3((E + 31) / 32 * 32), 0, stream, a);

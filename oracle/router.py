@@ -164,7 +164,9 @@ def compare_routes(dev_idx, dev_w, hidden, gate_weight, bias, *, dev_logits=None
       (correctly rounded, fp64-accumulated) ones -- the two then differ only in the last
       ulp of a logit, not in the selection logic;
     * ``unexplained`` = mismatched - explained (what a test asserts to be 0);
-    * ``weight_max_rel``: max relative weight difference over the matching tokens;
+    * ``weight_max_rel``: max relative weight difference over the matching tokens, and
+      ``weights_close``: every such weight within rtol 2e-6 + atol 1e-7 (the tolerance the
+      tests hold the device weights to);
     * ``max_logit_abs_diff`` (with ``dev_logits``): device vs correctly rounded logits.
     """
     dev_idx = np.asarray(dev_idx).astype(np.int64)
@@ -180,12 +182,15 @@ def compare_routes(dev_idx, dev_w, hidden, gate_weight, bias, *, dev_logits=None
         ok = np.all(r2.topk_idx == dev_idx[mism], axis=1) & near[mism]
         explained = int(ok.sum())
     wrel = 0.0
+    close = True
     if same.any():
         a = dev_w[same].astype(np.float64)
         b = r.topk_weight[same].astype(np.float64)
         wrel = float(np.max(np.abs(a - b) / np.maximum(np.abs(b), 1e-30)))
+        close = bool(np.all(np.abs(a - b) <= 2e-6 * np.abs(b) + 1e-7))
     out = {"tokens": int(dev_idx.shape[0]), "near_ties": int(near.sum()), "mismatched": int(mism.size),
            "explained": explained, "unexplained": int(mism.size) - explained, "weight_max_rel": wrel,
+           "weights_close": close,
            "mismatched_tokens": [int(t) for t in mism[:16]]}
     if dev_logits is not None:
         out["max_logit_abs_diff"] = float(np.max(np.abs(np.asarray(dev_logits, np.float64) - r.logits)))

@@ -92,7 +92,7 @@ def _check_layer(dev, ctx, gw, gb, bundle, x, tokens, label):
     print(f"\n{label}: T={x.shape[0]} touched={touched} checked_tokens={len(tokens)} routes={cmp} "
           f"bf16_rel={err16:.3e} fp32_rel={err32:.3e}")
     assert cmp["unexplained"] == 0, cmp
-    assert cmp["weight_max_rel"] <= 2e-6, cmp
+    assert cmp["weights_close"], cmp
     assert err16 <= REL_TOL, err16
     assert err32 <= 2e-3, err32
     return cmp
@@ -183,12 +183,16 @@ def test_router_exact_ties_go_to_the_lower_index(layer, T):
 def test_activation_outlier_floor(layer):
     """One element 1e4 times the rest inside a 128-column block of a full-size expert's input.
 
-    The decode packer scales each (row, 128-block) by one power of two fitted to the block's
-    max, so the 127 small elements of that block are represented with an absolute floor of
-    about 2e-6 of the outlier.  To see that floor alone, the expert's up and gate columns at
-    the outlier's position are zeroed: the exact output then does not depend on the outlier at
-    all, and any difference between the device and the oracle is the small elements'
-    representation error.  Bound: row-wise 1e-2 of the output (the benchmark's bar)."""
+    The decode packers give each of the three E4M3 terms of a (row, 128-block) its own power
+    of two, fitted to the block's largest residual, so the outlier takes the first term and the
+    127 small elements of its block keep ~2^-12 relative resolution in the other two.  To see
+    the small elements alone, the expert's up and gate columns at the outlier's position are
+    zeroed: the exact output then does not depend on the outlier at all, and any difference
+    between the device and the oracle is the small elements' representation error.
+    Bound (decode): 2e-4 row-wise, the fp32 expert bound of the other tests -- with one shared
+    power of two per block the same input measured 1.4e-2.  The prefill kernels keep one
+    power of two per row for their two terms (their absolute floor is ~2e-6 of the row max):
+    checked to 1e-2 up to a 1e2 outlier, and the larger ones are printed."""
     from constellation_b200 import synthetic
     from constellation_b200.context import ExpertContext, MoEConfig
     from oracle.expert import DequantExpert
@@ -201,20 +205,23 @@ def test_activation_outlier_floor(layer):
     ctx = ExpertContext(dev, MoEConfig(), n_slots=1, max_tokens=4)
     try:
         ctx.upload_expert(0, 3, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
-        x = synthetic.make_activations(4, H, seed=synthetic.ACTIVATION_SEED + 2, device=dev).float()
-        base = x.clone()
-        x[:, col] = 1e4 * x.abs().max()
-        xb, baseb = x.to(torch.bfloat16), base.to(torch.bfloat16)
-        y = ctx.expert_forward(3, xb, out_dtype=torch.float32)
-        y0 = ctx.expert_forward(3, baseb, out_dtype=torch.float32)
-        torch.cuda.synchronize(dev)
         de = DequantExpert(ex.host())
-        ref = de.forward(xb.float().cpu().numpy())
-        ref0 = de.forward(baseb.float().cpu().numpy())
-        assert rowwise_rel(ref, ref0) < 1e-6  # the outlier's column is inert in the exact product
-        err = rowwise_rel(y.cpu().numpy(), ref)
-        err0 = rowwise_rel(y0.cpu().numpy(), ref0)
-        print(f"\noutlier 1e4 x in one block: rel err {err:.3e} (same rows without it: {err0:.3e})")
-        assert err <= REL_TOL, err
+        base = synthetic.make_activations(4, H, seed=synthetic.ACTIVATION_SEED + 2, device=dev).float()
+        report = {}
+        for mode, mult in (("decode", 1e4), ("prefill", 1e2), ("prefill", 1e3), ("prefill", 1e4)):
+            x = base.clone()
+            x[:, col] = mult * base.abs().max()
+            xb = x.to(torch.bfloat16)
+            ctx.set_gemm_mode(mode)
+            y = ctx.expert_forward(3, xb, out_dtype=torch.float32)
+            torch.cuda.synchronize(dev)
+            ref = de.forward(xb.float().cpu().numpy())
+            ref0 = de.forward(base.to(torch.bfloat16).float().cpu().numpy())
+            assert rowwise_rel(ref, ref0) < 1e-6  # the outlier's column is inert in the exact product
+            report[(mode, mult)] = rowwise_rel(y.cpu().numpy(), ref)
+        print("\noutlier in one block, row-wise rel err: " +
+              ", ".join(f"{m} x{k:g}: {v:.2e}" for (m, k), v in report.items()))
+        assert report[("decode", 1e4)] <= 2e-4, report
+        assert report[("prefill", 1e2)] <= REL_TOL, report
     finally:
         ctx.close()

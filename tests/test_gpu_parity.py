@@ -45,7 +45,7 @@ def assert_routes(idx, wt, logits, x, w, b, **kw) -> dict:
     iw = wt.cpu().numpy() if wt is not None else router.route_batched(x, w, b, **kw).topk_weight
     c = router.compare_routes(idx.cpu().numpy(), iw, x, w, b, dev_logits=logits.cpu().numpy(), **kw)
     assert c["unexplained"] == 0, c
-    assert c["weight_max_rel"] <= 2e-6, c
+    assert c["weights_close"], c
     return c
 
 
