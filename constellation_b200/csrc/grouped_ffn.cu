@@ -74,6 +74,7 @@ __device__ __forceinline__ int choose_split(int base_items, int KB, int max_spli
 
 // The four epilogue warps (warps 2-5) synchronise among themselves on named barrier 1.
 __device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;\n" ::: "memory"); }
 
 // MATS accumulators per item: up/gate (DOWN false) -> mat 0 = w_up, mat 1 = w_gate of one
 // 128-row block; down (DOWN true) -> MATS consecutive 128-row blocks of w_down (so the down
@@ -338,18 +339,21 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                             o[a.ld_out] = acc[1][t];
                         }
                     }
-                    __threadfence();
                 }
                 epilogue_sync();
                 const bool all_ok = s_ok[eb][0] && s_ok[eb][1] && s_ok[eb][2] && s_ok[eb][3];
                 if (!all_ok) break;  // the same decision in all four warps: no barrier is left waiting
                 if (split > 1) {
                     if (threadIdx.x == 64) {
+                        // release: the four warps' partial sums (ordered before this thread by
+                        // the barrier) become visible at GPU scope before the count does;
+                        // acquire: the split that counts last then sees every other split's sums
+                        fence_acq_rel_gpu();
                         const int old = atomicAdd(a.fix_cnt + gm, 1);
                         const bool last = old == split - 1;
                         if (last) {
                             a.fix_cnt[gm] = 0;  // ready for the next launch
-                            __threadfence();
+                            fence_acq_rel_gpu();
                         }
                         s_last[eb] = last ? 1 : 0;
                     }
