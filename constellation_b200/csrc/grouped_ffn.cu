@@ -7,27 +7,32 @@
 // Work item = (group, 128-row block rb of the output dimension, K split ks); a group is <= 16
 // packed activation rows of one expert slot (route_pack.cu).  The K split S (1, 2 or 4) is
 // chosen on the device from the group count so that small decode batches still give every
-// SM several items; up/gate then writes S raw partial sums that the h packer adds in fixed
-// order (pack_act.cu), the down projection never splits; instead a down item takes two
+// SM several items; the down projection never splits; instead a down item takes two
 // consecutive 128-row blocks when H / 128 is even, so both projections stream 32 KB of
 // weights per K block.  One persistent CTA per SM walks the item list with 6 warps:
 //   warp 0, one lane: TMA producer.  Per 128-wide K block kb it bulk-copies the weight tile
 //     (16 KB per matrix: up+gate = 32 KB, down = 16 KB; contiguous in the arena and already in
 //     the swizzled K-major image the tensor cores read, relayout.cu), the group's B tile
-//     (three E4M3 activation terms x 8 or 16 tokens, 3 or 6 KB, pack_act.cu) and the block's
-//     scales (weight scale_inv entries and the tokens' activation scales, <= 96 B) into a
+//     (three E4M3 activation terms x 8 or 16 tokens, 3 or 6 KB) and the block's scales
+//     (weight scale_inv entries and the activation terms' powers of two, <= 224 B) into a
 //     ring of STAGES shared-memory stages; it runs ahead across item boundaries.
-//   warp 1, one lane: MMA issuer.  Per kb: 4 k-steps x MATS of
+//   warp 1, one lane: MMA issuer.  Per kb: copies the stage's scales into the scale slot of
+//     its TMEM accumulator buffer, then 4 k-steps x MATS of
 //     tcgen05.mma.cta_group::1.kind::f8f6f4, M = 128 weight rows, N = 3 terms x 8/16 tokens,
 //     K = 32, into one of four TMEM accumulator buffers; tcgen05.commit frees the smem stage
-//     and signals the accumulator to the epilogue.
+//     and signals the accumulator to the epilogue.  The epilogue never holds a stage.
 //   warps 2-5: epilogue.  Each thread owns one weight row (its TMEM lane): per kb it loads the
-//     accumulator (tcgen05.ld) and the stage's scales, releases both, and promotes
-//       acc[token] += (D[term0] + D[term1] + D[term2]) * scale_inv[rb, kb] * act_scale[token, kb]
+//     accumulator (tcgen05.ld), promotes
+//       acc[token] += (D[term0] s0[token] + D[term1] s1[token] + D[term2] s2[token]) * scale_inv[rb, kb]
 //     in fp32 -- the block-scaled algebra of dequantize-then-matmul (server/fp8_utils.py:4-39,
-//     server/moe_layer_runtime.py:604-609) with the scales applied once per 128x128 block.
-//     At the end of an item: up/gate -> the raw up and gate partial sums of split ks,
-//     down -> y * routing weight, written per packed row in fp32 (coalesced along the rows).
+//     server/moe_layer_runtime.py:604-609) with the scales applied once per 128x128 block and
+//     s0..s2 the powers of two of the activation terms -- and releases the buffer.
+//     At the end of an item: down -> y * routing weight, written per packed row in fp32
+//     (coalesced along the rows); up/gate -> h = silu(gate) * up (:604-609), quantized in
+//     place into the down projection's B tile (this item's 128 I-rows are exactly one K
+//     block of the down projection), so no separate h packer runs.  With a K split the
+//     splits write raw partial sums, count themselves on a per-(group, rb) counter, and the
+//     split that counts last adds the partials in split order and packs h.
 // TMEM: MATS x 48 fp32 columns per accumulator buffer, four buffers (512 / 256 columns),
 // allocated by warp 2 and freed on every exit path.
 //
@@ -51,6 +56,7 @@ struct TcShape {
     // scales of the group (3 terms x 8 NT tokens, <= 192 B)
     static constexpr int kScBytes = 256;
     static constexpr int kScAct = 32;                                   // act scales at +32
+    static constexpr int kScUsed = kScAct + kMaxTilesPerGroup * kScalesPerTile * 4;  // 224
     static constexpr int kColsPerBuf = MATS * 48;
     // four accumulator buffers let the MMA issuer run up to four K blocks ahead of the
     // epilogue (4 x 96 -> 512 columns for two accumulators, 4 x 48 -> 256 for one)
@@ -85,7 +91,11 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sc_base = smem + STAGES * S::kStage;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sc_base + STAGES * S::kScBytes);
+    // the scales of the K block in each TMEM accumulator buffer, copied out of the stage by
+    // the MMA issuer: the epilogue never holds a stage, so the bulk-copy ring runs up to
+    // STAGES K blocks ahead of the MMAs however long the epilogue takes at an item's end
+    uint8_t* bsc_base = sc_base + STAGES * S::kScBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(bsc_base + S::kTmemBufs * S::kScBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + S::kTmemBufs;
@@ -101,10 +111,10 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1 + 4);  // MMA commit + the four epilogue warps (scales read)
+            mbar_init(&empty[s], 1);  // the MMA commit
         }
         for (int b = 0; b < S::kTmemBufs; ++b) {
-            mbar_init(&tfull[b], 1);
+            mbar_init(&tfull[b], 2);  // the MMA commit + the issuer's copy of the scales
             mbar_init(&tempty[b], 4);
         }
         fence_barrier_init();
@@ -206,6 +216,14 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                         break;
                     }
                     tc_fence_after();
+                    {
+                        // the stage's scales -> buffer b's slot; the arrive releases them
+                        const uint4* src = reinterpret_cast<const uint4*>(sc_base + s * S::kScBytes);
+                        uint4* dst = reinterpret_cast<uint4*>(bsc_base + b * S::kScBytes);
+#pragma unroll
+                        for (int i = 0; i < S::kScUsed / 16; ++i) dst[i] = src[i];
+                        mbar_arrive(&tfull[b]);
+                    }
                     const uint32_t st = smem_base + s * S::kStage;
 #pragma unroll
                     for (int ks = 0; ks < kBlock / kKStep; ++ks) {
@@ -247,12 +265,10 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 for (int t = 0; t < kGroupRows; ++t) acc[m][t] = 0.0f;
 
             for (int kb = ks * KBs; ok && kb < (ks + 1) * KBs; ++kb) {
-                const int s = it % STAGES;
-                const uint32_t ph = (it / STAGES) & 1u;
                 const int b = it % S::kTmemBufs;
                 const uint32_t bph = (it / S::kTmemBufs) & 1u;
-                // full[s] makes the stage's scales (written by the bulk copies) visible here
-                if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tfull[b], bph, a.err)) {
+                // tfull[b]: the accumulator is complete and its K block's scales are in slot b
+                if (!mbar_wait(&tfull[b], bph, a.err)) {
                     ok = false;
                     break;
                 }
@@ -268,12 +284,9 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 tmem_wait_ld();
 #pragma unroll
                 for (int m = 0; m < MATS; ++m) tmem_reg_fence(d[m]);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[b]);
-                // scales of this K block, from the stage: weight scale_inv per matrix, and the
-                // power of two of every (term, token) of the group at xsc[term * TP + token]
-                const float* sc = reinterpret_cast<const float*>(sc_base + s * S::kScBytes);
+                // scales of this K block: weight scale_inv per matrix, and the power of two of
+                // every (term, token) of the group at xsc[term * TP + token]
+                const float* sc = reinterpret_cast<const float*>(bsc_base + b * S::kScBytes);
                 const float* xsc = sc + S::kScAct / 4;
                 float wsc[MATS];
 #pragma unroll
@@ -305,8 +318,9 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                         }
                     }
                 }
+                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);  // the stage's scales are read
+                if (lane == 0) mbar_arrive(&tempty[b]);  // accumulator and scale slot b are read
                 ++it;
             }
             if constexpr (DOWN) {
@@ -397,7 +411,7 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                         if (t < gr.n_rows) {
                             const float4 q4 = *reinterpret_cast<const float4*>(&s_red[eb][sp][t][0]);
                             const float scl = pow2_scale_for(fmaxf(fmaxf(q4.x, q4.y), fmaxf(q4.z, q4.w)));
-                            const uint8_t bq = e4m3_rn(r[t] * (1.0f / scl));
+                            const uint8_t bq = e4m3_rn(r[t] * __frcp_rn(scl));  // exact: a power of two
                             r[t] -= e4m3_to_f32(bq) * scl;  // exact, as in the x packer
                             const int n = sp * TP + t;
                             tile[n * kBlock + ((((row >> 4) ^ (n & 7)) << 4) | (row & 15))] = bq;
@@ -420,8 +434,8 @@ constexpr int kDownStages = 8;
 
 template <int MATS, int STAGES>
 size_t tc_smem_bytes() {
-    return size_t(STAGES) * (TcShape<MATS>::kStage + TcShape<MATS>::kScBytes) + 1024 /* alignment slack */ +
-           256 /* barriers */;
+    return size_t(STAGES) * (TcShape<MATS>::kStage + TcShape<MATS>::kScBytes) +
+           TcShape<MATS>::kTmemBufs * TcShape<MATS>::kScBytes + 1024 /* alignment slack */ + 256 /* barriers */;
 }
 
 cudaError_t grouped_ffn_init_attributes() {
