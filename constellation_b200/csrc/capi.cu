@@ -1049,7 +1049,8 @@ int cst_ctx_info(const cst_ctx* c, int64_t* out, int32_t n) {
     int resident = 0;
     for (int v : c->slot_of_expert) resident += v >= 0;
     const int64_t vals[] = {int64_t(c->cfg.n_slots) * c->geo.slot_bytes, c->geo.slot_bytes, int64_t(c->ws_bytes),
-                            c->num_sms, resident, c->shared_slot};
+                            c->num_sms, resident, c->shared_slot,
+                            static_cast<int64_t>(reinterpret_cast<uintptr_t>(c->arena))};
     const int m = std::min<int>(n, int(sizeof(vals) / sizeof(vals[0])));
     for (int i = 0; i < m; ++i) out[i] = vals[i];
     return m;

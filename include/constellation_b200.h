@@ -360,7 +360,8 @@ int cst_profile_enable(cst_ctx* ctx, int32_t enable);
 int cst_profile_read(cst_ctx* ctx, float* stage_ms, int32_t max_calls);
 
 /* Context facts: out[0] arena bytes, [1] bytes per slot, [2] workspace bytes,
- * [3] number of SMs, [4] resident routed experts, [5] shared slot. Returns #values written. */
+ * [3] number of SMs, [4] resident routed experts, [5] shared slot, [6] device address of
+ * the arena (slot s starts at [6] + s * [1]). Returns #values written. */
 int cst_ctx_info(const cst_ctx* ctx, int64_t* out, int32_t n);
 
 /* Message of the last failing call on this thread ("" if none). */
