@@ -57,6 +57,7 @@ struct TcShape {
     static constexpr int kScBytes = 256;
     static constexpr int kScAct = 32;                                   // act scales at +32
     static constexpr int kScUsed = kScAct + kMaxTilesPerGroup * kScalesPerTile * 4;  // 224
+    static constexpr int kScSlots = 8;  // > kTmemBufs: a slot is free again before the MMA needs it
     static constexpr int kColsPerBuf = MATS * 48;
     // four accumulator buffers let the MMA issuer run up to four K blocks ahead of the
     // epilogue (4 x 96 -> 512 columns for two accumulators, 4 x 48 -> 256 for one)
@@ -91,15 +92,17 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sc_base = smem + STAGES * S::kStage;
-    // the scales of the K block in each TMEM accumulator buffer, copied out of the stage by
-    // the MMA issuer: the epilogue never holds a stage, so the bulk-copy ring runs up to
-    // STAGES K blocks ahead of the MMAs however long the epilogue takes at an item's end
+    // a ring of kScSlots scale slots, filled by the MMA issuer from the stages: the epilogue
+    // reads a K block's scales there, so it holds neither a stage nor (after its TMEM loads)
+    // an accumulator buffer while it computes, and the bulk-copy ring and the MMAs run ahead
+    // however long the epilogue takes at an item's end
     uint8_t* bsc_base = sc_base + STAGES * S::kScBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(bsc_base + S::kTmemBufs * S::kScBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(bsc_base + S::kScSlots * S::kScBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + S::kTmemBufs;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + S::kTmemBufs);
+    uint64_t* sempty = tempty + S::kTmemBufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + S::kScSlots);
     // up/gate epilogue exchange (double-buffered by item): each warp's wait status, the
     // last-split flag, and the per-token block maxima of each term's residual per warp
     __shared__ int s_ok[2][4];
@@ -117,6 +120,7 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
             mbar_init(&tfull[b], 2);  // the MMA commit + the issuer's copy of the scales
             mbar_init(&tempty[b], 4);
         }
+        for (int j = 0; j < S::kScSlots; ++j) mbar_init(&sempty[j], 4);
         fence_barrier_init();
     }
     if (warp == 2) {
@@ -211,15 +215,18 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                     const uint32_t ph = (it / STAGES) & 1u;
                     const int b = it % S::kTmemBufs;
                     const uint32_t bph = (it / S::kTmemBufs) & 1u;
-                    if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tempty[b], bph ^ 1u, a.err)) {
+                    const int j = it % S::kScSlots;
+                    const uint32_t jph = (it / S::kScSlots) & 1u;
+                    if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tempty[b], bph ^ 1u, a.err) ||
+                        !mbar_wait(&sempty[j], jph ^ 1u, a.err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     {
-                        // the stage's scales -> buffer b's slot; the arrive releases them
+                        // the stage's scales -> scale slot j; the arrive on tfull[b] publishes them
                         const uint4* src = reinterpret_cast<const uint4*>(sc_base + s * S::kScBytes);
-                        uint4* dst = reinterpret_cast<uint4*>(bsc_base + b * S::kScBytes);
+                        uint4* dst = reinterpret_cast<uint4*>(bsc_base + j * S::kScBytes);
 #pragma unroll
                         for (int i = 0; i < S::kScUsed / 16; ++i) dst[i] = src[i];
                         mbar_arrive(&tfull[b]);
@@ -284,9 +291,13 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 tmem_wait_ld();
 #pragma unroll
                 for (int m = 0; m < MATS; ++m) tmem_reg_fence(d[m]);
-                // scales of this K block: weight scale_inv per matrix, and the power of two of
-                // every (term, token) of the group at xsc[term * TP + token]
-                const float* sc = reinterpret_cast<const float*>(bsc_base + b * S::kScBytes);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);  // the accumulator is in registers
+                // scales of this K block (slot j): weight scale_inv per matrix, and the power of
+                // two of every (term, token) of the group at xsc[term * TP + token]
+                const int j = it % S::kScSlots;
+                const float* sc = reinterpret_cast<const float*>(bsc_base + j * S::kScBytes);
                 const float* xsc = sc + S::kScAct / 4;
                 float wsc[MATS];
 #pragma unroll
@@ -318,9 +329,8 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                         }
                     }
                 }
-                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[b]);  // accumulator and scale slot b are read
+                if (lane == 0) mbar_arrive(&sempty[j]);  // scale slot j is read
                 ++it;
             }
             if constexpr (DOWN) {
@@ -435,7 +445,7 @@ constexpr int kDownStages = 8;
 template <int MATS, int STAGES>
 size_t tc_smem_bytes() {
     return size_t(STAGES) * (TcShape<MATS>::kStage + TcShape<MATS>::kScBytes) +
-           TcShape<MATS>::kTmemBufs * TcShape<MATS>::kScBytes + 1024 /* alignment slack */ + 256 /* barriers */;
+           TcShape<MATS>::kScSlots * TcShape<MATS>::kScBytes + 1024 /* alignment slack */ + 512 /* barriers */;
 }
 
 cudaError_t grouped_ffn_init_attributes() {
