@@ -12,12 +12,12 @@
 // weights per K block.  One persistent CTA per SM walks the item list with 6 warps:
 //   warp 0, one lane: TMA producer.  Per 128-wide K block kb it bulk-copies the weight tile
 //     (16 KB per matrix: up+gate = 32 KB, down = 16 KB; contiguous in the arena and already in
-//     the swizzled K-major image the tensor cores read, relayout.cu), the group's B tile
-//     (three E4M3 activation terms x 8 or 16 tokens, 3 or 6 KB) and the block's scales
-//     (weight scale_inv entries and the activation terms' powers of two, <= 224 B) into a
-//     ring of STAGES shared-memory stages; it runs ahead across item boundaries.
-//   warp 1, one lane: MMA issuer.  Per kb: copies the stage's scales into the scale slot of
-//     its TMEM accumulator buffer, then 4 k-steps x MATS of
+//     the swizzled K-major image the tensor cores read, relayout.cu) and the group's B tile
+//     (three E4M3 activation terms x 8 or 16 tokens, 3 or 6 KB) into a ring of STAGES
+//     shared-memory stages, and the block's scales (weight scale_inv entries and the
+//     activation terms' powers of two, <= 224 B) into a separate ring of scale slots; it runs
+//     ahead across item boundaries.
+//   warp 1, one lane: MMA issuer.  Per kb: 4 k-steps x MATS of
 //     tcgen05.mma.cta_group::1.kind::f8f6f4, M = 128 weight rows, N = 3 terms x 8/16 tokens,
 //     K = 32, into one of four TMEM accumulator buffers; tcgen05.commit frees the smem stage
 //     and signals the accumulator to the epilogue.  The epilogue never holds a stage.
@@ -56,8 +56,9 @@ struct TcShape {
     // scales of the group (3 terms x 8 NT tokens, <= 192 B)
     static constexpr int kScBytes = 256;
     static constexpr int kScAct = 32;                                   // act scales at +32
-    static constexpr int kScUsed = kScAct + kMaxTilesPerGroup * kScalesPerTile * 4;  // 224
-    static constexpr int kScSlots = 8;  // > kTmemBufs: a slot is free again before the MMA needs it
+    // > STAGES + kTmemBufs: the producer, at most that far ahead of the epilogue, never waits
+    // for a scale slot
+    static constexpr int kScSlots = 16;
     static constexpr int kColsPerBuf = MATS * 48;
     // four accumulator buffers let the MMA issuer run up to four K blocks ahead of the
     // epilogue (4 x 96 -> 512 columns for two accumulators, 4 x 48 -> 256 for one)
@@ -91,12 +92,11 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     using S = TcShape<MATS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sc_base = smem + STAGES * S::kStage;
-    // a ring of kScSlots scale slots, filled by the MMA issuer from the stages: the epilogue
-    // reads a K block's scales there, so it holds neither a stage nor (after its TMEM loads)
-    // an accumulator buffer while it computes, and the bulk-copy ring and the MMAs run ahead
-    // however long the epilogue takes at an item's end
-    uint8_t* bsc_base = sc_base + STAGES * S::kScBytes;
+    // a ring of kScSlots scale slots beside the stages, filled by the producer's bulk copies:
+    // the epilogue reads a K block's scales there, so it holds neither a stage nor (after
+    // its TMEM loads) an accumulator buffer while it computes, and the bulk-copy ring and the
+    // MMAs run ahead however long the epilogue takes at an item's end
+    uint8_t* bsc_base = smem + STAGES * S::kStage;
     uint64_t* full = reinterpret_cast<uint64_t*>(bsc_base + S::kScSlots * S::kScBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
             mbar_init(&empty[s], 1);  // the MMA commit
         }
         for (int b = 0; b < S::kTmemBufs; ++b) {
-            mbar_init(&tfull[b], 2);  // the MMA commit + the issuer's copy of the scales
+            mbar_init(&tfull[b], 2);  // the MMA commit + the issuer's arrive (the stage landed)
             mbar_init(&tempty[b], 4);
         }
         for (int j = 0; j < S::kScSlots; ++j) mbar_init(&sempty[j], 4);
@@ -167,12 +167,14 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 for (int kb = ks * KBs; kb < (ks + 1) * KBs; ++kb) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) {
+                    const int j = it % S::kScSlots;
+                    const uint32_t jph = (it / S::kScSlots) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, a.err) || !mbar_wait(&sempty[j], jph ^ 1u, a.err)) {
                         ok = false;
                         break;
                     }
                     uint8_t* st = smem + s * S::kStage;
-                    uint8_t* sc = sc_base + s * S::kScBytes;
+                    uint8_t* sc = bsc_base + j * S::kScBytes;  // completes on full[s] with the stage
                     mbar_arrive_expect_tx(&full[s], S::kABytes + bbytes + 16 * MATS + xsb);
                     if constexpr (DOWN) {
 #pragma unroll
@@ -215,22 +217,14 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                     const uint32_t ph = (it / STAGES) & 1u;
                     const int b = it % S::kTmemBufs;
                     const uint32_t bph = (it / S::kTmemBufs) & 1u;
-                    const int j = it % S::kScSlots;
-                    const uint32_t jph = (it / S::kScSlots) & 1u;
-                    if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tempty[b], bph ^ 1u, a.err) ||
-                        !mbar_wait(&sempty[j], jph ^ 1u, a.err)) {
+                    if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tempty[b], bph ^ 1u, a.err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    {
-                        // the stage's scales -> scale slot j; the arrive on tfull[b] publishes them
-                        const uint4* src = reinterpret_cast<const uint4*>(sc_base + s * S::kScBytes);
-                        uint4* dst = reinterpret_cast<uint4*>(bsc_base + j * S::kScBytes);
-#pragma unroll
-                        for (int i = 0; i < S::kScUsed / 16; ++i) dst[i] = src[i];
-                        mbar_arrive(&tfull[b]);
-                    }
+                    // this thread saw the stage (and its scale slot) land: its arrive passes that
+                    // on to the epilogue, whose wait on tfull[b] also needs the MMAs' commit
+                    mbar_arrive(&tfull[b]);
                     const uint32_t st = smem_base + s * S::kStage;
 #pragma unroll
                     for (int ks = 0; ks < kBlock / kKStep; ++ks) {
@@ -444,8 +438,8 @@ constexpr int kDownStages = 8;
 
 template <int MATS, int STAGES>
 size_t tc_smem_bytes() {
-    return size_t(STAGES) * (TcShape<MATS>::kStage + TcShape<MATS>::kScBytes) +
-           TcShape<MATS>::kScSlots * TcShape<MATS>::kScBytes + 1024 /* alignment slack */ + 512 /* barriers */;
+    return size_t(STAGES) * TcShape<MATS>::kStage + TcShape<MATS>::kScSlots * TcShape<MATS>::kScBytes +
+           1024 /* alignment slack */ + 512 /* barriers */;
 }
 
 cudaError_t grouped_ffn_init_attributes() {
