@@ -79,7 +79,6 @@ struct Workspace {
     float* h = nullptr;               // up/gate partial sums [part_rows, 2, I]
     uint8_t* hfrag = nullptr;
     float* hscale = nullptr;
-    int* fix_cnt = nullptr;           // [max_rows, I/128] finished up/gate K splits (self-resetting)
     float* y = nullptr;               // [max_rows, H]
     int* err = nullptr;
     float* tok_scale = nullptr;       // prefill: per x row scale [max(max_tokens, max_rows)]
@@ -203,7 +202,6 @@ int alloc_workspace(cst_ctx* c) {
         {reinterpret_cast<void**>(&w.h), size_t(c->part_rows) * 2 * I * 4},
         {reinterpret_cast<void**>(&w.hfrag), size_t(R) * (I / kBlock) * kBTileBytes},
         {reinterpret_cast<void**>(&w.hscale), size_t(R) * (I / kBlock) * kScalesPerTile * 4},
-        {reinterpret_cast<void**>(&w.fix_cnt), size_t(R) * (I / kBlock) * 4},
         {reinterpret_cast<void**>(&w.y), size_t(R) * H * 4},
         {reinterpret_cast<void**>(&w.err), 256},
         {reinterpret_cast<void**>(&w.hist), size_t(w.hist_cap) * 4},
@@ -295,18 +293,11 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     up.max_split = kMaxUpGateSplit;
     up.row_weight = nullptr;
     up.err = w.err;
-    // decode: the up/gate kernel applies SiLU * mul and packs h for the down kernel itself
-    up.h_frag = pf ? nullptr : w.hfrag;
-    up.h_scale = pf ? nullptr : w.hscale;
-    up.fix_cnt = pf ? nullptr : w.fix_cnt;
     CST_CUDA(grouped(up, true, c->num_sms, s));
     prof_mark(c, 3, s);
 
-    if (pf) {
-        PackActArgs ph{w.h, kSrcUpGatePartials, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale,
-                       terms};
-        CST_CUDA(launch_pack_rows(ph, c->num_sms, s));
-    }
+    PackActArgs ph{w.h, kSrcUpGatePartials, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale, terms};
+    CST_CUDA(pf ? launch_pack_rows(ph, c->num_sms, s) : launch_pack_act(ph, c->num_sms, s));
     prof_mark(c, 4, s);
 
     FfnArgs dn = up;
@@ -1009,8 +1000,6 @@ int cst_device_error(cst_ctx* c) {
     CST_CUDA(cudaMemcpy(&v, c->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
     if (v != CST_DEV_OK) {
         CST_CUDA(cudaMemset(c->ws.err, 0, sizeof(int)));
-        // a launch that gave up may have left K-split counters part-way: start them afresh
-        CST_CUDA(cudaMemset(c->ws.fix_cnt, 0, size_t(c->max_rows) * (c->cfg.inter_dim / kBlock) * 4));
         return fail(CST_ERR_DEVICE_TIMEOUT, "a device-side wait gave up (code %d)", v);
     }
     return CST_OK;

@@ -243,27 +243,4 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// Max over the warp of 16 values per lane at once (a transposed butterfly: 16 shuffles
-// instead of 80).  Lane l returns the warp-wide max of value t = l >> 1.
-template <int N>
-__device__ __forceinline__ void max_half(float* a, int o, int lane) {
-    const bool upper = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < N / 2; ++i) {
-        const float keep = upper ? a[i + N / 2] : a[i];
-        const float send = upper ? a[i] : a[i + N / 2];
-        a[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, o));
-    }
-}
-__device__ __forceinline__ float warp_max16(const float (&v)[16], int lane) {
-    float a[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) a[i] = v[i];
-    max_half<16>(a, 16, lane);
-    max_half<8>(a, 8, lane);
-    max_half<4>(a, 4, lane);
-    max_half<2>(a, 2, lane);
-    return fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], 1));
-}
-
 }  // namespace cst

@@ -7,7 +7,8 @@
 // Work item = (group, 128-row block rb of the output dimension, K split ks); a group is <= 16
 // packed activation rows of one expert slot (route_pack.cu).  The K split S (1, 2 or 4) is
 // chosen on the device from the group count so that small decode batches still give every
-// SM several items; the down projection never splits; instead a down item takes two
+// SM several items; up/gate then writes S raw partial sums that the h packer adds in fixed
+// order (pack_act.cu); the down projection never splits; instead a down item takes two
 // consecutive 128-row blocks when H / 128 is even, so both projections stream 32 KB of
 // weights per K block.  One persistent CTA per SM walks the item list with 6 warps:
 //   warp 0, one lane: TMA producer.  Per 128-wide K block kb it bulk-copies the weight tile
@@ -27,12 +28,9 @@
 //     in fp32 -- the block-scaled algebra of dequantize-then-matmul (server/fp8_utils.py:4-39,
 //     server/moe_layer_runtime.py:604-609) with the scales applied once per 128x128 block and
 //     s0..s2 the powers of two of the activation terms -- and releases the buffer.
-//     At the end of an item: down -> y * routing weight, written per packed row in fp32
-//     (coalesced along the rows); up/gate -> h = silu(gate) * up (:604-609), quantized in
-//     place into the down projection's B tile (this item's 128 I-rows are exactly one K
-//     block of the down projection), so no separate h packer runs.  With a K split the
-//     splits write raw partial sums, count themselves on a per-(group, rb) counter, and the
-//     split that counts last adds the partials in split order and packs h.
+//     At the end of an item: up/gate -> the raw up and gate partial sums of split ks (the h
+//     packer, pack_act.cu, adds the splits in order and applies SiLU * mul), down -> y *
+//     routing weight, written per packed row in fp32 (coalesced along the rows).
 // TMEM: MATS x 48 fp32 columns per accumulator buffer, four buffers (512 / 256 columns),
 // allocated by warp 2 and freed on every exit path.
 //
@@ -80,9 +78,6 @@ __device__ __forceinline__ int choose_split(int base_items, int KB, int max_spli
     return S;
 }
 
-// The four epilogue warps (warps 2-5) synchronise among themselves on named barrier 1.
-__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;\n" ::: "memory"); }
 
 // MATS accumulators per item: up/gate (DOWN false) -> mat 0 = w_up, mat 1 = w_gate of one
 // 128-row block; down (DOWN true) -> MATS consecutive 128-row blocks of w_down (so the down
@@ -103,11 +98,6 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     uint64_t* tempty = tfull + S::kTmemBufs;
     uint64_t* sempty = tempty + S::kTmemBufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + S::kScSlots);
-    // up/gate epilogue exchange (double-buffered by item): each warp's wait status, the
-    // last-split flag, and the per-token block maxima of each term's residual per warp
-    __shared__ int s_ok[2][4];
-    __shared__ int s_last[2];
-    __shared__ __align__(16) float s_red[2][kSplits][kGroupRows][4];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
@@ -249,9 +239,8 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
         const int row = quarter * 32 + lane;          // weight row inside the 128-row block
         const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
         uint32_t it = 0;
-        uint32_t ep_it = 0;  // items this CTA's epilogue finished (parity selects the exchange buffers)
         bool ok = true;
-        for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++ep_it) {
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             const int ks = item % split;
             const int gm = item / split;
             const int gi = gm / a.n_mb;
@@ -327,100 +316,22 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 if (lane == 0) mbar_arrive(&sempty[j]);  // scale slot j is read
                 ++it;
             }
-            if constexpr (DOWN) {
-                if (!ok) break;
-                // y * routing weight, one weight row for every token of the group
+            if (!ok) break;
+            // one weight row, every token of the group (coalesced along the rows)
 #pragma unroll
-                for (int t = 0; t < kGroupRows; ++t) {
-                    if (t < gr.n_rows) {
-                        const int prow = gr.row_start + t;
+            for (int t = 0; t < kGroupRows; ++t) {
+                if (t < gr.n_rows) {
+                    const int prow = gr.row_start + t;
+                    if constexpr (!DOWN) {
+                        // raw split accumulators; the h packer adds the splits and applies SiLU
+                        float* o = a.out + (int64_t(ks) * n_rows + prow) * 2 * a.ld_out + rb * kBlock + row;
+                        o[0] = acc[0][t];
+                        o[a.ld_out] = acc[1][t];
+                    } else {
                         const float rw = a.row_weight[prow];
 #pragma unroll
                         for (int m = 0; m < MATS; ++m)
                             a.out[int64_t(prow) * a.ld_out + (rb * MATS + m) * kBlock + row] = acc[m][t] * rw;
-                    }
-                }
-            } else {
-                // up/gate: h = silu(gate) * up for I-rows [rb 128, rb 128 + 128) of the group's
-                // tokens -- exactly the down projection's K block kb = rb -- quantized here into
-                // the down kernel's B tile (three E4M3 terms, a power of two per term and
-                // token, as pack_act.cu packs x).  With a K split, each split writes its raw
-                // partial sums and the split that finishes last adds them in split order.
-                const int eb = ep_it & 1;
-                if (lane == 0) s_ok[eb][quarter] = ok ? 1 : 0;
-                if (ok && split > 1) {
-#pragma unroll
-                    for (int t = 0; t < kGroupRows; ++t) {
-                        if (t < gr.n_rows) {
-                            float* o = a.out + (int64_t(ks) * n_rows + gr.row_start + t) * 2 * a.ld_out + rb * kBlock + row;
-                            o[0] = acc[0][t];
-                            o[a.ld_out] = acc[1][t];
-                        }
-                    }
-                }
-                epilogue_sync();
-                const bool all_ok = s_ok[eb][0] && s_ok[eb][1] && s_ok[eb][2] && s_ok[eb][3];
-                if (!all_ok) break;  // the same decision in all four warps: no barrier is left waiting
-                if (split > 1) {
-                    if (threadIdx.x == 64) {
-                        // release: the four warps' partial sums (ordered before this thread by
-                        // the barrier) become visible at GPU scope before the count does;
-                        // acquire: the split that counts last then sees every other split's sums
-                        fence_acq_rel_gpu();
-                        const int old = atomicAdd(a.fix_cnt + gm, 1);
-                        const bool last = old == split - 1;
-                        if (last) {
-                            a.fix_cnt[gm] = 0;  // ready for the next launch
-                            fence_acq_rel_gpu();
-                        }
-                        s_last[eb] = last ? 1 : 0;
-                    }
-                    epilogue_sync();
-                    if (!s_last[eb]) continue;
-#pragma unroll
-                    for (int t = 0; t < kGroupRows; ++t) {
-                        if (t < gr.n_rows) {
-                            const float* p = a.out + (int64_t(gr.row_start) + t) * 2 * a.ld_out + rb * kBlock + row;
-                            const int64_t ss = int64_t(n_rows) * 2 * a.ld_out;
-                            float u = ks == 0 ? acc[0][t] : __ldcg(p);
-                            float g = ks == 0 ? acc[1][t] : __ldcg(p + a.ld_out);
-                            for (int z = 1; z < split; ++z) {
-                                u += z == ks ? acc[0][t] : __ldcg(p + z * ss);
-                                g += z == ks ? acc[1][t] : __ldcg(p + z * ss + a.ld_out);
-                            }
-                            acc[0][t] = u;
-                            acc[1][t] = g;
-                        }
-                    }
-                }
-                float r[kGroupRows];
-#pragma unroll
-                for (int t = 0; t < kGroupRows; ++t) {
-                    const float g = acc[1][t];
-                    r[t] = t < gr.n_rows ? (g / (1.0f + expf(-g))) * acc[0][t] : 0.0f;
-                }
-                uint8_t* tile = a.h_frag + (int64_t(gr.tile_base) * a.n_mb + int64_t(rb) * NT) * kBTileBytes;
-                float* tsc = a.h_scale + (int64_t(gr.tile_base) * a.n_mb + int64_t(rb) * NT) * kScalesPerTile;
-#pragma unroll
-                for (int sp = 0; sp < kSplits; ++sp) {
-                    // block max of the residual of every token over the 128 rows (4 warps)
-                    float m[kGroupRows];
-#pragma unroll
-                    for (int t = 0; t < kGroupRows; ++t) m[t] = fabsf(r[t]);
-                    const float wm = warp_max16(m, lane);
-                    if ((lane & 1) == 0) s_red[eb][sp][lane >> 1][quarter] = wm;
-                    epilogue_sync();
-#pragma unroll
-                    for (int t = 0; t < kGroupRows; ++t) {
-                        if (t < gr.n_rows) {
-                            const float4 q4 = *reinterpret_cast<const float4*>(&s_red[eb][sp][t][0]);
-                            const float scl = pow2_scale_for(fmaxf(fmaxf(q4.x, q4.y), fmaxf(q4.z, q4.w)));
-                            const uint8_t bq = e4m3_rn(r[t] * __frcp_rn(scl));  // exact: a power of two
-                            r[t] -= e4m3_to_f32(bq) * scl;  // exact, as in the x packer
-                            const int n = sp * TP + t;
-                            tile[n * kBlock + ((((row >> 4) ^ (n & 7)) << 4) | (row & 15))] = bq;
-                            if (row == t) tsc[sp * TP + t] = scl;
-                        }
                     }
                 }
             }

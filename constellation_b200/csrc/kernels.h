@@ -137,9 +137,8 @@ struct FfnArgs {
     PackMeta* meta;           // read: n_groups; written (block 0): the K split chosen
     const uint8_t* bfrag;
     const float* bscale;
-    // up/gate, K split > 1: raw fp32 partial sums out[((split * n_rows + row) * 2 + mat) * ld_out
-    //          + col], n_rows = meta->n_rows (the decode kernel adds them itself; the prefill
-    //          kernel leaves them to the h packer)
+    // up/gate: raw fp32 accumulators out[((split * n_rows + row) * 2 + mat) * ld_out + col],
+    //          n_rows = meta->n_rows
     // down:    out[row * ld_out + col] = accumulator * row_weight[row]
     float* out;
     int64_t ld_out;
@@ -152,13 +151,6 @@ struct FfnArgs {
     // Below one row-block pair per SM the launch takes single row blocks per item, which
     // doubles the items a lone expert spreads over.
     int groups_hint;
-    // decode up/gate only: h = silu(gate) * up is packed by the kernel itself into the down
-    // projection's B tiles (h_frag, h_scale: the layout pack_act.cu writes for x), and
-    // fix_cnt [groups * n_mb] counts the finished K splits of each (group, row block) (zero
-    // between launches: the last split resets its counter)
-    uint8_t* h_frag;
-    float* h_scale;
-    int* fix_cnt;
 };
 cudaError_t grouped_ffn_init_attributes();
 cudaError_t launch_grouped_ffn(const FfnArgs& a, bool upgate, int num_sms, cudaStream_t stream);
