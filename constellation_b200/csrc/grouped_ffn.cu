@@ -14,20 +14,19 @@
 //   warp 0, one lane: TMA producer.  Per 128-wide K block kb it bulk-copies the weight tile
 //     (16 KB per matrix: up+gate = 32 KB, down = 16 KB; contiguous in the arena and already in
 //     the swizzled K-major image the tensor cores read, relayout.cu) and the group's B tile
-//     (three E4M3 activation terms x 8 or 16 tokens, 3 or 6 KB) into a ring of STAGES
-//     shared-memory stages, and the block's scales (weight scale_inv entries and the
-//     activation terms' powers of two, <= 224 B) into a separate ring of scale slots; it runs
-//     ahead across item boundaries.
+//     (three E4M3 activation terms x 8 or 16 tokens, 3 or 6 KB) and the block's scales
+//     (weight scale_inv entries and the activation terms' powers of two, <= 224 B) into a ring
+//     of STAGES shared-memory stages; it runs ahead across item boundaries.
 //   warp 1, one lane: MMA issuer.  Per kb: 4 k-steps x MATS of
 //     tcgen05.mma.cta_group::1.kind::f8f6f4, M = 128 weight rows, N = 3 terms x 8/16 tokens,
 //     K = 32, into one of four TMEM accumulator buffers; tcgen05.commit frees the smem stage
-//     and signals the accumulator to the epilogue.  The epilogue never holds a stage.
+//     and signals the accumulator to the epilogue.
 //   warps 2-5: epilogue.  Each thread owns one weight row (its TMEM lane): per kb it loads the
-//     accumulator (tcgen05.ld), promotes
+//     accumulator (tcgen05.ld) and the stage's scales into registers, releases both, promotes
 //       acc[token] += (D[term0] s0[token] + D[term1] s1[token] + D[term2] s2[token]) * scale_inv[rb, kb]
 //     in fp32 -- the block-scaled algebra of dequantize-then-matmul (server/fp8_utils.py:4-39,
 //     server/moe_layer_runtime.py:604-609) with the scales applied once per 128x128 block and
-//     s0..s2 the powers of two of the activation terms -- and releases the buffer.
+//     s0..s2 the powers of two of the activation terms.
 //     At the end of an item: up/gate -> the raw up and gate partial sums of split ks (the h
 //     packer, pack_act.cu, adds the splits in order and applies SiLU * mul), down -> y *
 //     routing weight, written per packed row in fp32 (coalesced along the rows).
@@ -54,9 +53,6 @@ struct TcShape {
     // scales of the group (3 terms x 8 NT tokens, <= 192 B)
     static constexpr int kScBytes = 256;
     static constexpr int kScAct = 32;                                   // act scales at +32
-    // > STAGES + kTmemBufs: the producer, at most that far ahead of the epilogue, never waits
-    // for a scale slot
-    static constexpr int kScSlots = 16;
     static constexpr int kColsPerBuf = MATS * 48;
     // four accumulator buffers let the MMA issuer run up to four K blocks ahead of the
     // epilogue (4 x 96 -> 512 columns for two accumulators, 4 x 48 -> 256 for one)
@@ -87,30 +83,26 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
     using S = TcShape<MATS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    // a ring of kScSlots scale slots beside the stages, filled by the producer's bulk copies:
-    // the epilogue reads a K block's scales there, so it holds neither a stage nor (after
-    // its TMEM loads) an accumulator buffer while it computes, and the bulk-copy ring and the
-    // MMAs run ahead however long the epilogue takes at an item's end
+    // each stage's scales sit beside the stages; the epilogue copies a K block's scales to
+    // registers and releases the stage and the TMEM buffer before it computes
     uint8_t* bsc_base = smem + STAGES * S::kStage;
-    uint64_t* full = reinterpret_cast<uint64_t*>(bsc_base + S::kScSlots * S::kScBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(bsc_base + STAGES * S::kScBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + S::kTmemBufs;
-    uint64_t* sempty = tempty + S::kTmemBufs;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + S::kScSlots);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + S::kTmemBufs);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);  // the MMA commit
+            mbar_init(&empty[s], 1 + 4);  // the MMA commit + the four epilogue warps
         }
         for (int b = 0; b < S::kTmemBufs; ++b) {
-            mbar_init(&tfull[b], 2);  // the MMA commit + the issuer's arrive (the stage landed)
+            mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 4);
         }
-        for (int j = 0; j < S::kScSlots; ++j) mbar_init(&sempty[j], 4);
         fence_barrier_init();
     }
     if (warp == 2) {
@@ -157,14 +149,12 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                 for (int kb = ks * KBs; kb < (ks + 1) * KBs; ++kb) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
-                    const int j = it % S::kScSlots;
-                    const uint32_t jph = (it / S::kScSlots) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, a.err) || !mbar_wait(&sempty[j], jph ^ 1u, a.err)) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) {
                         ok = false;
                         break;
                     }
                     uint8_t* st = smem + s * S::kStage;
-                    uint8_t* sc = bsc_base + j * S::kScBytes;  // completes on full[s] with the stage
+                    uint8_t* sc = bsc_base + s * S::kScBytes;
                     mbar_arrive_expect_tx(&full[s], S::kABytes + bbytes + 16 * MATS + xsb);
                     if constexpr (DOWN) {
 #pragma unroll
@@ -212,9 +202,6 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                         break;
                     }
                     tc_fence_after();
-                    // this thread saw the stage (and its scale slot) land: its arrive passes that
-                    // on to the epilogue, whose wait on tfull[b] also needs the MMAs' commit
-                    mbar_arrive(&tfull[b]);
                     const uint32_t st = smem_base + s * S::kStage;
 #pragma unroll
                     for (int ks = 0; ks < kBlock / kKStep; ++ks) {
@@ -257,8 +244,9 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
             for (int kb = ks * KBs; ok && kb < (ks + 1) * KBs; ++kb) {
                 const int b = it % S::kTmemBufs;
                 const uint32_t bph = (it / S::kTmemBufs) & 1u;
-                // tfull[b]: the accumulator is complete and its K block's scales are in slot b
-                if (!mbar_wait(&tfull[b], bph, a.err)) {
+                const int s = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1u;
+                if (!mbar_wait(&full[s], ph, a.err) || !mbar_wait(&tfull[b], bph, a.err)) {
                     ok = false;
                     break;
                 }
@@ -271,22 +259,24 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                     tmem_ld16(base + m * 48 + 16, &d[m][16]);
                     tmem_ld16(base + m * 48 + 32, &d[m][32]);
                 }
-                tmem_wait_ld();
-#pragma unroll
-                for (int m = 0; m < MATS; ++m) tmem_reg_fence(d[m]);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[b]);  // the accumulator is in registers
-                // scales of this K block (slot j): weight scale_inv per matrix, and the power of
-                // two of every (term, token) of the group at xsc[term * TP + token]
-                const int j = it % S::kScSlots;
-                const float* sc = reinterpret_cast<const float*>(bsc_base + j * S::kScBytes);
-                const float* xsc = sc + S::kScAct / 4;
+                const float* sc = reinterpret_cast<const float*>(bsc_base + s * S::kScBytes);
                 float wsc[MATS];
 #pragma unroll
                 for (int m = 0; m < MATS; ++m) {
                     const int64_t wr = int64_t(DOWN ? rb * MATS + m : rb) * a.scale_ld;
                     wsc[m] = sc[4 * m + int((wr + kb) & 3)];
+                }
+                float xsc[3 * kGroupRows];
+#pragma unroll
+                for (int i = 0; i < 3 * kGroupRows; ++i) xsc[i] = (i < 3 * TP) ? sc[S::kScAct / 4 + i] : 0.0f;
+                tmem_wait_ld();
+#pragma unroll
+                for (int m = 0; m < MATS; ++m) tmem_reg_fence(d[m]);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&tempty[b]);
+                    mbar_arrive(&empty[s]);
                 }
                 // acc[t] += (D[term0] s0[t] + D[term1] s1[t] + D[term2] s2[t]) * scale_inv[rb, kb]
                 if (NT == 1) {
@@ -312,8 +302,6 @@ __global__ void __launch_bounds__(192, 1) grouped_ffn_tc_kernel(FfnArgs a) {
                         }
                     }
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sempty[j]);  // scale slot j is read
                 ++it;
             }
             if (!ok) break;
@@ -349,7 +337,7 @@ constexpr int kDownStages = 8;
 
 template <int MATS, int STAGES>
 size_t tc_smem_bytes() {
-    return size_t(STAGES) * TcShape<MATS>::kStage + TcShape<MATS>::kScSlots * TcShape<MATS>::kScBytes +
+    return size_t(STAGES) * TcShape<MATS>::kStage + STAGES * TcShape<MATS>::kScBytes +
            1024 /* alignment slack */ + 512 /* barriers */;
 }
 
