@@ -78,12 +78,14 @@ __device__ __forceinline__ void load4(const PackActArgs& a, int64_t src_row, int
 
 constexpr int kPackKbPerTask = 8;  // K blocks one warp packs for one row (at most)
 
+// KBPT: K blocks one warp packs for one row (x rows: 8; split partials, which read up to 8
+// loads per element: 2, so more warps are in flight)
+template <int KBPT>
 __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
     chain_wait();
     chain_release();
     const int KB = a.K / kBlock;
-    // split partials read up to 8 loads per element: smaller tasks, more warps in flight
-    const int kbpt = a.src_dtype == kSrcUpGatePartials ? 2 : kPackKbPerTask;
+    const int kbpt = KBPT;
     const int n_chunks = (KB + kbpt - 1) / kbpt;
     const int n_tiles = a.meta->n_tiles;
     const int split = a.src_dtype == kSrcUpGatePartials ? a.meta->split_k : 1;
@@ -109,9 +111,9 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
         const int64_t src_row = a.row_map ? a.row_map[prow] : prow;
         const int kb0 = chunk * kbpt;
         // all source loads of the chunk first
-        float v[kPackKbPerTask][4];
+        float v[KBPT][4];
 #pragma unroll
-        for (int i = 0; i < kPackKbPerTask; ++i) {
+        for (int i = 0; i < KBPT; ++i) {
             if (i < kbpt && kb0 + i < KB) {
                 load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, split, v[i]);
             } else {
@@ -121,31 +123,43 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
         const int tok = nt * kTileCols + j;
         const int TP = NT * kTileCols;
         const int c = lane >> 2;
+        // Term sp carries the residual of the terms before it, scaled by its own power of two
+        // fitted to the block's largest residual: a large element then limits the resolution
+        // of the small ones in its block only through the first term.  The task's K blocks are
+        // independent, so each term's block maxima of all of them are reduced side by side.
+        uint32_t q[KBPT][kSplits];
+        float sc[KBPT][kSplits];
 #pragma unroll
-        for (int i = 0; i < kPackKbPerTask; ++i) {
-            const int kb = kb0 + i;
-            if (i >= kbpt || kb >= KB) break;
-            // term sp carries the residual of the terms before it, scaled by its own power of
-            // two fitted to the block's largest residual: a large element then limits the
-            // resolution of the small ones in its block only through the first term
-            uint32_t q[kSplits] = {0u, 0u, 0u};
-            float sc[kSplits] = {1.0f, 1.0f, 1.0f};
-            float* r = v[i];
+        for (int sp = 0; sp < kSplits; ++sp) {
+            if (sp >= a.terms) break;
+            float m[KBPT];
 #pragma unroll
-            for (int sp = 0; sp < kSplits; ++sp) {
-                if (sp >= a.terms) break;
-                float amax = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
-                amax = warp_max(amax);
-                const float s = pow2_scale_for(amax);
+            for (int i = 0; i < KBPT; ++i)
+                m[i] = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int i = 0; i < KBPT; ++i) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+            }
+#pragma unroll
+            for (int i = 0; i < KBPT; ++i) {
+                const float s = pow2_scale_for(m[i]);
                 const float inv = 1.0f / s;  // exact: s is a power of two
+                uint32_t w = 0u;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const uint8_t b = e4m3_rn(r[e] * inv);
-                    q[sp] |= uint32_t(b) << (8 * e);
-                    r[e] -= e4m3_to_f32(b) * s;  // exact: the scaled residual is representable
+                    const uint8_t b = e4m3_rn(v[i][e] * inv);
+                    w |= uint32_t(b) << (8 * e);
+                    v[i][e] -= e4m3_to_f32(b) * s;  // exact: the scaled residual is representable
                 }
-                sc[sp] = s;
+                q[i][sp] = w;
+                sc[i][sp] = s;
             }
+        }
+#pragma unroll
+        for (int i = 0; i < KBPT; ++i) {
+            const int kb = kb0 + i;
+            if (i >= kbpt || kb >= KB) break;
             // K-major, 128-byte swizzled placement: B row n = term * TP + token (TP = 8 NT),
             // 128 bytes of K per row, 16-byte chunk c of row n stored at chunk c ^ (n & 7);
             // the (group, kb) tile is terms x TP rows (3 terms: decode, 2 terms: prefill).
@@ -156,12 +170,12 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
                 if (sp >= a.terms) break;
                 const int n = sp * TP + tok;
                 const int pc = c ^ (n & 7);
-                *reinterpret_cast<uint32_t*>(base + n * kBlock + pc * 16 + 4 * (lane & 3)) = q[sp];
+                *reinterpret_cast<uint32_t*>(base + n * kBlock + pc * 16 + 4 * (lane & 3)) = q[i][sp];
             }
             if (lane == 0) {
 #pragma unroll
                 for (int sp = 0; sp < kSplits; ++sp)
-                    if (sp < a.terms) a.bscale[gk * kScalesPerTile + sp * TP + tok] = sc[sp];
+                    if (sp < a.terms) a.bscale[gk * kScalesPerTile + sp * TP + tok] = sc[i][sp];
             }
         }
     }
@@ -285,7 +299,9 @@ cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t str
 }
 
 cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream) {
-    return launch_chained(pack_act_kernel, dim3(num_sms * 8), dim3(256), 0, stream, a);
+    if (a.src_dtype == kSrcUpGatePartials)
+        return launch_chained(pack_act_kernel<2>, dim3(num_sms * 8), dim3(256), 0, stream, a);
+    return launch_chained(pack_act_kernel<kPackKbPerTask>, dim3(num_sms * 8), dim3(256), 0, stream, a);
 }
 
 }  // namespace cst
