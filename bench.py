@@ -106,6 +106,27 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def upgate_traffic(bytes_per_launch: int):
+    """DRAM bytes of one decode up/gate launch: the traffic / algorithmic-bytes ratio that ncu
+    measured on a scaled config-2 case (profiles/grouped_ffn_config2_dram_traffic.md: the
+    weights stream once, so traffic grows with the experts a launch streams) times this
+    launch's algorithmic bytes.  None when the summary is missing."""
+    import re
+
+    f = REPO / "profiles" / "grouped_ffn_config2_dram_traffic.md"
+    try:
+        m = re.search(r"traffic_per_algorithmic_byte_upgate:\s*([0-9.]+)", f.read_text())
+    except OSError:
+        return None
+    if not m:
+        return None
+    return int(float(m.group(1)) * bytes_per_launch)
+
+
+TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of a 54-expert config-2 up/gate launch "
+                  "(traffic / algorithmic bytes = 1.0056), scaled by the experts this launch streams")
+
+
 def fp8_peak_tflops():
     """Dense FP8 tensor peak: twice the measured bf16 GEMM rate (the FP8 rate itself is not
     in the measured file; B200's FP8 dense rate is twice its bf16 rate), else nominal."""
@@ -496,7 +517,8 @@ def run_ours(args):
                      "bound": "hbm",
                      "achieved": round(ach_upg, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(ach_upg / peak, 4), "peak_source": peak_kind,
-                     "bytes_per_launch": upg_bytes, "ms_per_launch": round(upg_ms, 4), "traffic": None},
+                     "bytes_per_launch": upg_bytes, "ms_per_launch": round(upg_ms, 4),
+                     "traffic": upgate_traffic(upg_bytes), "traffic_source": TRAFFIC_SOURCE},
         "expert_matvec": {"kernels": "grouped up/gate + down", "bytes": pair_bytes,
                           "ms": round(upg_ms + dn_ms, 4), "achieved_gbs": round(ach_pair, 1),
                           "frac": round(ach_pair / peak, 4)},
@@ -853,7 +875,8 @@ def run_config1(args):
         "roofline": {"kernel": "grouped_ffn_tc up/gate (tcgen05 kind::f8f6f4, TMEM accumulators, TMA bulk ring)",
                      "bound": "hbm", "achieved": round(ach_upg, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(ach_upg / peak, 4), "peak_source": peak_kind,
-                     "bytes_per_launch": upg_bytes, "ms_per_launch": round(upg_ms, 4), "traffic": None},
+                     "bytes_per_launch": upg_bytes, "ms_per_launch": round(upg_ms, 4),
+                     "traffic": upgate_traffic(upg_bytes), "traffic_source": TRAFFIC_SOURCE},
         "expert_matvec": {"kernels": "grouped up/gate + down", "bytes": pair_bytes,
                           "ms": round(upg_ms + dn_ms, 4), "achieved_gbs": round(ach_pair, 1),
                           "frac": round(ach_pair / peak, 4)},
