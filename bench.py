@@ -65,6 +65,10 @@ def parse():
                    help="expert-parallel exchange: NCCL all-gather + reduce-scatter, NCCL all-to-all-v, or "
                         "NCCL all-gather + the combine pushed to the token owners over peer memory")
     p.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
+    p.add_argument("--replicate-hot", default="auto",
+                   help="expert parallelism: replicate the hottest experts on every rank, each rank serving "
+                        "them for its own tokens ('auto': chosen from a calibration batch for config4 at N>1, "
+                        "none otherwise; or a number of experts, 0 = none)")
     p.add_argument("--cpu-sample-tokens", type=int, default=2)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -290,13 +294,16 @@ def layer_parity(torch, moe, rank, world, dev, x_all, gw, gb, out_local, n_token
 
 
 # ---------------------------------------------------------------------------------------
-def setup_layer(torch, rank, world, T_total, dev, resident=E, zipf=False):
+MAX_REPLICAS = 32
+
+
+def setup_layer(torch, rank, world, T_total, dev, resident=E, zipf=False, spare_slots=0):
     from constellation_b200 import synthetic
     from constellation_b200.context import ExpertContext, MoEConfig
 
     cfg = MoEConfig()
     epr = E // world
-    ctx = ExpertContext(dev, cfg, n_slots=epr + 1, max_tokens=T_total)
+    ctx = ExpertContext(dev, cfg, n_slots=epr + 1 + spare_slots, max_tokens=T_total)
     for j in range(min(epr, resident)):
         e = rank * epr + j
         ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(e), device=dev)
@@ -314,6 +321,38 @@ def setup_layer(torch, rank, world, T_total, dev, resident=E, zipf=False):
     torch.cuda.synchronize(dev)
     torch.cuda.empty_cache()
     return ctx, gw, gb, x, x_all
+
+
+def place_replicas(torch, ctx, rank, world, T, dev, gw, gb, how):
+    """Hot-expert replicas for a skewed router: the experts to replicate come from a
+    calibration batch (other activations than the timed ones, same router), chosen by
+    ep.choose_replicas (or the N hottest for a number); each rank uploads the ones it does
+    not own into spare slots and serves all of them for its own tokens only."""
+    from constellation_b200 import ep, synthetic
+
+    calib = synthetic.make_activations(T, H, seed=synthetic.ACTIVATION_SEED + 100, device=dev)
+    idx, _ = ctx.route(calib, gw, gb)
+    idx = idx.cpu().numpy()
+    if how == "auto":
+        reps = ep.choose_replicas(idx, world, E, max_replicas=MAX_REPLICAS)
+    else:
+        import numpy as np
+
+        order = np.argsort(-np.bincount(idx.ravel(), minlength=E), kind="stable")
+        reps = sorted(int(e) for e in order[:min(int(how), MAX_REPLICAS)])
+    epr = E // world
+    spare = epr + 1
+    for e in reps:
+        if not rank * epr <= e < (rank + 1) * epr:
+            ex = synthetic.make_expert(H, I, seed=synthetic.expert_seed(e), device=dev)
+            ctx.upload_expert(spare, e, ex.w_up, ex.s_up, ex.w_gate, ex.s_gate, ex.w_down, ex.s_down)
+            spare += 1
+            del ex
+    for e in reps:
+        ctx.set_own_tokens_only(e)
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    return reps
 
 
 def touched_experts(torch, ctx, gw, gb, x_all, resident=E):
@@ -344,7 +383,11 @@ def run_ours(args):
         raise SystemExit(f"T={T} does not shard over {world} ranks")
     from constellation_b200.ep import ExpertParallelMoE
 
-    ctx, gw, gb, x, x_all = setup_layer(torch, rank, world, T, dev, args.resident_experts, zipf=prefill)
+    want_reps = world > 1 and args.ep_mode != "alltoall" and args.replicate_hot != "0" and \
+        (args.replicate_hot != "auto" or prefill)
+    ctx, gw, gb, x, x_all = setup_layer(torch, rank, world, T, dev, args.resident_experts, zipf=prefill,
+                                        spare_slots=MAX_REPLICAS if want_reps else 0)
+    replicas = place_replicas(torch, ctx, rank, world, T, dev, gw, gb, args.replicate_hot) if want_reps else []
     moe = ExpertParallelMoE(ctx, rank=rank, world=world, n_routed_experts=E, mode=args.ep_mode)
     out = torch.empty_like(x)
 
@@ -458,7 +501,12 @@ def run_ours(args):
     if world > 1:
         idx, _ = ctx.route(x_all, gw, gb)
         lo, hi = rank * (E // world), (rank + 1) * (E // world)
-        loc = idx[(idx >= lo) & (idx < hi)]
+        Tl = T // world
+        rep_mask = torch.zeros(E, dtype=torch.bool, device=dev)
+        rep_mask[list(replicas)] = True
+        own = idx[(idx >= lo) & (idx < hi) & ~rep_mask[idx.long()]]
+        mine = idx[rank * Tl:(rank + 1) * Tl]
+        loc = torch.cat([own, mine[rep_mask[mine.long()]]])
         U_local = int(torch.unique(loc).numel())
         rows = int(loc.numel())
         U_t = torch.tensor([U_local], device=dev)
@@ -550,7 +598,11 @@ def run_ours(args):
         line["tensor_util"] = {"flop_per_rank": flop_rank, "layer_tflops_per_gpu": round(tflops_layer, 1),
                                "frac_of_fp8_peak": round(tflops_layer / fp8_peak, 4),
                                "flop_whole_job": int((K + 1) * T * 3 * 2 * H * I)}
-        line["load_imbalance"] = {"rows_per_rank": rows_per_rank, "max_over_mean": round(imbalance, 3)}
+        line["load_imbalance"] = {"rows_per_rank": rows_per_rank, "max_over_mean": round(imbalance, 3),
+                                  "replicated_experts": replicas,
+                                  "replica_choice": "ep.choose_replicas on a calibration batch (activation "
+                                                    "seed + 100): fewest hottest experts with max/mean <= 1.1"
+                                  if replicas else None}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = cpu_reference_rate(args.cpu_sample_tokens, args.cpu_seconds, T=T, zipf=prefill)

@@ -35,7 +35,7 @@ EXPORTED = (
     "cst_route_noalloc", "cst_moe_routed_range", "cst_set_gemm_mode", "cst_rmsnorm",
     "cst_ipc_alloc", "cst_ipc_open", "cst_ipc_close", "cst_ipc_free", "cst_moe_routed_push", "cst_reduce_pushed",
     "cst_encode_infer_request", "cst_decode_infer_request", "cst_encode_infer_response", "cst_decode_infer_response",
-    "cst_serve_infer_request", "cst_gather_rows",
+    "cst_serve_infer_request", "cst_gather_rows", "cst_set_expert_own_tokens_only",
 )
 CST_INFER_REQUEST_FIXED_BYTES = 24
 CST_INFER_RESPONSE_FIXED_BYTES = 20
@@ -118,6 +118,7 @@ def _load() -> ctypes.CDLL:
         "cst_upload_expert": (ctypes.c_int, [P, I32, I32, ctypes.POINTER(CstExpertWeights), P]),
         "cst_free_expert": (ctypes.c_int, [P, I32]),
         "cst_find_slot": (I32, [P, I32]),
+        "cst_set_expert_own_tokens_only": (ctypes.c_int, [P, I32, I32]),
         "cst_set_shared_slot": (ctypes.c_int, [P, I32]),
         "cst_set_gemm_mode": (ctypes.c_int, [P, I32]),
         "cst_rmsnorm": (ctypes.c_int, [P, I32, I32, I32, P, ctypes.c_float, P, I32, P]),

@@ -182,6 +182,12 @@ class ExpertContext:
     def find_slot(self, expert_id: int) -> int:
         return int(_lib.lib.cst_find_slot(self.handle, int(expert_id)))
 
+    def set_own_tokens_only(self, expert_id: int, flag: bool = True) -> None:
+        """Serve resident expert ``expert_id`` for this rank's own tokens only (a replicated
+        hot expert under expert parallelism; ``cst_set_expert_own_tokens_only``)."""
+        with torch.cuda.device(self.device):
+            check(_lib.lib.cst_set_expert_own_tokens_only(self.handle, int(expert_id), int(bool(flag))))
+
     def find_shared_slot(self) -> int:
         """Arena slot of the shared expert (raises when none is resident)."""
         s = int(self.info().get("shared_slot", -1))

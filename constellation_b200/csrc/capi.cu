@@ -97,6 +97,8 @@ struct cst_ctx {
     uint8_t* staging = nullptr;        // 3 * I * H bytes for uploads
     int32_t* d_slot_of_expert = nullptr;
     std::vector<int32_t> slot_of_expert;  // router expert -> slot
+    std::vector<uint8_t> own_tokens_only;  // router expert -> served for this rank's own tokens only
+    std::vector<int32_t> slot_table;       // the device copy's staging: slot | kSlotOwnTokensOnly
     std::vector<int32_t> expert_of_slot;  // slot -> router expert, -1 shared, -2 empty
     int32_t shared_slot = -1;
     int max_rows = 0;
@@ -156,6 +158,18 @@ int ensure_device(const cst_ctx* c) {
     CST_CUDA(cudaGetDevice(&cur));
     if (cur != c->device) CST_CUDA(cudaSetDevice(c->device));
     return CST_OK;
+}
+
+// The device slot table: slot of each router expert (-1: not here), with kSlotOwnTokensOnly
+// set for experts served only for the tokens of this rank's shared-expert range.
+cudaError_t upload_slot_table(cst_ctx* c, cudaStream_t s) {
+    c->slot_table.resize(c->slot_of_expert.size());
+    for (size_t e = 0; e < c->slot_of_expert.size(); ++e) {
+        const int32_t v = c->slot_of_expert[e];
+        c->slot_table[e] = (v >= 0 && c->own_tokens_only[e]) ? (v | kSlotOwnTokensOnly) : v;
+    }
+    return cudaMemcpyAsync(c->d_slot_of_expert, c->slot_table.data(), c->slot_table.size() * 4,
+                           cudaMemcpyHostToDevice, s);
 }
 
 bool valid_dtype(int d) { return d == CST_DTYPE_FP16 || d == CST_DTYPE_BF16 || d == CST_DTYPE_FP32; }
@@ -368,6 +382,7 @@ int cst_create(int32_t device, const cst_config* cfg, cst_ctx** out) {
     }
     c->geo = ArenaGeom::make(f.hidden_dim, f.inter_dim);
     c->slot_of_expert.assign(f.n_routed_experts, -1);
+    c->own_tokens_only.assign(f.n_routed_experts, 0);
     c->expert_of_slot.assign(f.n_slots, -2);
     int rc = CST_OK;
     auto bail = [&](int code) {
@@ -462,8 +477,7 @@ int cst_upload_expert(cst_ctx* c, int32_t slot, int32_t expert_id, const cst_exp
         c->expert_of_slot[slot] = -1;
         c->shared_slot = slot;
     }
-    CST_CUDA(cudaMemcpyAsync(c->d_slot_of_expert, c->slot_of_expert.data(), c->slot_of_expert.size() * 4,
-                             cudaMemcpyHostToDevice, s));
+    CST_CUDA(upload_slot_table(c, s));
     // upload is a load-time path: finish it before the staging buffer is reused
     CST_CUDA(cudaStreamSynchronize(s));
     return CST_OK;
@@ -479,8 +493,21 @@ int cst_free_expert(cst_ctx* c, int32_t slot) {
     if (c->shared_slot == slot) c->shared_slot = -1;
     c->expert_of_slot[slot] = -2;
     CST_CUDA(cudaDeviceSynchronize());
-    CST_CUDA(cudaMemcpy(c->d_slot_of_expert, c->slot_of_expert.data(), c->slot_of_expert.size() * 4,
-                        cudaMemcpyHostToDevice));
+    CST_CUDA(upload_slot_table(c, nullptr));
+    CST_CUDA(cudaDeviceSynchronize());
+    return CST_OK;
+}
+
+int cst_set_expert_own_tokens_only(cst_ctx* c, int32_t expert_id, int32_t own_tokens_only) {
+    g_last_error.clear();
+    if (int rc = check_ctx(c)) return rc;
+    if (expert_id < 0 || expert_id >= c->cfg.n_routed_experts)
+        return fail(CST_ERR_UNKNOWN_EXPERT, "expert_id %d out of [0, %d)", expert_id, c->cfg.n_routed_experts);
+    if (int rc = ensure_device(c)) return rc;
+    c->own_tokens_only[expert_id] = own_tokens_only ? 1 : 0;
+    CST_CUDA(cudaDeviceSynchronize());
+    CST_CUDA(upload_slot_table(c, nullptr));
+    CST_CUDA(cudaDeviceSynchronize());
     return CST_OK;
 }
 

@@ -62,6 +62,10 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
                           int* err, cudaStream_t stream, bool allow_tc = true, float* logits_out = nullptr);
 
 // route_pack.cu
+// A slot-table entry with this bit set is an expert served only for the tokens of the call's
+// own-token range (shared_t_begin..shared_t_end): a replica of a hot expert that every rank
+// holds and applies to its own tokens alone.
+constexpr int32_t kSlotOwnTokensOnly = int32_t(1) << 30;
 struct PackArgs {
     // mode A (routes): topk_idx/topk_w [T, K]; slot_of_expert [E]
     const int32_t* topk_idx;

@@ -73,6 +73,10 @@ __device__ __forceinline__ int route_slot(const PackArgs& a, bool mode_rows, int
         if (*k < a.K) {
             const int e = a.topk_idx[*t * a.K + *k];
             slot = (e >= 0 && e < a.E) ? a.slot_of_expert[e] : -1;
+            if (slot >= 0 && (slot & kSlotOwnTokensOnly)) {
+                // a replicated expert: this rank serves it for its own tokens only
+                slot = (*t >= a.shared_t_begin && *t < a.shared_t_end) ? (slot & ~kSlotOwnTokensOnly) : -1;
+            }
         } else {
             slot = (*t >= a.shared_t_begin && *t < a.shared_t_end) ? a.shared_slot : -1;
         }

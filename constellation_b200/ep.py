@@ -32,8 +32,17 @@ Three exchange strategies, all deterministic and all behind ``ExpertParallelMoE.
     outputs back (``:780-790``) and combine at the source in fixed k order.  The split
     sizes must reach the host (NCCL takes host counts), which costs one device sync.
 
-The communication plan (``plan_dispatch``) is plain torch and runs on any device, so the
-multi-rank host logic is tested on CPU with the gloo backend.
+Hot-expert replicas (``all-gather`` and ``p2p`` modes).  With a skewed router (a prefill
+chunk whose bias favours a few experts) the owners of the hot experts get most of the rows
+and the step waits for them.  ``choose_replicas`` picks, from a calibration batch's routes,
+the fewest hottest experts whose replication brings the busiest rank within ``target`` of
+the mean; every rank then holds a copy of each and serves it for its OWN tokens only
+(``ExpertContext.set_own_tokens_only``), while every other expert keeps its single owner.
+Each (token, expert) row is still computed exactly once, by the same kernels, so the layer's
+output is unchanged.
+
+The communication plan (``plan_dispatch``) and the replica choice are plain torch / numpy
+and run on any device, so the multi-rank host logic is tested on CPU with the gloo backend.
 """
 from __future__ import annotations
 
@@ -41,6 +50,48 @@ from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
+
+
+def rows_per_rank(topk_idx, world: int, n_experts: int, replicas=(), shared: bool = True) -> list[int]:
+    """Packed rows each rank computes for a gathered batch ``topk_idx`` ([T, K], rank-major
+    token shards): its own experts' routes from every token, the replicated experts' routes
+    from its own tokens, plus one shared-expert row per own token."""
+    import numpy as np
+
+    idx = np.asarray(topk_idx)
+    T = idx.shape[0]
+    tl, epr = T // world, n_experts // world
+    rep = np.zeros(n_experts, dtype=bool)
+    rep[list(replicas)] = True
+    owner = np.arange(n_experts) // epr
+    out = []
+    for r in range(world):
+        own = (owner == r) & ~rep
+        rows = int(own[idx].sum()) + int(rep[idx[r * tl:(r + 1) * tl]].sum())
+        out.append(rows + (tl if shared else 0))
+    return out
+
+
+def choose_replicas(calib_topk_idx, world: int, n_experts: int, *, target: float = 1.1,
+                    max_replicas: int = 32) -> list[int]:
+    """The fewest hottest experts (by routes in the calibration batch) whose replication on
+    every rank brings the busiest rank's rows within ``target`` x the mean (or the best of
+    up to ``max_replicas``)."""
+    import numpy as np
+
+    idx = np.asarray(calib_topk_idx)
+    if world <= 1:
+        return []
+    order = np.argsort(-np.bincount(idx.ravel(), minlength=n_experts), kind="stable")
+    best, best_r = None, 0
+    for r in range(0, max_replicas + 1):
+        rows = rows_per_rank(idx, world, n_experts, order[:r].tolist())
+        imb = max(rows) / (sum(rows) / len(rows))
+        if best is None or imb < best - 1e-9:
+            best, best_r = imb, r
+        if imb <= target:
+            return sorted(int(e) for e in order[:r])
+    return sorted(int(e) for e in order[:best_r])
 
 
 @dataclass

@@ -114,6 +114,16 @@ int cst_free_expert(cst_ctx* ctx, int32_t slot);
  * expert_node_v2/expert_registry_v2.cc:437). */
 int32_t cst_find_slot(const cst_ctx* ctx, int32_t expert_id);
 
+/* Marks resident router expert `expert_id` as served for this rank's own tokens only (1) or
+ * for every token routed to it (0, the default).  Expert parallelism gives each expert one
+ * owner rank, which serves it for all gathered tokens; a hot expert replicated on every rank
+ * and marked here is instead applied by each rank to the tokens it owns (the shared expert's
+ * token range of cst_moe_routed_range / cst_moe_routed_push; every token in cst_moe_layer),
+ * which spreads its rows over the ranks.  No counterpart in the reference (its coordinator
+ * places one replica per expert, server/expert_placement.py).  Load-time call: it
+ * synchronises the device. */
+int cst_set_expert_own_tokens_only(cst_ctx* ctx, int32_t expert_id, int32_t own_tokens_only);
+
 /* Marks `slot` as the shared expert (-1: none). */
 int cst_set_shared_slot(cst_ctx* ctx, int32_t slot);
 

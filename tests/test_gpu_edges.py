@@ -108,3 +108,45 @@ def test_max_tokens_is_inclusive(dev):
     with pytest.raises(CstError) as ei:
         ctx.moe_layer(x9, torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev))
     assert ei.value.code == CST_ERR_INVALID_ARG
+
+
+def test_own_tokens_only_experts_serve_the_own_range():
+    """Experts marked own-tokens-only (replicated hot experts under expert parallelism) get
+    rows only for tokens inside the call's own-token range, like the shared expert; the
+    others serve every token.  Checked through cst_moe_routed_range against the oracle's
+    per-route outputs, and unmarking restores the full layer."""
+    T, lo, hi = 24, 6, 15
+    ctx, w, b, de, sh = setup(dev_or_skip(), 360, T)
+    dev = ctx.device
+    x = cases.activations(361, T, H)
+    xt = torch.from_numpy(x).to(dev, torch.bfloat16)
+    idx, wts = ctx.route(xt, torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev))
+    marked = (0, 3, 9)
+    for e in marked:
+        ctx.set_own_tokens_only(e)
+    out = ctx.moe_routed_range(xt, idx, wts, lo, hi, out_dtype=torch.float32).cpu().numpy()
+    xb = xt.float().cpu().numpy()
+    ih, wh = idx.cpu().numpy(), wts.cpu().numpy()
+    ref = np.zeros((T, H), np.float32)
+    for t in range(T):
+        inside = lo <= t < hi
+        for k in range(K):
+            e = int(ih[t, k])
+            if e in marked and not inside:
+                continue
+            ref[t] += wh[t, k] * de[e].forward(xb[t:t + 1])[0]
+        if inside:
+            ref[t] += sh.forward(xb[t:t + 1])[0]
+    rel = np.abs(out - ref).max(axis=1) / np.maximum(np.abs(ref).max(axis=1), 1e-30)
+    assert float(rel.max()) < 2e-3, rel
+    for e in marked:
+        ctx.set_own_tokens_only(e, False)
+    full = ctx.moe_routed_range(xt, idx, wts, 0, T, out_dtype=torch.float32)
+    lay = ctx.moe_layer(xt, torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev), out_dtype=torch.float32)
+    assert torch.equal(full, lay)
+
+
+def dev_or_skip():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)

@@ -44,7 +44,7 @@ def _rank_main(rank, world, port, q):
         cfg = MoEConfig(hidden_size=H, moe_intermediate_size=I, n_routed_experts=E, n_group=G, topk_group=TG,
                         num_experts_per_tok=K)
         epr = E // world
-        ctx = ExpertContext(dev, cfg, n_slots=epr + 1, max_tokens=T)
+        ctx = ExpertContext(dev, cfg, n_slots=epr + 3, max_tokens=T)
         for j in range(epr):
             e = rank * epr + j
             ctx.upload_bundle(j, e, cases.expert(3000 + e, H, I))
@@ -55,15 +55,24 @@ def _rank_main(rank, world, port, q):
         Tl = T // world
         xl = x[rank * Tl:(rank + 1) * Tl].contiguous()
         res = {}
-        for mode in ("allgather", "allgather_local", "alltoall", "p2p"):
+        for mode in ("allgather", "allgather_local", "alltoall", "p2p", "p2p_replicated", "allgather_replicated"):
+            if mode == "p2p_replicated":
+                # experts 1 and E-2 replicated on every rank (the copies go to spare slots) and
+                # served by each rank for its own tokens only: the same rows, spread differently
+                reps = [e for e in (1, E - 2) if not (rank * epr <= e < (rank + 1) * epr)]
+                for j, e in enumerate(reps):
+                    ctx.upload_bundle(epr + 1 + j, e, cases.expert(3000 + e, H, I))
+                for e in (1, E - 2):
+                    ctx.set_own_tokens_only(e, True)
+            base_mode = mode.split("_")[0]
             # allgather_local: own-token routing + gathered routes (the prefill-sized path)
             local = mode == "allgather_local"
             moe = ExpertParallelMoE(ctx, rank=rank, world=world, n_routed_experts=E,
-                                    mode="allgather" if local else mode, local_route_min=1 if local else 128)
+                                    mode=base_mode, local_route_min=1 if local else 128)
             res[mode] = moe.forward(xl, gw, gb, out_dtype=torch.float32).cpu().numpy()
-            if mode == "p2p":
+            if base_mode == "p2p":
                 # a second exchange through the same buffers (epoch 2), then release them
-                res["p2p_again"] = moe.forward(xl, gw, gb, out_dtype=torch.float32).cpu().numpy()
+                res[mode + "_again"] = moe.forward(xl, gw, gb, out_dtype=torch.float32).cpu().numpy()
                 torch.cuda.synchronize()
                 dist.barrier()
                 moe.close()
@@ -104,7 +113,8 @@ def test_ep_two_gpus_both_modes():
     x = cases.activations(82, T, H)
     ref = moe_layer(x, w, b, {e: DequantExpert(cases.expert(3000 + e, H, I)) for e in range(E)},
                     DequantExpert(cases.expert(3999, H, I)), n_group=G, topk_group=TG, top_k=K)
-    for mode in ("allgather", "allgather_local", "alltoall", "p2p", "p2p_again"):
+    for mode in ("allgather", "allgather_local", "alltoall", "p2p", "p2p_again", "p2p_replicated",
+                 "p2p_replicated_again", "allgather_replicated"):
         out = np.concatenate([got[r][mode] for r in range(world)])
         num = np.abs(out - ref.out_f32).max(axis=1)
         den = np.abs(ref.out_f32).max(axis=1)

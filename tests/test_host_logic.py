@@ -105,3 +105,25 @@ def test_moe_config_from_the_reference_router_config():
         MoEConfig.from_router_config({**rc, "scoring_func": "softmax"}, inter=2048)
     with pytest.raises(RuntimeError, match="topk_method"):
         MoEConfig.from_router_config({**rc, "topk_method": "greedy"}, inter=2048)
+
+
+def test_replica_choice_balances_skewed_routes():
+    """choose_replicas / rows_per_rank (constellation_b200.ep): a Zipf-like route skew that
+    loads one rank, balanced by replicating the hot experts; each row counted exactly once."""
+    import numpy as np
+
+    from constellation_b200 import ep
+
+    rng = np.random.default_rng(7)
+    W, E, T, K = 4, 32, 256, 4
+    p = 1.0 / np.arange(1, E + 1) ** 1.5
+    idx = np.stack([rng.choice(E, size=K, replace=False, p=p / p.sum()) for _ in range(T)])
+    base = ep.rows_per_rank(idx, W, E)
+    assert sum(base) == T * K + T  # every route plus one shared row per token
+    assert max(base) / (sum(base) / W) > 1.5  # experts 0-7 all live on rank 0
+    reps = ep.choose_replicas(idx, W, E, target=1.1)
+    bal = ep.rows_per_rank(idx, W, E, reps)
+    assert sum(bal) == sum(base)
+    assert max(bal) / (sum(bal) / W) <= 1.1
+    assert reps == sorted(reps) and 0 in reps
+    assert ep.choose_replicas(idx, 1, E) == []
