@@ -106,12 +106,24 @@ __global__ void __launch_bounds__(kLWarps * 32) router_logits_kernel(const TX* _
     for (int t = 0; t < kLT; ++t) xr[t] = x + int64_t(min(t0 + t, T - 1)) * H;
 #pragma unroll
     for (int e = 0; e < kLE; ++e) wr[e] = w + int64_t(min(e0 + e, E - 1)) * H;
-    for (int k = k_begin + 4 * lane; k < k_end; k += 128) {
-        float4 wv[kLE], xv[kLT];
+    // software-pipelined: the loads of the next 128-column step are issued before the FMAs
+    // of this one, so a warp waits for one memory latency per two steps (the summation
+    // order per lane is unchanged)
+    float4 wv[kLE], xv[kLT];
+    int k = k_begin + 4 * lane;
+    if (k < k_end) {
 #pragma unroll
         for (int e = 0; e < kLE; ++e) wv[e] = __ldg(reinterpret_cast<const float4*>(wr[e] + k));
 #pragma unroll
         for (int t = 0; t < kLT; ++t) xv[t] = load4x<TX>(xr[t], k);
+    }
+    for (; k < k_end; k += 128) {
+        float4 wn[kLE], xn[kLT];
+        const int kn = k + 128 < k_end ? k + 128 : k;  // the last step reloads its own columns
+#pragma unroll
+        for (int e = 0; e < kLE; ++e) wn[e] = __ldg(reinterpret_cast<const float4*>(wr[e] + kn));
+#pragma unroll
+        for (int t = 0; t < kLT; ++t) xn[t] = load4x<TX>(xr[t], kn);
 #pragma unroll
         for (int t = 0; t < kLT; ++t) {
 #pragma unroll
@@ -124,6 +136,10 @@ __global__ void __launch_bounds__(kLWarps * 32) router_logits_kernel(const TX* _
                 acc[t * kLE + e] = a;
             }
         }
+#pragma unroll
+        for (int e = 0; e < kLE; ++e) wv[e] = wn[e];
+#pragma unroll
+        for (int t = 0; t < kLT; ++t) xv[t] = xn[t];
     }
     reduce_half<64>(acc, 16, lane);
     reduce_half<32>(acc, 8, lane);
