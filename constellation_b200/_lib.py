@@ -91,7 +91,8 @@ class CstPeerSet(ctypes.Structure):
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("tl", ctypes.c_int32),
                 ("tl_cap", ctypes.c_int32), ("recv", ctypes.c_void_p * CST_MAX_PEERS),
                 ("flags", ctypes.c_void_p * CST_MAX_PEERS), ("epoch", ctypes.c_void_p), ("done", ctypes.c_void_p),
-                ("x_offset", ctypes.c_int64), ("gather_epoch", ctypes.c_void_p)]
+                ("x_offset", ctypes.c_int64), ("gather_epoch", ctypes.c_void_p),
+                ("presence_offset", ctypes.c_int64)]
 
 
 class CstInferRequest(ctypes.Structure):

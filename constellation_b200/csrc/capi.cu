@@ -613,6 +613,10 @@ static int peer_set_from(const cst_peer_set* p, PeerSet* out) {
                     static_cast<long long>(p->x_offset));
     q.x_off = p->x_offset;
     q.gather_epoch = p->gather_epoch;
+    if (p->presence_offset < 0 || p->presence_offset % 16)
+        return fail(CST_ERR_INVALID_ARG, "peer set: bad presence offset %lld",
+                    static_cast<long long>(p->presence_offset));
+    q.pres_off = p->presence_offset;
     *out = q;
     return CST_OK;
 }

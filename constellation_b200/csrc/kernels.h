@@ -180,6 +180,8 @@ struct PeerSet {
     int32_t* done;               // reserved
     int64_t x_off;               // byte offset of the gathered-row slots from recv[q] (0: none)
     int32_t* gather_epoch;       // this rank's gather counter
+    int64_t pres_off;            // byte offset of the presence words [world][tl_cap] from recv[q]
+                                 // (0: none -- every partial is pushed and added)
 };
 // Gathered-row exchange: arrival counters at flags[q] + kGatherFlags
 constexpr int kGatherFlags = 8;

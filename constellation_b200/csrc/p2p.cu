@@ -68,10 +68,19 @@ __global__ void __launch_bounds__(256) combine_push_kernel(PushArgs a) {
     const int i0 = (blockIdx.x - q * nblk) * kPushTok;
     const int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
     float* dst = a.peers.recv[q] + int64_t(a.peers.rank) * a.peers.tl_cap * a.H;
-    if (h < a.H) {
-        for (int i = i0; i < min(a.tl, i0 + kPushTok); ++i) {
-            const int t = q * a.tl + i;
-            const int32_t* rows = a.tk_row + int64_t(t) * a.K1;
+    // presence words of this rank in q's buffer: a token with no row here is not pushed
+    int32_t* pres = a.peers.pres_off
+                        ? reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(a.peers.recv[q]) + a.peers.pres_off) +
+                              int64_t(a.peers.rank) * a.peers.tl_cap
+                        : nullptr;
+    for (int i = i0; i < min(a.tl, i0 + kPushTok); ++i) {
+        const int t = q * a.tl + i;
+        const int32_t* rows = a.tk_row + int64_t(t) * a.K1;
+        bool present = pres == nullptr;
+        for (int k = 0; k < a.K1 && !present; ++k) present = __ldg(rows + k) >= 0;
+        if (pres != nullptr && blockIdx.y == 0 && threadIdx.x == 0) pres[i] = present ? 1 : 0;
+        if (!present || h >= a.H) continue;
+        {
             float4 v[16];
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
@@ -202,10 +211,14 @@ __global__ void __launch_bounds__(256) reduce_cast_kernel(ReduceArgs a) {
     __syncthreads();
     __threadfence();
     const float* recv = a.peers.recv[a.peers.rank];
+    const int32_t* pres =
+        a.peers.pres_off ? reinterpret_cast<const int32_t*>(reinterpret_cast<const uint8_t*>(recv) + a.peers.pres_off)
+                         : nullptr;
     for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < a.H; h += gridDim.y * blockDim.x * 4) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         if (s_ok) {
             for (int r = 0; r < a.peers.world; ++r) {  // rank order
+                if (pres != nullptr && pres[int64_t(r) * a.peers.tl_cap + t] == 0) continue;  // nothing pushed
                 const float4 v =
                     *reinterpret_cast<const float4*>(recv + (int64_t(r) * a.peers.tl_cap + t) * a.H + h);
                 acc.x += v.x;

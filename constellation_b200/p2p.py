@@ -7,7 +7,10 @@ Each rank allocates one device buffer through ``cst_ipc_alloc``:
 * ``world * tl_cap`` gathered rows of ``hidden`` 2-byte elements (the all-gather of the
   tokens, rank-major);
 * 64 int32: combine arrival counters at [0, world), gather arrival counters at [8, 8 +
-  world), the combine epoch at [32], a reserved word at [33], the gather epoch at [34].
+  world), the combine epoch at [32], a reserved word at [33], the gather epoch at [34];
+* ``world * tl_cap`` presence words (int32): rank r writes 0 for a token of this rank it
+  has no row for and pushes nothing for it; the reduce skips that slot (at a decode batch
+  about a third of the (rank, token) partials are empty, at a skewed prefill most are).
 
 The ranks swap the CUDA IPC handles with one all-gather, so every rank maps every other
 rank's buffer.  ``cst_gather_rows`` stores each rank's rows into every rank's gathered
@@ -43,7 +46,9 @@ class PeerExchange:
         self.x_off = self.slot_bytes
         self.x_bytes = self.world * self.tl_cap * self.hidden * 2
         self.tail_off = self.x_off + self.x_bytes
-        nbytes = self.tail_off + _TAIL_INTS * 4
+        # presence words [world][tl_cap]: a rank with no row for a token pushes only a 0 here
+        self.pres_off = self.tail_off + _TAIL_INTS * 4
+        nbytes = self.pres_off + self.world * self.tl_cap * 4
         own = ctypes.c_void_p()
         handle = CstIpcHandle()
         with torch.cuda.device(self.device):
@@ -85,6 +90,7 @@ class PeerExchange:
         ps.done = tail + 33 * 4
         ps.x_offset = self.x_off
         ps.gather_epoch = tail + 34 * 4
+        ps.presence_offset = self.pres_off
         return ps
 
     def gathered(self, tl: int, dtype: torch.dtype) -> torch.Tensor:

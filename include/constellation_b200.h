@@ -282,6 +282,10 @@ typedef struct {
                              * [world * tl_cap, hidden] 2-byte rows; 0: none (cst_gather_rows) */
     int32_t* gather_epoch;  /* this rank's gather counter (zeroed int32); gather arrival counters
                              * are flags[q][8 + r] */
+    int64_t presence_offset; /* byte offset from recv[q] of rank q's presence words
+                              * [world][tl_cap] int32 (16-byte aligned), or 0: with it, a rank
+                              * that has no row for a token pushes no partial for it, only a 0
+                              * presence word, and the owner skips that rank's slot */
 } cst_peer_set;
 
 /* The all-gather of the expert-parallel exchange over peer memory: this rank's tl rows of x

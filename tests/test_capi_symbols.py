@@ -92,7 +92,8 @@ def test_peer_set_layout_matches_the_header():
     assert CstPeerSet.epoch.offset == 16 + 2 * CST_MAX_PEERS * P
     assert CstPeerSet.x_offset.offset == 16 + (2 * CST_MAX_PEERS + 2) * P
     assert CstPeerSet.gather_epoch.offset == 16 + (2 * CST_MAX_PEERS + 2) * P + 8
-    assert ctypes.sizeof(CstPeerSet) == 16 + (2 * CST_MAX_PEERS + 3) * P + 8
+    assert CstPeerSet.presence_offset.offset == 16 + (2 * CST_MAX_PEERS + 3) * P + 8
+    assert ctypes.sizeof(CstPeerSet) == 16 + (2 * CST_MAX_PEERS + 3) * P + 16
     assert ctypes.sizeof(CstIpcHandle) == 64
     hdr = (Path(__file__).resolve().parents[1] / "include" / "constellation_b200.h").read_text()
     assert f"#define CST_MAX_PEERS {CST_MAX_PEERS}" in hdr

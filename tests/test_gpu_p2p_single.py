@@ -168,3 +168,38 @@ def test_gather_rows_across_counter_wrap_and_timeout(layer, dev):
     with pytest.raises(CstError):
         ctx.device_error()
     ctx.device_error()  # cleared
+
+
+def test_push_skips_tokens_without_rows_here(dev):
+    """With presence words, a rank pushes nothing for a token it has no row for (only a 0
+    word) and the owner adds only the present slots: here only experts 0-3 are resident and
+    there is no shared expert, so most tokens have no row; the exchange must still equal the
+    fused single-GPU layer, and a token without rows gets exactly its residual."""
+    from constellation_b200.context import ExpertContext, MoEConfig
+
+    cfg = MoEConfig(hidden_size=H, moe_intermediate_size=I, n_routed_experts=E, n_group=G, topk_group=TG,
+                    num_experts_per_tok=K)
+    x = cases.activations(411, T, H)
+    w, b = cases.router(411, E, H, bias_std=0.05)
+    res = cases.activations(412, T, H)
+    ctx = ExpertContext(dev, cfg, n_slots=4, max_tokens=T)
+    for e in range(4):
+        ctx.upload_bundle(e, e, cases.expert(41100 + e, H, I))
+    xt = torch.from_numpy(x).to(dev, torch.bfloat16)
+    wt, bt = torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev)
+    rt = torch.from_numpy(res).to(dev)
+    pres_off = (TAIL + 64) * 4
+    buf = torch.zeros(TAIL + 64 + T, dtype=torch.int32, device=dev)
+    buf[TAIL + 64:] = 7  # stale words from an earlier exchange
+    buf[:T * H] = torch.full((T * H,), 1.0, device=dev).view(torch.int32)  # stale partials
+    ps = peer_set(buf)
+    ps.presence_offset = pres_off
+    got = exchange(ctx, xt, wt, bt, rt, ps)
+    ctx.device_error()
+    idx, _ = ctx.route(xt, wt, bt)
+    present = (idx < 4).any(dim=1)
+    assert 0 < int(present.sum()) < T  # both kinds of token occur
+    assert torch.equal(buf[TAIL + 64:].bool(), present)
+    fused = ctx.moe_layer(xt, wt, bt, out_dtype=torch.float32) + rt
+    torch.testing.assert_close(got, fused, rtol=1e-5, atol=1e-5)
+    assert torch.equal(got[~present], rt[~present])
