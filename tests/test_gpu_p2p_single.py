@@ -200,6 +200,6 @@ def test_push_skips_tokens_without_rows_here(dev):
     present = (idx < 4).any(dim=1)
     assert 0 < int(present.sum()) < T  # both kinds of token occur
     assert torch.equal(buf[TAIL + 64:].bool(), present)
-    fused = ctx.moe_layer(xt, wt, bt, out_dtype=torch.float32) + rt
+    fused = ctx.moe_layer(xt, wt, bt, add_shared=False, out_dtype=torch.float32) + rt
     torch.testing.assert_close(got, fused, rtol=1e-5, atol=1e-5)
     assert torch.equal(got[~present], rt[~present])
