@@ -223,6 +223,26 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
     return __half2float(__half(h));
 }
 
+// Two floats -> two E4M3 bytes in one conversion, `lo` in bits 0..7 (as e4m3_rn each).
+__device__ __forceinline__ uint32_t e4m3x2_rn(float lo, float hi) {
+    return __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
+}
+
+// The two E4M3 bytes in bits 0..15 of b2 as floats, exactly; .x is bits 0..7.
+__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t b2) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(b2), __NV_E4M3);
+    return __half22float2(__half2(h));
+}
+
+// Warp maximum of non-negative values in one reduction: the bit patterns of non-negative
+// floats order as unsigned integers.  A NaN lane counts as 0, so the result is fmaxf's over
+// the other lanes (0 when every lane is NaN, where fmaxf gives NaN; pow2_scale_for maps
+// both to 1).
+__device__ __forceinline__ float warp_max_nonneg(float a) {
+    const uint32_t u = (a == a) ? __float_as_uint(a) : 0u;
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, u));
+}
+
 // Smallest power of two s with amax / s <= 448 (s = 1 for amax == 0).  Returns s.
 __device__ __forceinline__ float pow2_scale_for(float amax) {
     if (!(amax > 0.0f)) return 1.0f;
@@ -235,6 +255,13 @@ __device__ __forceinline__ float pow2_scale_for(float amax) {
     if (mant != 0) e += 0x00800000u;
     if (e >= 0x7F800000u) e = 0x7F000000u;
     return __uint_as_float(e);
+}
+
+// 1 / s, exactly, for a power of two s from pow2_scale_for (2^-126 .. 2^127): the exponent
+// reflected about 2^0 (2^-127, a subnormal, for s = 2^127).
+__device__ __forceinline__ float pow2_recip(float s) {
+    const uint32_t b = __float_as_uint(s);
+    return b >= 0x7F000000u ? __uint_as_float(0x00400000u) : __uint_as_float(0x7F000000u - b);
 }
 
 __device__ __forceinline__ float warp_max(float v) {

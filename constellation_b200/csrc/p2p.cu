@@ -73,18 +73,30 @@ __global__ void __launch_bounds__(256) combine_push_kernel(PushArgs a) {
                         ? reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(a.peers.recv[q]) + a.peers.pres_off) +
                               int64_t(a.peers.rank) * a.peers.tl_cap
                         : nullptr;
-    for (int i = i0; i < min(a.tl, i0 + kPushTok); ++i) {
-        const int t = q * a.tl + i;
-        const int32_t* rows = a.tk_row + int64_t(t) * a.K1;
+    const int i_end = min(a.tl, i0 + kPushTok);
+    // a token's row indices are loaded together, the next token's while this one is summed
+    int nxt[16];
+    auto load_rows = [&](int i, int (&r)[16]) {
+        const int32_t* rows = a.tk_row + int64_t(q * a.tl + i) * a.K1;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) r[k] = (k < a.K1) ? __ldg(rows + k) : -1;
+    };
+    if (i0 < i_end) load_rows(i0, nxt);
+    for (int i = i0; i < i_end; ++i) {
+        int rw[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) rw[k] = nxt[k];
+        if (i + 1 < i_end) load_rows(i + 1, nxt);
         bool present = pres == nullptr;
-        for (int k = 0; k < a.K1 && !present; ++k) present = __ldg(rows + k) >= 0;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) present |= rw[k] >= 0;
         if (pres != nullptr && blockIdx.y == 0 && threadIdx.x == 0) pres[i] = present ? 1 : 0;
         if (!present || h >= a.H) continue;
         {
             float4 v[16];
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
-                const int r = (k < a.K1) ? __ldg(rows + k) : -1;
+                const int r = rw[k];
                 v[k] = (r >= 0) ? __ldg(reinterpret_cast<const float4*>(a.y + int64_t(r) * a.ldy + h))
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             }

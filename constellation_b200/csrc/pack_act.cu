@@ -22,6 +22,11 @@
 // One warp per (packed row, 8 consecutive K blocks): the row's metadata is read once and
 // the 8 source loads are issued together; per K block 128 elements, 4 per lane, one 32-bit
 // store per term.  Rows of a group's last n-tile beyond its row count are not written.
+// The tasks run over the packed rows themselves (0 .. meta->n_rows, contiguous in group
+// order): every CTA first copies the groups' first rows to shared memory and finds a
+// row's group there by binary search, so no warp spends a task on an unused tile column
+// (at decode most columns of the 8-wide n-tiles are), and the grid is the CTAs that fit
+// on the GPU at once, so every task starts in the first wave.
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -77,44 +82,58 @@ __device__ __forceinline__ void load4(const PackActArgs& a, int64_t src_row, int
 }
 
 constexpr int kPackKbPerTask = 8;  // K blocks one warp packs for one row (at most)
+constexpr int kPackSmemGroups = 4096;  // groups whose first rows a CTA keeps in shared memory
+
+// Group of packed row `prow`: the last g with row_start[g] <= prow (groups hold >= 1 row
+// each and start in increasing row order).  From shared memory when the CTA staged the
+// groups, else from the group records themselves.
+__device__ __forceinline__ int group_of_row(const int32_t* s_rs, const GroupRec* groups, int n_groups, int prow) {
+    int lo = 0, hi = n_groups - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        const int rs = s_rs ? s_rs[mid] : groups[mid].row_start;
+        if (rs <= prow) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
 
 // KBPT: K blocks one warp packs for one row (x rows: 8; split partials, which read up to 8
 // loads per element: 2, so more warps are in flight)
 template <int KBPT>
 __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
+    __shared__ int32_t s_rs[kPackSmemGroups];
     chain_wait();
     chain_release();
     const int KB = a.K / kBlock;
-    const int kbpt = KBPT;
-    const int n_chunks = (KB + kbpt - 1) / kbpt;
-    const int n_tiles = a.meta->n_tiles;
+    const int n_chunks = (KB + KBPT - 1) / KBPT;
+    const int n_rows = a.meta->n_rows;
+    const int n_groups = a.meta->n_groups;
+    const bool staged = n_groups <= kPackSmemGroups;
+    if (staged)
+        for (int g = threadIdx.x; g < n_groups; g += blockDim.x) s_rs[g] = a.groups[g].row_start;
+    __syncthreads();
     const int split = a.src_dtype == kSrcUpGatePartials ? a.meta->split_k : 1;
     const int lane = threadIdx.x & 31;
-    const int64_t n_tasks = int64_t(n_tiles) * kTileCols * n_chunks;
+    const int64_t n_tasks = int64_t(n_rows) * n_chunks;
     const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
     for (int64_t task = warp_global; task < n_tasks; task += n_warps) {
-        // task = (n-tile, token column j, chunk of 8 K blocks); the row metadata is read once
-        const int chunk = static_cast<int>(task % n_chunks);
-        const int64_t tr = task / n_chunks;
-        const int tile = static_cast<int>(tr / kTileCols);
-        const int j = static_cast<int>(tr % kTileCols);
-        const int gi = a.tile_group[tile];
-        const GroupRec gr = a.groups[gi];
-        const int nt = tile - gr.tile_base;
-        const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
-        const int r = nt * kTileCols + j;
-        // columns of a group's last n-tile beyond its rows are left as they are: each feeds
-        // only its own accumulator column, which the grouped kernel never reads
-        if (r >= gr.n_rows) continue;
-        const int prow = gr.row_start + r;
+        // task = (packed row, chunk of KBPT K blocks)
+        const int prow = static_cast<int>(task / n_chunks);
+        const int chunk = static_cast<int>(task - int64_t(prow) * n_chunks);
         const int64_t src_row = a.row_map ? a.row_map[prow] : prow;
-        const int kb0 = chunk * kbpt;
+        const GroupRec gr = a.groups[group_of_row(staged ? s_rs : nullptr, a.groups, n_groups, prow)];
+        const int r = prow - gr.row_start;
+        const int nt = r / kTileCols;
+        const int j = r - nt * kTileCols;
+        const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
+        const int kb0 = chunk * KBPT;
         // all source loads of the chunk first
         float v[KBPT][4];
 #pragma unroll
         for (int i = 0; i < KBPT; ++i) {
-            if (i < kbpt && kb0 + i < KB) {
+            if (kb0 + i < KB) {
                 load4(a, src_row, (kb0 + i) * kBlock + 4 * lane, split, v[i]);
             } else {
                 v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.0f;
@@ -126,56 +145,38 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
         // Term sp carries the residual of the terms before it, scaled by its own power of two
         // fitted to the block's largest residual: a large element then limits the resolution
         // of the small ones in its block only through the first term.  The task's K blocks are
-        // independent, so each term's block maxima of all of them are reduced side by side.
-        uint32_t q[KBPT][kSplits];
-        float sc[KBPT][kSplits];
+        // independent, so each term's block maxima of all of them are reduced side by side,
+        // and each term is stored as soon as it is known.
 #pragma unroll
         for (int sp = 0; sp < kSplits; ++sp) {
             if (sp >= a.terms) break;
             float m[KBPT];
 #pragma unroll
             for (int i = 0; i < KBPT; ++i)
-                m[i] = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-                for (int i = 0; i < KBPT; ++i) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
-            }
-#pragma unroll
-            for (int i = 0; i < KBPT; ++i) {
-                const float s = pow2_scale_for(m[i]);
-                const float inv = 1.0f / s;  // exact: s is a power of two
-                uint32_t w = 0u;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const uint8_t b = e4m3_rn(v[i][e] * inv);
-                    w |= uint32_t(b) << (8 * e);
-                    v[i][e] -= e4m3_to_f32(b) * s;  // exact: the scaled residual is representable
-                }
-                q[i][sp] = w;
-                sc[i][sp] = s;
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < KBPT; ++i) {
-            const int kb = kb0 + i;
-            if (i >= kbpt || kb >= KB) break;
+                m[i] = warp_max_nonneg(fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3]))));
             // K-major, 128-byte swizzled placement: B row n = term * TP + token (TP = 8 NT),
             // 128 bytes of K per row, 16-byte chunk c of row n stored at chunk c ^ (n & 7);
             // the (group, kb) tile is terms x TP rows (3 terms: decode, 2 terms: prefill).
-            const int64_t gk = int64_t(gr.tile_base) * KB + int64_t(kb) * NT;  // (group, kb) tile
-            uint8_t* base = a.bfrag + gk * (a.terms * kTileCols * kBlock);
+            const int n = sp * TP + tok;
+            const int off = n * kBlock + (c ^ (n & 7)) * 16 + 4 * (lane & 3);
 #pragma unroll
-            for (int sp = 0; sp < kSplits; ++sp) {
-                if (sp >= a.terms) break;
-                const int n = sp * TP + tok;
-                const int pc = c ^ (n & 7);
-                *reinterpret_cast<uint32_t*>(base + n * kBlock + pc * 16 + 4 * (lane & 3)) = q[i][sp];
-            }
-            if (lane == 0) {
-#pragma unroll
-                for (int sp = 0; sp < kSplits; ++sp)
-                    if (sp < a.terms) a.bscale[gk * kScalesPerTile + sp * TP + tok] = sc[i][sp];
+            for (int i = 0; i < KBPT; ++i) {
+                const int kb = kb0 + i;
+                if (kb >= KB) break;
+                const float s = pow2_scale_for(m[i]);
+                const float inv = pow2_recip(s);  // exact: s is a power of two
+                // element e in byte e; the scaled residual of each is exact in fp32
+                const uint32_t q01 = e4m3x2_rn(v[i][0] * inv, v[i][1] * inv);
+                const uint32_t q23 = e4m3x2_rn(v[i][2] * inv, v[i][3] * inv);
+                const float2 d01 = e4m3x2_to_f32x2(q01), d23 = e4m3x2_to_f32x2(q23);
+                v[i][0] -= d01.x * s;
+                v[i][1] -= d01.y * s;
+                v[i][2] -= d23.x * s;
+                v[i][3] -= d23.y * s;
+                const uint32_t w = q01 | (q23 << 16);
+                const int64_t gk = int64_t(gr.tile_base) * KB + int64_t(kb) * NT;  // (group, kb) tile
+                *reinterpret_cast<uint32_t*>(a.bfrag + gk * (a.terms * kTileCols * kBlock) + off) = w;
+                if (lane == 0) a.bscale[gk * kScalesPerTile + sp * TP + tok] = s;
             }
         }
     }
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackActArgs a) {
             amax = warp_max(amax);
             s = pow2_scale_for(amax);
         }
-        const float inv = 1.0f / s;  // exact: s is a power of two
+        const float inv = pow2_recip(s);  // exact: s is a power of two
         const int tok = r;
         const int TP = NT * kTileCols;
         const int c = lane >> 2;
@@ -235,15 +236,20 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackActArgs a) {
             for (int i = 0; i < 4; ++i) {
                 const int kb = kb0 + i;
                 if (kb >= KB) break;
+                // element e in byte e of each term; the residual after the first is exact
                 uint32_t q[2] = {0u, 0u};
+                float rsd[4] = {v[i][0] * inv, v[i][1] * inv, v[i][2] * inv, v[i][3] * inv};
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    float rsd = v[i][e] * inv;
-#pragma unroll
-                    for (int sp = 0; sp < 2; ++sp) {
-                        const uint8_t b = e4m3_rn(rsd);
-                        q[sp] |= uint32_t(b) << (8 * e);
-                        rsd -= e4m3_to_f32(b);
+                for (int sp = 0; sp < 2; ++sp) {
+                    const uint32_t q01 = e4m3x2_rn(rsd[0], rsd[1]);
+                    const uint32_t q23 = e4m3x2_rn(rsd[2], rsd[3]);
+                    q[sp] = q01 | (q23 << 16);
+                    if (sp == 0) {
+                        const float2 d01 = e4m3x2_to_f32x2(q01), d23 = e4m3x2_to_f32x2(q23);
+                        rsd[0] -= d01.x;
+                        rsd[1] -= d01.y;
+                        rsd[2] -= d23.x;
+                        rsd[3] -= d23.y;
                     }
                 }
                 // (group, kb) tile: 2 terms x TP rows x 128 B, swizzled as in pack_act_kernel
@@ -298,10 +304,25 @@ cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t str
     return launch_chained(pack_rows_kernel, dim3(num_sms * 8), dim3(256), 0, stream, a);
 }
 
+// CTAs of `kernel` (256 threads) resident on one SM at once; 1 if the query fails
+template <typename K>
+static int resident_ctas(K kernel) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 256, 0) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        return 1;
+    }
+    return n;
+}
+
 cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream) {
-    if (a.src_dtype == kSrcUpGatePartials)
-        return launch_chained(pack_act_kernel<2>, dim3(num_sms * 8), dim3(256), 0, stream, a);
-    return launch_chained(pack_act_kernel<kPackKbPerTask>, dim3(num_sms * 8), dim3(256), 0, stream, a);
+    // one wave: the row count is known on the device only, the loop strides over it
+    if (a.src_dtype == kSrcUpGatePartials) {
+        static const int occ = resident_ctas(pack_act_kernel<2>);
+        return launch_chained(pack_act_kernel<2>, dim3(num_sms * occ), dim3(256), 0, stream, a);
+    }
+    static const int occ = resident_ctas(pack_act_kernel<kPackKbPerTask>);
+    return launch_chained(pack_act_kernel<kPackKbPerTask>, dim3(num_sms * occ), dim3(256), 0, stream, a);
 }
 
 }  // namespace cst

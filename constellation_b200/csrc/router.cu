@@ -17,6 +17,10 @@
 //     results are bit-identical from run to run; logits [T, E] are written once.
 //   router_select_kernel: one warp per token does the sigmoid / bias / group / top-k
 //     logic with warp-shuffle arg-max reductions.
+// Large bf16 batches take the logits on the tensor cores instead (router_split_w_kernel +
+// router_logits_tc_kernel below: W split exactly into three bf16 terms, fp32 fold per K
+// block), and decode-sized batches select with one CTA per token
+// (router_select_rank_kernel).
 #include <cfloat>
 #include <cstdint>
 #include <cuda_bf16.h>
@@ -168,27 +172,87 @@ __global__ void __launch_bounds__(kLWarps * 32) router_logits_kernel(const TX* _
 // fresh TMEM buffer (4 k-steps x 3 terms) and every thread adds its expert row of that
 // buffer into fp32 registers -- the tensor core's internal accumulation never spans more
 // than one block, so the result matches an fp32 FMA chain to within summation-order
-// rounding.  Two stages and two TMEM buffers alternate: while the MMAs of block j run, the
-// threads stage block j + 1 and fold block j - 1.  CTAs along grid.z take disjoint K ranges
-// and write partial logits [z][T][E]; the selection kernel adds the partials in z order.
+// rounding.  CTAs along grid.z take disjoint K ranges and write partial logits [z][T][E];
+// the selection kernel adds the partials in z order.
+//
+// Two launches per call:
+//   router_split_w_kernel: the three terms of W, once per call, written as the very bytes
+//     the MMAs read from shared memory -- per (128-expert tile, K block) 3 x 16 KB, rows of
+//     128 bytes with the 128-byte swizzle -- so a CTA copies a block's 48 KB of A operand
+//     as one contiguous run instead of converting it again (every token tile used to).
+//   router_logits_tc_kernel: kRtStages shared-memory stages filled by cp.async, each
+//     thread copying its share of block j + kRtStages - 1 while the MMAs of block j run and
+//     it folds block j - 1; x rows are copied into their swizzled places, rows past T
+//     zero-filled.  Two TMEM buffers alternate between the MMAs of one block and the fold
+//     of the previous one.
 constexpr int kRtThreads = 128;
 constexpr int kRtKB = 64;                        // bf16 per 128-byte row
 constexpr int kRtATerm = 128 * 128;              // bytes of one W term tile (128 rows x 128 B)
+constexpr int kRtWBytes = 3 * kRtATerm;          // the three terms of one (expert tile, K block)
 constexpr int kRtMaxN = 128;
-constexpr int kRtStage = 3 * kRtATerm + kRtMaxN * 128;  // 64 KB
+constexpr int kRtStage = kRtWBytes + kRtMaxN * 128;  // 64 KB
+constexpr int kRtStages = 3;
+constexpr size_t kRtSmem = size_t(kRtStages) * kRtStage + 1024 + 64;
 
 __device__ __forceinline__ uint32_t bf16_pair(float a, float b) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// 16-byte asynchronous global -> shared copy; src_bytes 0 fills the 16 bytes with zeros
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// W [E, H] fp32 -> image[((et * (H / 64) + kb) * 3 + term) * 16 KB + r * 128 + ((c ^ (r & 7)) << 4)]
+// = the 8 bf16 of term `term` of W[et * 128 + r][kb * 64 + c * 8 .. + 8].  One thread per
+// 8 consecutive weights of a row: 32 bytes read, 16 bytes written per term.
+__global__ void __launch_bounds__(256) router_split_w_kernel(const float* __restrict__ w, uint8_t* __restrict__ img,
+                                                             int E, int H) {
+    chain_wait();
+    chain_release();
+    const int cpr = H / 8;  // 8-column chunks per row
+    const int kbn = H / kRtKB;
+    const int64_t n = int64_t(E) * cpr;
+    for (int64_t q = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; q < n; q += int64_t(gridDim.x) * blockDim.x) {
+        const int e = static_cast<int>(q / cpr);
+        const int c8 = static_cast<int>(q - int64_t(e) * cpr);
+        const float4* src = reinterpret_cast<const float4*>(w + int64_t(e) * H + c8 * 8);
+        const float4 p = __ldg(src), s = __ldg(src + 1);
+        const float v[8] = {p.x, p.y, p.z, p.w, s.x, s.y, s.z, s.w};
+        uint32_t t1[4], t2[4], t3[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float a = v[2 * i], b = v[2 * i + 1];
+            const float a1 = __bfloat162float(__float2bfloat16_rn(a));
+            const float b1 = __bfloat162float(__float2bfloat16_rn(b));
+            const float ra = a - a1, rb = b - b1;
+            const float a2 = __bfloat162float(__float2bfloat16_rn(ra));
+            const float b2 = __bfloat162float(__float2bfloat16_rn(rb));
+            t1[i] = bf16_pair(a1, b1);
+            t2[i] = bf16_pair(a2, b2);
+            t3[i] = bf16_pair(ra - a2, rb - b2);
+        }
+        const int et = e >> 7, r = e & 127, kb = c8 >> 3, c = c8 & 7;
+        uint8_t* dst = img + (int64_t(et) * kbn + kb) * kRtWBytes + r * 128 + ((c ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(t1[0], t1[1], t1[2], t1[3]);
+        *reinterpret_cast<uint4*>(dst + kRtATerm) = make_uint4(t2[0], t2[1], t2[2], t2[3]);
+        *reinterpret_cast<uint4*>(dst + 2 * kRtATerm) = make_uint4(t3[0], t3[1], t3[2], t3[3]);
+    }
+}
+
 __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const __nv_bfloat16* __restrict__ x,
-                                                                        const float* __restrict__ w,
+                                                                        const uint8_t* __restrict__ wimg,
                                                                         float* __restrict__ part, int T, int E,
                                                                         int H, int N, int nb, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * kRtStage);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kRtStages * kRtStage);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t0 = blockIdx.x * N;
@@ -211,6 +275,25 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const _
     chain_release();
     const uint32_t lane_addr = uint32_t(warp * 32) << 16;
     const uint32_t idesc = umma_idesc_bf16(128, N);
+    const uint8_t* wblk = wimg + (int64_t(blockIdx.y) * (H / kRtKB) + kb0) * kRtWBytes;  // this CTA's block 0
+    // this thread's copies of block j into stage j % kRtStages (none past the CTA's last
+    // block), then a commit -- one group per call, so group j is block j's
+    auto issue = [&](int j) {
+        if (j < nb) {
+            uint8_t* st = smem + (j % kRtStages) * kRtStage;
+            const uint8_t* src = wblk + int64_t(j) * kRtWBytes;
+#pragma unroll 4
+            for (int q = tid; q < kRtWBytes / 16; q += kRtThreads) cp_async16(smem_u32(st + q * 16), src + q * 16, 16u);
+            const int k0 = (kb0 + j) * kRtKB;
+            for (int q = tid; q < N * 8; q += kRtThreads) {
+                const int r = q >> 3, c = q & 7, t = t0 + r;
+                const bool in = t < T;
+                const __nv_bfloat16* xs = x + int64_t(in ? t : 0) * H + k0 + c * 8;
+                cp_async16(smem_u32(st + kRtWBytes + r * 128 + ((c ^ (r & 7)) << 4)), xs, in ? 16u : 0u);
+            }
+        }
+        cp_async_commit();
+    };
     float acc[kRtMaxN];
 #pragma unroll
     for (int i = 0; i < kRtMaxN; ++i) acc[i] = 0.0f;
@@ -233,76 +316,37 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const _
         }
         tc_fence_before();
     };
+#pragma unroll 1
+    for (int j = 0; j < kRtStages - 1; ++j) issue(j);
+    int committed = -1;  // last block whose MMAs were committed
     for (int j = 0; j < nb; ++j) {
-        const int s = j & 1;
-        // stage s and TMEM buffer s were last used by block j - 2, folded in iteration j - 1
-        uint8_t* st = smem + s * kRtStage;
-        const int k0 = (kb0 + j) * kRtKB;
-        // W rows -> three bf16 terms: a warp takes 32 of the 128 rows (rows warp + 4 i, 8 B of
-        // each per lane), loaded 16 rows at a time so the loads are in flight together
+        cp_async_wait<kRtStages - 2>();  // block j's copies (group j) have landed
+        fence_proxy_async_smem();        // the tensor cores read what cp.async just wrote
+        if (__syncthreads_or(!ok)) break;
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + (j % kRtStages) * kRtStage);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            float2 v[16];
+            for (int ks = 0; ks < 4; ++ks) {
+                const uint64_t bdesc = umma_desc_sw128(sa + kRtWBytes + ks * 32);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int r = warp + 4 * (16 * half + i);
-                v[i] = __ldg(reinterpret_cast<const float2*>(w + int64_t(e0 + r) * H + k0) + lane);
-            }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int r = warp + 4 * (16 * half + i);
-                const float a1 = __bfloat162float(__float2bfloat16_rn(v[i].x));
-                const float b1 = __bfloat162float(__float2bfloat16_rn(v[i].y));
-                const float ra = v[i].x - a1, rb = v[i].y - b1;
-                const float a2 = __bfloat162float(__float2bfloat16_rn(ra));
-                const float b2 = __bfloat162float(__float2bfloat16_rn(rb));
-                const int off = r * 128 + (((lane >> 2) ^ (r & 7)) << 4) + ((lane & 3) << 2);
-                *reinterpret_cast<uint32_t*>(st + off) = bf16_pair(a1, b1);
-                *reinterpret_cast<uint32_t*>(st + kRtATerm + off) = bf16_pair(a2, b2);
-                *reinterpret_cast<uint32_t*>(st + 2 * kRtATerm + off) = bf16_pair(ra - a2, rb - b2);
-            }
-        }
-        // x rows (bf16, copied as is), up to 32 per warp, loaded together; rows past T are zero
-        {
-            uint32_t v[kRtMaxN / 4];
-#pragma unroll
-            for (int i = 0; i < kRtMaxN / 4; ++i) {
-                const int r = warp + 4 * i, t = t0 + r;
-                v[i] = (r < N && t < T) ? __ldg(reinterpret_cast<const uint32_t*>(x + int64_t(t) * H + k0) + lane) : 0u;
-            }
-#pragma unroll
-            for (int i = 0; i < kRtMaxN / 4; ++i) {
-                const int r = warp + 4 * i;
-                if (r < N)
-                    *reinterpret_cast<uint32_t*>(st + 3 * kRtATerm + r * 128 + (((lane >> 2) ^ (r & 7)) << 4) +
-                                                 ((lane & 3) << 2)) = v[i];
-            }
-        }
-        fence_proxy_async_smem();  // the tensor cores read what the threads just wrote
-        __syncthreads();
-        if (!__syncthreads_or(!ok)) {
-            if (tid == 0) {
-                tc_fence_after();
-                const uint32_t sa = smem_u32(st);
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
-                    const uint64_t bdesc = umma_desc_sw128(sa + 3 * kRtATerm + ks * 32);
-#pragma unroll
-                    for (int term = 0; term < 3; ++term) {
-                        const uint64_t adesc = umma_desc_sw128(sa + term * kRtATerm + ks * 32);
-                        tc_mma_bf16(tmem + s * kRtMaxN, adesc, bdesc, idesc, (ks > 0 || term > 0) ? 1u : 0u);
-                    }
+                for (int term = 0; term < 3; ++term) {
+                    const uint64_t adesc = umma_desc_sw128(sa + term * kRtATerm + ks * 32);
+                    tc_mma_bf16(tmem + (j & 1) * kRtMaxN, adesc, bdesc, idesc, (ks > 0 || term > 0) ? 1u : 0u);
                 }
-                tc_commit(&bar[s]);
             }
-        } else {
-            break;
+            tc_commit(&bar[j & 1]);
         }
+        committed = j;
+        // block j - 1's MMAs are complete once its fold has waited for them, so its stage
+        // takes block j + kRtStages - 1
         if (j > 0) fold(j - 1);
+        issue(j + kRtStages - 1);
     }
-    if (ok && nb > 0) fold(nb - 1);
-    else if (nb > 0) mbar_wait(&bar[(nb - 1) & 1], ((nb - 1) >> 1) & 1u, err);  // nothing in flight at exit
-    if (__syncthreads_and(ok)) {
+    cp_async_wait<0>();  // no copy in flight at exit
+    if (ok && committed == nb - 1 && nb > 0) fold(nb - 1);
+    else if (committed >= 0) mbar_wait(&bar[committed & 1], (committed >> 1) & 1u, err);  // no MMA in flight
+    if (__syncthreads_and(ok && committed == nb - 1)) {
         const int e = e0 + warp * 32 + lane;
         float* out = part + int64_t(blockIdx.z) * T * E;
 #pragma unroll
@@ -569,14 +613,14 @@ __global__ void __launch_bounds__(1024) router_select_rank_kernel(RouterArgs a) 
     }
 }
 
-// Tensor-core logits apply to bf16 activations with E a multiple of 128 and H of 64, above
-// 2048 tokens: below that the SIMT kernel is faster (per call, measured: 64 tokens 19 us vs
-// 26 us, 512 tokens 78 us vs 115 us; 4096 tokens 506 us vs 301 us the other way).
-// K split: CTAs along K while the grid stays within two waves, each CTA keeps >= 2 K blocks
-// and the partials fit both `cap` and a budget that depends only on T * E (2 Mi floats up to
-// 524288 logits, 8 x the logits beyond) -- so a context and the allocation-free entry
-// point choose the same split, and the same summation order, for the same call.
+// Tensor-core logits apply to bf16 activations with E a multiple of 128 and H of 64, from
+// kRtMinTokens tokens on (below that the CUDA-core kernel is faster per call).
+// K split: the grid (token tiles x expert tiles x ks) runs one CTA per SM at a time, so the
+// critical path is ceil(CTAs / SMs) waves of H / 64 / ks K blocks each; ks is the divisor
+// of the K blocks (each CTA keeping >= 2) with the fewest blocks on that path, the smaller
+// ks on a tie (fewer partial sums for the selection to add), within `cap` partial floats.
 constexpr int kRtMinTokens = 2049;
+constexpr int kRtSms = 148;
 static bool router_tc_ok(int x_dtype, int T, int E, int H) {
     return x_dtype == 2 && T >= kRtMinTokens && E % 128 == 0 && H % kRtKB == 0;
 }
@@ -587,25 +631,39 @@ int router_tc_split(int T, int E, int H, int64_t cap) {
     const int N = router_tc_n(T);
     const int64_t base = int64_t((T + N - 1) / N) * (E / 128);
     const int64_t logits = int64_t(T) * E;
-    const int64_t budget = std::min<int64_t>(cap, logits <= (int64_t(1) << 19) ? (int64_t(1) << 19) : 8 * logits);
-    for (int ks = nbt / 2; ks > 1; --ks)
-        if (nbt % ks == 0 && base * ks <= 296 && ks * logits <= budget) return ks;
-    return 1;
+    int best = 1;
+    int64_t best_path = ((base + kRtSms - 1) / kRtSms) * nbt;
+    for (int ks = 2; ks <= nbt / 2; ++ks) {
+        if (nbt % ks != 0 || ks * logits > cap) continue;
+        const int64_t path = ((base * ks + kRtSms - 1) / kRtSms) * (nbt / ks);
+        if (path < best_path) {
+            best = ks;
+            best_path = path;
+        }
+    }
+    return best;
 }
+
+// floats of the split-W image (3 bf16 terms of E x H), a multiple of 64 (256 bytes)
+static int64_t router_img_floats(int E, int H) { return (int64_t(E) * H * 6 / 4 + 63) / 64 * 64; }
 
 int64_t router_scratch_floats(int x_dtype, int T, int E, int H) {
-    const int ks = router_tc_ok(x_dtype, T, E, H) ? router_tc_split(T, E, H, INT64_MAX) : 1;
-    return int64_t(ks) * T * E;
+    if (!router_tc_ok(x_dtype, T, E, H)) return int64_t(T) * E;
+    return router_img_floats(E, H) + int64_t(router_tc_split(T, E, H, INT64_MAX)) * T * E;
 }
 
-// x_dtype: 1 fp16, 2 bf16, 3 fp32.  `logits` holds `cap` floats: the partial logits
-// (scratch), or, with cap == T * E, the caller's [T, E] logits (then K is not split).
+// x_dtype: 1 fp16, 2 bf16, 3 fp32.  `logits` holds `cap` floats of scratch: the partial
+// logits, and, on the tensor-core path, in front of them the split-W image (the path is
+// taken only when `cap` holds both and x rows start on 16-byte boundaries).
 cudaError_t launch_router(const void* x, int x_dtype, const float* w, const float* bias, const uint8_t* resident,
                           int T, int E, int H, int n_group, int topk_group, int top_k, int norm, float scale,
                           float* logits, int64_t cap, int32_t* topk_idx, float* topk_w, float* group_scores_out,
                           int* err, cudaStream_t stream, bool allow_tc, float* logits_out) {
     int ks = 1;
-    if (allow_tc && err != nullptr && router_tc_ok(x_dtype, T, E, H)) {
+    float* part = logits;
+    const int64_t img_floats = router_img_floats(E, H);
+    if (allow_tc && err != nullptr && router_tc_ok(x_dtype, T, E, H) && cap >= img_floats + int64_t(T) * E &&
+        (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         static std::mutex mu;
         static bool attr_set[64] = {};
         int dev = 0;
@@ -614,19 +672,23 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
             std::lock_guard<std::mutex> lock(mu);
             if (dev >= 0 && dev < 64 && !attr_set[dev]) {
                 const cudaError_t e = cudaFuncSetAttribute(router_logits_tc_kernel,
-                                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                           2 * kRtStage + 1024 + 64);
+                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(kRtSmem));
                 if (e != cudaSuccess) return e;
                 attr_set[dev] = true;
             }
         }
-        ks = router_tc_split(T, E, H, cap);
+        uint8_t* img = reinterpret_cast<uint8_t*>(logits);
+        part = logits + img_floats;
+        ks = router_tc_split(T, E, H, cap - img_floats);
+        const int64_t chunks = int64_t(E) * (H / 8);
+        const int split_grid = int(std::min<int64_t>((chunks + 255) / 256, 4096));
+        cudaError_t e = launch_chained(router_split_w_kernel, dim3(split_grid), dim3(256), 0, stream, w, img, E, H);
+        if (e != cudaSuccess) return e;
         const int N = router_tc_n(T);
         const dim3 grid((T + N - 1) / N, E / 128, ks);
-        const cudaError_t e = launch_chained(router_logits_tc_kernel, grid, dim3(kRtThreads),
-                                             size_t(2 * kRtStage + 1024 + 64), stream,
-                                             static_cast<const __nv_bfloat16*>(x), w, logits, T, E, H, N,
-                                             H / kRtKB / ks, err);
+        e = launch_chained(router_logits_tc_kernel, grid, dim3(kRtThreads), kRtSmem, stream,
+                           static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(img), part, T, E, H, N,
+                           H / kRtKB / ks, err);
         if (e != cudaSuccess) return e;
     } else {
         const dim3 grid((T + kLT - 1) / kLT, (E + kLE - 1) / kLE);
@@ -643,7 +705,7 @@ cudaError_t launch_router(const void* x, int x_dtype, const float* w, const floa
         }
         if (e != cudaSuccess) return e;
     }
-    RouterArgs a{logits, ks, bias, resident, T, E, n_group, topk_group, top_k, norm, scale,
+    RouterArgs a{part, ks, bias, resident, T, E, n_group, topk_group, top_k, norm, scale,
                  topk_idx, topk_w, group_scores_out, logits_out};
     if (T <= 2048) {
         // decode-sized batches: one CTA per token, short dependency chains
