@@ -282,6 +282,10 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
         // every token's scale once, then one pass per packed row
         CST_CUDA(launch_row_scale(px, pa.T, w.tok_scale, c->num_sms, s));
         px.src_scale = w.tok_scale;
+        const bool mode_rows = (pa.row_slot != nullptr) || (pa.single_slot >= 0);
+        px.tk_row = w.tk_row;
+        px.K1 = mode_rows ? 1 : pa.K + 1;
+        px.n_src = pa.T;
         CST_CUDA(launch_pack_rows(px, c->num_sms, s));
     } else {
         CST_CUDA(launch_pack_act(px, c->num_sms, s));

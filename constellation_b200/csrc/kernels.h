@@ -113,6 +113,11 @@ struct PackActArgs {
     float* bscale;           // per (row, K block) scales
     int terms;               // E4M3 terms per element: 3 (decode kernels) or 2 (prefill kernels)
     const float* src_scale = nullptr;  // prefill: per source row scale (row_scale_kernel), or null
+    // prefill x, token-major (with src_scale): tk_row [n_src, K1] -> packed row of each of a
+    // source row's routes, -1 where absent; the packer then reads each source row once
+    const int32_t* tk_row = nullptr;
+    int K1 = 0;
+    int n_src = 0;
 };
 // src_dtype 4: `src` holds the up/gate kernel's split accumulators (meta->split_k splits of
 // meta->n_rows rows each); the packer adds the splits in order and applies

@@ -266,6 +266,152 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackActArgs a) {
     }
 }
 
+// Prefill x, token-major.  A prefill call packs each x row for ~9 experts (its routes and
+// the shared expert) with ONE power-of-two scale per token (row_scale_kernel), so every
+// packed row of a token carries the same bytes.  One warp per (token, 8 K blocks): the
+// chunk is loaded and quantized once, then stored into each packed row of the token
+// (tk_row: token -> packed row per route, -1 where absent), placed as pack_rows_kernel
+// places it.  x is read once instead of once per packed row, and quantized once.
+__global__ void __launch_bounds__(256) pack_tokens_kernel(PackActArgs a) {
+    __shared__ int32_t s_rs[kPackSmemGroups];
+    chain_wait();
+    chain_release();
+    const int KB = a.K / kBlock;
+    const int n_chunks = (KB + kPackKbPerTask - 1) / kPackKbPerTask;
+    const int n_groups = a.meta->n_groups;
+    const bool staged = n_groups <= kPackSmemGroups;
+    if (staged)
+        for (int g = threadIdx.x; g < n_groups; g += blockDim.x) s_rs[g] = a.groups[g].row_start;
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int c = lane >> 2;
+    const int64_t n_tasks = int64_t(a.n_src) * n_chunks;
+    const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t task = warp_global; task < n_tasks; task += n_warps) {
+        const int t = static_cast<int>(task / n_chunks);
+        const int chunk = static_cast<int>(task - int64_t(t) * n_chunks);
+        int prow[16];
+        bool any = false;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            prow[k] = k < a.K1 ? __ldg(a.tk_row + int64_t(t) * a.K1 + k) : -1;
+            any |= prow[k] >= 0;
+        }
+        if (!any) continue;  // no packed row of this token in this call
+        const float s = a.src_scale[t];
+        const float inv = pow2_recip(s);  // exact: s is a power of two
+        const int kb0 = chunk * kPackKbPerTask;
+        float v[kPackKbPerTask][4];
+#pragma unroll
+        for (int i = 0; i < kPackKbPerTask; ++i) {
+            if (kb0 + i < KB) {
+                load4(a, t, (kb0 + i) * kBlock + 4 * lane, 1, v[i]);
+            } else {
+                v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.0f;
+            }
+        }
+        uint32_t w0[kPackKbPerTask], w1[kPackKbPerTask];
+#pragma unroll
+        for (int i = 0; i < kPackKbPerTask; ++i) {
+            // element e in byte e of each term; the residual after the first is exact
+            const float r0 = v[i][0] * inv, r1 = v[i][1] * inv, r2 = v[i][2] * inv, r3 = v[i][3] * inv;
+            const uint32_t q01 = e4m3x2_rn(r0, r1);
+            const uint32_t q23 = e4m3x2_rn(r2, r3);
+            const float2 d01 = e4m3x2_to_f32x2(q01), d23 = e4m3x2_to_f32x2(q23);
+            w0[i] = q01 | (q23 << 16);
+            w1[i] = e4m3x2_rn(r0 - d01.x, r1 - d01.y) | (e4m3x2_rn(r2 - d23.x, r3 - d23.y) << 16);
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (prow[k] < 0) continue;
+            const GroupRec gr = a.groups[group_of_row(staged ? s_rs : nullptr, a.groups, n_groups, prow[k])];
+            const int tok = prow[k] - gr.row_start;
+            const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
+            const int n0 = tok, n1 = NT * kTileCols + tok;
+            const int off0 = n0 * kBlock + ((c ^ (n0 & 7)) * 16) + 4 * (lane & 3);
+            const int off1 = n1 * kBlock + ((c ^ (n1 & 7)) * 16) + 4 * (lane & 3);
+#pragma unroll
+            for (int i = 0; i < kPackKbPerTask; ++i) {
+                const int kb = kb0 + i;
+                if (kb >= KB) break;
+                // (group, kb) tile: 2 terms x TP rows x 128 B, swizzled as in pack_act_kernel
+                uint8_t* base = a.bfrag + (int64_t(gr.tile_base) * KB + int64_t(kb) * NT) * (2 * kTileCols * kBlock);
+                *reinterpret_cast<uint32_t*>(base + off0) = w0[i];
+                *reinterpret_cast<uint32_t*>(base + off1) = w1[i];
+            }
+            if (chunk == 0 && lane == 0) a.bscale[prow[k]] = s;
+        }
+    }
+}
+
+// pack_rows_kernel for rows of at most kRowRegBlocks K blocks with no precomputed scale (h:
+// I = 2048 -> 16 blocks): the row is loaded once into registers, 4 elements per lane per
+// K block, its max |v| reduced there and both terms written from the registers -- one pass
+// over the up/gate partials instead of two (a prefill chunk's partials exceed the L2, so
+// the second pass re-read them from HBM).  Same scale, bytes and placement as
+// pack_rows_kernel.
+constexpr int kRowRegBlocks = 16;
+__global__ void __launch_bounds__(256) pack_rows_reg_kernel(PackActArgs a) {
+    chain_wait();
+    chain_release();
+    const int KB = a.K / kBlock;
+    const int n_tiles = a.meta->n_tiles;
+    const int split = a.src_dtype == kSrcUpGatePartials ? a.meta->split_k : 1;
+    const int lane = threadIdx.x & 31;
+    const int64_t n_tasks = int64_t(n_tiles) * kTileCols;
+    const int64_t warp_global = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t task = warp_global; task < n_tasks; task += n_warps) {
+        const int tile = static_cast<int>(task / kTileCols);
+        const int j = static_cast<int>(task % kTileCols);
+        const GroupRec gr = a.groups[a.tile_group[tile]];
+        const int nt = tile - gr.tile_base;
+        const int NT = (gr.n_rows + kTileCols - 1) / kTileCols;
+        const int r = nt * kTileCols + j;
+        if (r >= gr.n_rows) continue;  // unread accumulator columns need no data
+        const int prow = gr.row_start + r;
+        const int64_t src_row = a.row_map ? a.row_map[prow] : prow;
+        float v[kRowRegBlocks][4];
+#pragma unroll
+        for (int i = 0; i < kRowRegBlocks; ++i) {
+            if (i < KB) {
+                load4(a, src_row, i * kBlock + 4 * lane, split, v[i]);
+            } else {
+                v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.0f;
+            }
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kRowRegBlocks; ++i)
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3]))));
+        amax = warp_max(amax);
+        const float s = pow2_scale_for(amax);
+        const float inv = pow2_recip(s);  // exact: s is a power of two
+        const int tok = r;
+        const int TP = NT * kTileCols;
+        const int c = lane >> 2;
+#pragma unroll
+        for (int i = 0; i < kRowRegBlocks; ++i) {
+            if (i >= KB) break;
+            // element e in byte e of each term; the residual after the first is exact
+            float rsd[4] = {v[i][0] * inv, v[i][1] * inv, v[i][2] * inv, v[i][3] * inv};
+            const uint32_t q01 = e4m3x2_rn(rsd[0], rsd[1]);
+            const uint32_t q23 = e4m3x2_rn(rsd[2], rsd[3]);
+            const float2 d01 = e4m3x2_to_f32x2(q01), d23 = e4m3x2_to_f32x2(q23);
+            const uint32_t w0 = q01 | (q23 << 16);
+            const uint32_t w1 = e4m3x2_rn(rsd[0] - d01.x, rsd[1] - d01.y) | (e4m3x2_rn(rsd[2] - d23.x, rsd[3] - d23.y) << 16);
+            // (group, kb) tile: 2 terms x TP rows x 128 B, swizzled as in pack_act_kernel
+            const int64_t gk = int64_t(gr.tile_base) * KB + int64_t(i) * NT;
+            uint8_t* base = a.bfrag + gk * (2 * kTileCols * kBlock);
+            const int n0 = tok, n1 = TP + tok;
+            *reinterpret_cast<uint32_t*>(base + n0 * kBlock + ((c ^ (n0 & 7)) * 16) + 4 * (lane & 3)) = w0;
+            *reinterpret_cast<uint32_t*>(base + n1 * kBlock + ((c ^ (n1 & 7)) * 16) + 4 * (lane & 3)) = w1;
+        }
+        if (lane == 0) a.bscale[prow] = s;
+    }
+}
+
 // One warp per source row: the power-of-two scale pack_rows_kernel would find for it
 // (max |v| over the row -> pow2_scale_for).  Lets the x packer run one pass when a token
 // appears in several packed rows.
@@ -278,13 +424,13 @@ __global__ void __launch_bounds__(256) row_scale_kernel(PackActArgs a, int n_src
     const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
     for (int64_t row = warp_global; row < n_src_rows; row += n_warps) {
         float amax = 0.0f;
-        for (int kb0 = 0; kb0 < KB; kb0 += 4) {
-            float v[4][4];
+        for (int kb0 = 0; kb0 < KB; kb0 += 8) {  // 8 loads in flight per round
+            float v[8][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 8; ++i)
                 if (kb0 + i < KB) load4(a, row, (kb0 + i) * kBlock + 4 * lane, 1, v[i]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 8; ++i)
                 if (kb0 + i < KB)
                     amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3]))));
         }
@@ -299,10 +445,7 @@ cudaError_t launch_row_scale(const PackActArgs& a, int n_src_rows, float* out, i
     return launch_chained(row_scale_kernel, dim3(num_sms * 4), dim3(256), 0, stream, a, n_src_rows, out);
 }
 
-cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t stream) {
-    if (a.terms != 2) return cudaErrorInvalidValue;
-    return launch_chained(pack_rows_kernel, dim3(num_sms * 8), dim3(256), 0, stream, a);
-}
+
 
 // CTAs of `kernel` (256 threads) resident on one SM at once; 1 if the query fails
 template <typename K>
@@ -313,6 +456,19 @@ static int resident_ctas(K kernel) {
         return 1;
     }
     return n;
+}
+
+cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t stream) {
+    if (a.terms != 2) return cudaErrorInvalidValue;
+    if (a.src_scale == nullptr && a.K / kBlock <= kRowRegBlocks) {
+        static const int occ = resident_ctas(pack_rows_reg_kernel);
+        return launch_chained(pack_rows_reg_kernel, dim3(num_sms * occ), dim3(256), 0, stream, a);
+    }
+    if (a.src_scale != nullptr && a.tk_row != nullptr && a.src_dtype != kSrcUpGatePartials) {
+        static const int occ = resident_ctas(pack_tokens_kernel);
+        return launch_chained(pack_tokens_kernel, dim3(num_sms * occ), dim3(256), 0, stream, a);
+    }
+    return launch_chained(pack_rows_kernel, dim3(num_sms * 8), dim3(256), 0, stream, a);
 }
 
 cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream) {

@@ -12,7 +12,7 @@
 //
 // Two kernels:
 //   router_logits_kernel: [T, H] x [E, H]^T in fp32 on CUDA cores (the router needs exact
-//     fp32 products; TF32 tensor cores would change which experts win).  8-token x 8-expert
+//     fp32 products; TF32 tensor cores would change which experts win).  4-token x 8-expert
 //     tiles, one per CTA, K split over the CTA's warps and folded in a fixed order, so
 //     results are bit-identical from run to run; logits [T, E] are written once.
 //   router_select_kernel: one warp per token does the sigmoid / bias / group / top-k
@@ -64,7 +64,7 @@ __device__ __forceinline__ float4 load4x<__half>(const __half* x, int64_t off) {
     return make_float4(a.x, a.y, b.x, b.y);
 }
 
-constexpr int kLT = 8;       // tokens per CTA tile
+constexpr int kLT = 4;       // tokens per CTA tile
 constexpr int kLE = 8;       // experts per CTA tile
 constexpr int kLWarps = 4;   // warps per CTA, each over a contiguous quarter of K
 
@@ -81,17 +81,19 @@ __device__ __forceinline__ void reduce_half(float* v, int o, int lane) {
     }
 }
 
-// logits[t][e] = sum_k x[t][k] * w[e][k] in fp32 for an 8-token x 8-expert tile per CTA.
+// logits[t][e] = sum_k x[t][k] * w[e][k] in fp32 for a 4-token x 8-expert tile per CTA.
 // Warp q sums k in [q H/4, (q+1) H/4) with lane l taking columns k = 4 l + 128 j: per step
-// one float4 of each expert row and 4 activations of each token row, 256 independent FMA.
-// The 64 per-lane sums are folded across the warp by a fixed butterfly (lane l ends with
-// outputs 2l and 2l+1) and the four warps' sums are added in warp order, so the result is
-// bit-identical from run to run.  No global scratch: the tile is written once.
+// one float4 of each expert row and 4 activations of each token row, 128 independent FMA.
+// The 32 per-lane sums are folded across the warp by a fixed butterfly (lane l ends with
+// output l) and the four warps' sums are added in warp order, so the result is
+// bit-identical from run to run.  No global scratch: the tile is written once.  The tile
+// keeps a thread under 128 registers, so 4 CTAs fit an SM and a 64-token call's 512 CTAs
+// run in one wave with 16 warps per SM hiding each other's load latency.
 template <typename TX>
-__global__ void __launch_bounds__(kLWarps * 32) router_logits_kernel(const TX* __restrict__ x,
-                                                                     const float* __restrict__ w,
-                                                                     float* __restrict__ logits, int T, int E,
-                                                                     int H) {
+__global__ void __launch_bounds__(kLWarps * 32, 4) router_logits_kernel(const TX* __restrict__ x,
+                                                                        const float* __restrict__ w,
+                                                                        float* __restrict__ logits, int T, int E,
+                                                                        int H) {
     __shared__ float s_part[kLWarps][kLT * kLE];
     chain_wait();
     chain_release();
@@ -110,24 +112,12 @@ __global__ void __launch_bounds__(kLWarps * 32) router_logits_kernel(const TX* _
     for (int t = 0; t < kLT; ++t) xr[t] = x + int64_t(min(t0 + t, T - 1)) * H;
 #pragma unroll
     for (int e = 0; e < kLE; ++e) wr[e] = w + int64_t(min(e0 + e, E - 1)) * H;
-    // software-pipelined: the loads of the next 128-column step are issued before the FMAs
-    // of this one, so a warp waits for one memory latency per two steps (the summation
-    // order per lane is unchanged)
-    float4 wv[kLE], xv[kLT];
-    int k = k_begin + 4 * lane;
-    if (k < k_end) {
+    for (int k = k_begin + 4 * lane; k < k_end; k += 128) {
+        float4 wv[kLE], xv[kLT];
 #pragma unroll
         for (int e = 0; e < kLE; ++e) wv[e] = __ldg(reinterpret_cast<const float4*>(wr[e] + k));
 #pragma unroll
         for (int t = 0; t < kLT; ++t) xv[t] = load4x<TX>(xr[t], k);
-    }
-    for (; k < k_end; k += 128) {
-        float4 wn[kLE], xn[kLT];
-        const int kn = k + 128 < k_end ? k + 128 : k;  // the last step reloads its own columns
-#pragma unroll
-        for (int e = 0; e < kLE; ++e) wn[e] = __ldg(reinterpret_cast<const float4*>(wr[e] + kn));
-#pragma unroll
-        for (int t = 0; t < kLT; ++t) xn[t] = load4x<TX>(xr[t], kn);
 #pragma unroll
         for (int t = 0; t < kLT; ++t) {
 #pragma unroll
@@ -140,18 +130,13 @@ __global__ void __launch_bounds__(kLWarps * 32) router_logits_kernel(const TX* _
                 acc[t * kLE + e] = a;
             }
         }
-#pragma unroll
-        for (int e = 0; e < kLE; ++e) wv[e] = wn[e];
-#pragma unroll
-        for (int t = 0; t < kLT; ++t) xv[t] = xn[t];
     }
-    reduce_half<64>(acc, 16, lane);
-    reduce_half<32>(acc, 8, lane);
-    reduce_half<16>(acc, 4, lane);
-    reduce_half<8>(acc, 2, lane);
-    reduce_half<4>(acc, 1, lane);
-    s_part[warp][2 * lane] = acc[0];
-    s_part[warp][2 * lane + 1] = acc[1];
+    reduce_half<32>(acc, 16, lane);
+    reduce_half<16>(acc, 8, lane);
+    reduce_half<8>(acc, 4, lane);
+    reduce_half<4>(acc, 2, lane);
+    reduce_half<2>(acc, 1, lane);
+    s_part[warp][lane] = acc[0];
     __syncthreads();
     if (threadIdx.x < kLT * kLE) {
         const int o = threadIdx.x;
@@ -192,7 +177,7 @@ constexpr int kRtWBytes = 3 * kRtATerm;          // the three terms of one (expe
 constexpr int kRtMaxN = 128;
 constexpr int kRtStage = kRtWBytes + kRtMaxN * 128;  // 64 KB
 constexpr int kRtStages = 3;
-constexpr size_t kRtSmem = size_t(kRtStages) * kRtStage + 1024 + 64;
+constexpr size_t kRtSmem = size_t(kRtStages) * kRtStage + 1024 + 64;  // + barriers, TMEM slot
 
 __device__ __forceinline__ uint32_t bf16_pair(float a, float b) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
@@ -252,8 +237,9 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const _
                                                                         int H, int N, int nb, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kRtStages * kRtStage);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 2);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kRtStages * kRtStage);  // MMAs of even / odd blocks
+    uint64_t* full = bar + 2;                                                   // W bytes of each stage
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + kRtStages);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t0 = blockIdx.x * N;
     const int e0 = blockIdx.y * 128;
@@ -261,6 +247,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const _
     if (tid == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
+        for (int s = 0; s < kRtStages; ++s) mbar_init(&full[s], 1);
         fence_barrier_init();
     }
     if (warp == 0) {
@@ -276,21 +263,40 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const _
     const uint32_t lane_addr = uint32_t(warp * 32) << 16;
     const uint32_t idesc = umma_idesc_bf16(128, N);
     const uint8_t* wblk = wimg + (int64_t(blockIdx.y) * (H / kRtKB) + kb0) * kRtWBytes;  // this CTA's block 0
-    // this thread's copies of block j into stage j % kRtStages (none past the CTA's last
-    // block), then a commit -- one group per call, so group j is block j's
+    // This thread's 16-byte pieces of every x tile, fixed for all K blocks: piece m is row
+    // r = q / 8, chunk c = q % 8 of the tile (q = tid + 128 m), placed at its swizzled chunk;
+    // rows past T read 0 bytes (zero fill) from a valid address.
+    constexpr int kXPer = kRtMaxN * 8 / kRtThreads;
+    const int nx = N / 16;  // pieces per thread of an N-row tile (N a multiple of 16)
+    const __nv_bfloat16* xsrc[kXPer];
+    uint32_t xdst[kXPer];
+    uint32_t xin = 0;
+#pragma unroll
+    for (int m = 0; m < kXPer; ++m) {
+        const int q = tid + kRtThreads * m, r = q >> 3, c = q & 7, t = t0 + r;
+        const bool in = m < nx && t < T;
+        xsrc[m] = x + int64_t(in ? t : 0) * H + c * 8;
+        xdst[m] = kRtWBytes + r * 128 + ((c ^ (r & 7)) << 4);
+        xin |= (in ? 1u : 0u) << m;
+    }
+    int issued = -1, waited = -1;  // thread 0: last block whose W copy was issued / seen landed
+    // block j into stage j % kRtStages (nothing past the CTA's last block): thread 0 copies its
+    // 48 KB of W terms in one bulk copy onto the stage's barrier, every thread its x pieces
+    // with cp.async; one cp.async group per call, so group j is block j's
     auto issue = [&](int j) {
         if (j < nb) {
-            uint8_t* st = smem + (j % kRtStages) * kRtStage;
-            const uint8_t* src = wblk + int64_t(j) * kRtWBytes;
-#pragma unroll 4
-            for (int q = tid; q < kRtWBytes / 16; q += kRtThreads) cp_async16(smem_u32(st + q * 16), src + q * 16, 16u);
-            const int k0 = (kb0 + j) * kRtKB;
-            for (int q = tid; q < N * 8; q += kRtThreads) {
-                const int r = q >> 3, c = q & 7, t = t0 + r;
-                const bool in = t < T;
-                const __nv_bfloat16* xs = x + int64_t(in ? t : 0) * H + k0 + c * 8;
-                cp_async16(smem_u32(st + kRtWBytes + r * 128 + ((c ^ (r & 7)) << 4)), xs, in ? 16u : 0u);
+            const int s = j % kRtStages;
+            uint8_t* st = smem + s * kRtStage;
+            if (tid == 0) {
+                mbar_arrive_expect_tx(&full[s], kRtWBytes);
+                tma_bulk_g2s(st, wblk + int64_t(j) * kRtWBytes, kRtWBytes, &full[s]);
+                issued = j;
             }
+            const int k0 = (kb0 + j) * kRtKB;
+            const uint32_t sb = smem_u32(st);
+#pragma unroll
+            for (int m = 0; m < kXPer; ++m)
+                if (m < nx) cp_async16(sb + xdst[m], xsrc[m] + k0, ((xin >> m) & 1u) ? 16u : 0u);
         }
         cp_async_commit();
     };
@@ -298,20 +304,26 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const _
 #pragma unroll
     for (int i = 0; i < kRtMaxN; ++i) acc[i] = 0.0f;
     bool ok = true;
-    // fold the finished block jj (its MMAs committed to bar[jj & 1]) into acc
+    // fold the finished block jj (its MMAs committed to bar[jj & 1]) into acc, 32 columns per
+    // wait (the upper 16 of a pair past N are read, as garbage, and not used)
     auto fold = [&](int jj) {
         if (!mbar_wait(&bar[jj & 1], (jj >> 1) & 1u, err)) ok = false;
         tc_fence_after();
         const uint32_t base = tmem + lane_addr + (jj & 1) * kRtMaxN;
 #pragma unroll
-        for (int c0 = 0; c0 < kRtMaxN; c0 += 16) {
+        for (int c0 = 0; c0 < kRtMaxN; c0 += 32) {
             if (c0 < N) {
-                uint32_t d[16];
+                uint32_t d[32];
                 tmem_ld16(base + c0, d);
+                tmem_ld16(base + c0 + 16, d + 16);
                 tmem_wait_ld();
                 tmem_reg_fence(d);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) acc[c0 + i] += __uint_as_float(d[i]);
+                if (c0 + 16 < N) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) acc[c0 + 16 + i] += __uint_as_float(d[16 + i]);
+                }
             }
         }
         tc_fence_before();
@@ -320,8 +332,12 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const _
     for (int j = 0; j < kRtStages - 1; ++j) issue(j);
     int committed = -1;  // last block whose MMAs were committed
     for (int j = 0; j < nb; ++j) {
-        cp_async_wait<kRtStages - 2>();  // block j's copies (group j) have landed
+        cp_async_wait<kRtStages - 2>();  // this thread's x pieces of block j (group j) have landed
         fence_proxy_async_smem();        // the tensor cores read what cp.async just wrote
+        if (tid == 0) {
+            if (mbar_wait(&full[j % kRtStages], (j / kRtStages) & 1u, err)) waited = j;
+            else ok = false;
+        }
         if (__syncthreads_or(!ok)) break;
         if (tid == 0) {
             tc_fence_after();
@@ -343,9 +359,12 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_logits_tc_kernel(const _
         if (j > 0) fold(j - 1);
         issue(j + kRtStages - 1);
     }
-    cp_async_wait<0>();  // no copy in flight at exit
+    // nothing in flight at exit: x pieces, W bulk copies not yet seen landed, the MMAs
+    cp_async_wait<0>();
+    if (tid == 0)
+        for (int b = waited + 1; b <= issued; ++b) mbar_wait(&full[b % kRtStages], (b / kRtStages) & 1u, err);
     if (ok && committed == nb - 1 && nb > 0) fold(nb - 1);
-    else if (committed >= 0) mbar_wait(&bar[committed & 1], (committed >> 1) & 1u, err);  // no MMA in flight
+    else if (committed >= 0) mbar_wait(&bar[committed & 1], (committed >> 1) & 1u, err);
     if (__syncthreads_and(ok && committed == nb - 1)) {
         const int e = e0 + warp * 32 + lane;
         float* out = part + int64_t(blockIdx.z) * T * E;
@@ -614,12 +633,16 @@ __global__ void __launch_bounds__(1024) router_select_rank_kernel(RouterArgs a) 
 }
 
 // Tensor-core logits apply to bf16 activations with E a multiple of 128 and H of 64, from
-// kRtMinTokens tokens on (below that the CUDA-core kernel is faster per call).
+// kRtMinTokens tokens on: below that the CUDA-core kernel is faster per call (graph
+// replay, E = 256, H = 7168, measured: 64 tokens 25 us vs 33 us, 128 tokens 35 vs 37;
+// 256 tokens 55 vs 35, 1024 tokens 156 vs 49, 2048 tokens 303 vs 85 the other way).
 // K split: the grid (token tiles x expert tiles x ks) runs one CTA per SM at a time, so the
-// critical path is ceil(CTAs / SMs) waves of H / 64 / ks K blocks each; ks is the divisor
-// of the K blocks (each CTA keeping >= 2) with the fewest blocks on that path, the smaller
-// ks on a tie (fewer partial sums for the selection to add), within `cap` partial floats.
-constexpr int kRtMinTokens = 2049;
+// critical path is ceil(CTAs / SMs) waves, each of H / 64 / ks K blocks plus the CTA's fixed
+// cost (prologue, pipeline fill, partial-sum stores: about kRtCtaCostBlocks blocks,
+// measured); ks is the divisor of the K blocks (each CTA keeping >= 2) with the shortest
+// path, the smaller ks on a tie, and at most kRtMaxPartials partial floats (the selection
+// adds them back).
+constexpr int kRtMinTokens = 192;
 constexpr int kRtSms = 148;
 static bool router_tc_ok(int x_dtype, int T, int E, int H) {
     return x_dtype == 2 && T >= kRtMinTokens && E % 128 == 0 && H % kRtKB == 0;
@@ -627,15 +650,18 @@ static bool router_tc_ok(int x_dtype, int T, int E, int H) {
 static int router_tc_n(int T) { return T >= kRtMaxN ? kRtMaxN : ((T + 15) / 16) * 16; }  // token tile
 
 int router_tc_split(int T, int E, int H, int64_t cap) {
+    constexpr int64_t kRtCtaCostBlocks = 4;
+    constexpr int64_t kRtMaxPartials = int64_t(1) << 22;
     const int nbt = H / kRtKB;
     const int N = router_tc_n(T);
     const int64_t base = int64_t((T + N - 1) / N) * (E / 128);
     const int64_t logits = int64_t(T) * E;
+    cap = std::min(cap, std::max(logits, kRtMaxPartials));
     int best = 1;
-    int64_t best_path = ((base + kRtSms - 1) / kRtSms) * nbt;
+    int64_t best_path = ((base + kRtSms - 1) / kRtSms) * (nbt + kRtCtaCostBlocks);
     for (int ks = 2; ks <= nbt / 2; ++ks) {
         if (nbt % ks != 0 || ks * logits > cap) continue;
-        const int64_t path = ((base * ks + kRtSms - 1) / kRtSms) * (nbt / ks);
+        const int64_t path = ((base * ks + kRtSms - 1) / kRtSms) * (nbt / ks + kRtCtaCostBlocks);
         if (path < best_path) {
             best = ks;
             best_path = path;
