@@ -120,10 +120,18 @@ def test_dummy_fixture_full_size_vs_reference(dev, golden):
         assert cos >= 0.9999, cos
 
 
-@pytest.mark.parametrize("T", [2100])
+@pytest.mark.parametrize("T", [192, 200, 333, 1000, 2100])
 def test_router_tensor_core_path_vs_oracle(dev, T):
-    """Above 2048 bf16 tokens the logits run on the tensor cores (gate weight split into
-    three bf16 terms, per-block fp32 promotion): same tolerances as the SIMT path."""
+    """From 192 bf16 tokens on the logits run on the tensor cores (gate weight split into
+    three bf16 terms once per call, per-block fp32 promotion): same tolerances as the SIMT
+    path, at token counts that leave the last 128-token tile ragged (200, 333, 1000, 2100)
+    and at K splits from 28 down to 4.  Where the CUDA-core kernel fits the allocation-free
+    entry point's scratch, both paths must choose the same experts on every token that is
+    not a near-tie."""
+    import ctypes
+
+    from constellation_b200 import _lib
+
     E, H, G, TG, K = 256, 7168, 8, 4, 8
     x = cases.activations(400 + T, T, H)
     w, b = cases.router(401, E, H, bias_std=0.01)
@@ -134,6 +142,17 @@ def test_router_tensor_core_path_vs_oracle(dev, T):
     print(f"\ntensor-core router T={T}: {c}")
     i2, w2 = ctx.route(*args)
     assert torch.equal(i2, idx) and torch.equal(w2, wt)  # deterministic
+    if T * E <= (1 << 19):
+        i3 = torch.full((T, K), -1, dtype=torch.int32, device=dev)
+        w3 = torch.zeros((T, K), dtype=torch.float32, device=dev)
+        rc = _lib.lib.cst_route_noalloc(args[0].data_ptr(), 2, T, H, args[1].data_ptr(), args[2].data_ptr(), None, E,
+                                        G, TG, K, 1, ctypes.c_float(2.5), i3.data_ptr(), w3.data_ptr(),
+                                        torch.cuda.current_stream(dev).cuda_stream)
+        assert rc == 0, _lib.last_error()
+        torch.cuda.synchronize(dev)
+        near = router.route_batched(x.astype(np.float32), w, b, n_group=G, topk_group=TG, top_k=K).margin <= 1e-5
+        differ = (i3.sort(dim=1).values != idx.sort(dim=1).values).any(dim=1).cpu().numpy()
+        assert not (differ & ~near).any(), np.nonzero(differ & ~near)
 
 
 @pytest.mark.parametrize("case", ["small", "bias_heavy", "restricted", "g4_k6", "full"])
