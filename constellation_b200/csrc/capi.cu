@@ -278,13 +278,15 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     prof_mark(c, 1, s);
 
     PackActArgs px{x, x_dtype, H, w.row_token, w.groups, w.tile_group, w.meta, H, w.xfrag, w.xscale, terms};
+    const bool rows_mode = (pa.row_slot != nullptr) || (pa.single_slot >= 0);
+    const int64_t rows_bound = rows_mode ? int64_t(pa.T) : int64_t(pa.T) * (pa.K + 1);
+    px.rows_hint = int(std::min<int64_t>(rows_bound, c->max_rows));
     if (pf) {
         // every token's scale once, then one pass per packed row
         CST_CUDA(launch_row_scale(px, pa.T, w.tok_scale, c->num_sms, s));
         px.src_scale = w.tok_scale;
-        const bool mode_rows = (pa.row_slot != nullptr) || (pa.single_slot >= 0);
         px.tk_row = w.tk_row;
-        px.K1 = mode_rows ? 1 : pa.K + 1;
+        px.K1 = rows_mode ? 1 : pa.K + 1;
         px.n_src = pa.T;
         CST_CUDA(launch_pack_rows(px, c->num_sms, s));
     } else {
@@ -315,6 +317,7 @@ int run_experts(cst_ctx* c, PackArgs pa, const void* x, int x_dtype, cudaStream_
     prof_mark(c, 3, s);
 
     PackActArgs ph{w.h, kSrcUpGatePartials, I, nullptr, w.groups, w.tile_group, w.meta, I, w.hfrag, w.hscale, terms};
+    ph.rows_hint = px.rows_hint;
     CST_CUDA(pf ? launch_pack_rows(ph, c->num_sms, s) : launch_pack_act(ph, c->num_sms, s));
     prof_mark(c, 4, s);
 

@@ -118,6 +118,9 @@ struct PackActArgs {
     const int32_t* tk_row = nullptr;
     int K1 = 0;
     int n_src = 0;
+    // an upper bound on the packed rows known on the host (0: none); a small call then
+    // launches only the CTAs its tasks can use
+    int rows_hint = 0;
 };
 // src_dtype 4: `src` holds the up/gate kernel's split accumulators (meta->split_k splits of
 // meta->n_rows rows each); the packer adds the splits in order and applies

@@ -23,10 +23,12 @@
 // the 8 source loads are issued together; per K block 128 elements, 4 per lane, one 32-bit
 // store per term.  Rows of a group's last n-tile beyond its row count are not written.
 // The tasks run over the packed rows themselves (0 .. meta->n_rows, contiguous in group
-// order): every CTA first copies the groups' first rows to shared memory and finds a
-// row's group there by binary search, so no warp spends a task on an unused tile column
-// (at decode most columns of the 8-wide n-tiles are), and the grid is the CTAs that fit
-// on the GPU at once, so every task starts in the first wave.
+// order).  A row's group is found by one load and a warp ballot up to 32 groups, beyond
+// that by binary search over the groups' first rows, which every CTA first copies to shared
+// memory.  No warp spends a task on an unused tile column (at decode most columns of the
+// 8-wide n-tiles are), and the grid is at most the CTAs that fit on the GPU at once (fewer
+// when the host's bound on the rows needs fewer), so every task starts in the first wave.
+#include <algorithm>
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -109,10 +111,13 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
     const int n_chunks = (KB + KBPT - 1) / KBPT;
     const int n_rows = a.meta->n_rows;
     const int n_groups = a.meta->n_groups;
-    const bool staged = n_groups <= kPackSmemGroups;
+    // up to 32 groups (a worker request, a rank's share of a decode batch): each task's
+    // warp finds the group with one load and a ballot; more: staged in shared memory
+    const bool warp_search = n_groups <= 32;
+    const bool staged = !warp_search && n_groups <= kPackSmemGroups;
     if (staged)
         for (int g = threadIdx.x; g < n_groups; g += blockDim.x) s_rs[g] = a.groups[g].row_start;
-    __syncthreads();
+    if (!warp_search) __syncthreads();  // the same on every thread: meta is read by all
     const int split = a.src_dtype == kSrcUpGatePartials ? a.meta->split_k : 1;
     const int lane = threadIdx.x & 31;
     const int64_t n_tasks = int64_t(n_rows) * n_chunks;
@@ -123,7 +128,16 @@ __global__ void __launch_bounds__(256) pack_act_kernel(PackActArgs a) {
         const int prow = static_cast<int>(task / n_chunks);
         const int chunk = static_cast<int>(task - int64_t(prow) * n_chunks);
         const int64_t src_row = a.row_map ? a.row_map[prow] : prow;
-        const GroupRec gr = a.groups[group_of_row(staged ? s_rs : nullptr, a.groups, n_groups, prow)];
+        int gi;
+        if (warp_search) {
+            // row starts increase with the group index and group 0 starts at row 0, so the
+            // highest lane whose group starts at or before prow holds prow
+            const int rs = lane < n_groups ? a.groups[lane].row_start : 0x7fffffff;
+            gi = 31 - __clz(__ballot_sync(0xffffffffu, rs <= prow));
+        } else {
+            gi = group_of_row(staged ? s_rs : nullptr, a.groups, n_groups, prow);
+        }
+        const GroupRec gr = a.groups[gi];
         const int r = prow - gr.row_start;
         const int nt = r / kTileCols;
         const int j = r - nt * kTileCols;
@@ -471,14 +485,25 @@ cudaError_t launch_pack_rows(const PackActArgs& a, int num_sms, cudaStream_t str
     return launch_chained(pack_rows_kernel, dim3(num_sms * 8), dim3(256), 0, stream, a);
 }
 
+// CTAs for a dense-row launch: one wave (the row count is known on the device only, the
+// loop strides over it), or fewer when the host's bound on the rows needs fewer warps
+static int pack_grid(const PackActArgs& a, int kbpt, int num_sms, int occ) {
+    int64_t grid = int64_t(num_sms) * occ;
+    if (a.rows_hint > 0) {
+        const int64_t tasks = int64_t(a.rows_hint) * ((a.K / kBlock + kbpt - 1) / kbpt);
+        grid = std::min<int64_t>(grid, std::max<int64_t>(1, (tasks + 7) / 8));  // 8 warps per CTA
+    }
+    return static_cast<int>(grid);
+}
+
 cudaError_t launch_pack_act(const PackActArgs& a, int num_sms, cudaStream_t stream) {
-    // one wave: the row count is known on the device only, the loop strides over it
     if (a.src_dtype == kSrcUpGatePartials) {
         static const int occ = resident_ctas(pack_act_kernel<2>);
-        return launch_chained(pack_act_kernel<2>, dim3(num_sms * occ), dim3(256), 0, stream, a);
+        return launch_chained(pack_act_kernel<2>, dim3(pack_grid(a, 2, num_sms, occ)), dim3(256), 0, stream, a);
     }
     static const int occ = resident_ctas(pack_act_kernel<kPackKbPerTask>);
-    return launch_chained(pack_act_kernel<kPackKbPerTask>, dim3(num_sms * occ), dim3(256), 0, stream, a);
+    return launch_chained(pack_act_kernel<kPackKbPerTask>, dim3(pack_grid(a, kPackKbPerTask, num_sms, occ)),
+                          dim3(256), 0, stream, a);
 }
 
 }  // namespace cst
