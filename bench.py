@@ -198,6 +198,18 @@ class ClockSampler:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.p = None
 
+    def _lines(self) -> int:
+        self.f.flush()
+        try:
+            return sum(1 for line in Path(self.f.name).read_text().splitlines() if line.count(",") >= 8)
+        except OSError:
+            return 0
+
+    def _wait_lines(self, n: int, limit_s: float) -> None:
+        t_end = time.monotonic() + limit_s
+        while self.p is not None and self._lines() < n and time.monotonic() < t_end and self.p.poll() is None:
+            time.sleep(0.02)
+
     def __enter__(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
@@ -205,11 +217,16 @@ class ClockSampler:
                                       stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.p = None
-        time.sleep(0.25)
+        # nvidia-smi can take longer than a short timed region to start on a busy box: wait
+        # (bounded) for its first sample, so the region is bracketed by samples
+        self._wait_lines(1, 5.0)
+        self._n_enter = self._lines()
         return self
 
     def __exit__(self, *a):
         if self.p is not None:
+            # one sample after the region started (the next 200 ms tick), then stop
+            self._wait_lines(self._n_enter + 1, 1.0)
             self.p.terminate()
             try:
                 self.p.wait(timeout=5)
