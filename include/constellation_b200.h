@@ -166,8 +166,10 @@ int cst_route(cst_ctx* ctx, const void* x, int32_t x_dtype, int32_t T, const flo
  * call before any stream capture.  All calls share the one array: calls that overlap on
  * the GPU (other streams, threads or graph replays) race on it.  The logits always run on
  * the CUDA cores (a kernel with no device-side waits, so no call can time out unreported);
- * results equal cst_route's wherever cst_route does the same (up to 2048 bf16 tokens, or
- * fp16 / fp32 input) and differ elsewhere only in the last ulp of a logit. */
+ * results equal cst_route's wherever cst_route does the same (below 192 bf16 tokens, or
+ * fp16 / fp32 input); from 192 bf16 tokens on cst_route sums the logits on the tensor
+ * cores in another order, so a logit may differ in its last bits and an expert choice
+ * only on a near-tie. */
 int cst_route_noalloc(const void* x, int32_t x_dtype, int32_t T, int32_t hidden, const float* gate_weight,
                       const float* bias, const uint8_t* resident, int32_t n_experts, int32_t n_group,
                       int32_t topk_group, int32_t top_k, int32_t norm_topk_prob, float routed_scaling_factor,
